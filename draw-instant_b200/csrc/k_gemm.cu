@@ -1,0 +1,517 @@
+// k_gemm.cu — tcgen05 / TMEM / TMA GEMM and implicit-GEMM 3x3 convolution (sm_100a).
+//
+// Replaces the reference's 64x64 fp32 FMA tiles (WGSL_MATMUL wgsl-ops.js:477-556, WGSL_GEMM :821-897,
+// WGSL_CONV_MM :584-698, the fused-block matmuls fused-block-full.js:128-186, and the direct convs
+// fused-resnet.js:173-208 / fused-conv.js:50-100) with one warp-specialised tensor-core kernel:
+//
+//   warp 0      TMA producer: A tile (128 rows x 64 K, 128B-swizzled) + B tile (BN rows x 64 K) per stage
+//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per stage, accumulator in TMEM,
+//               tcgen05.commit releases the stage back to the producer
+//   warps 2..5  epilogue: tcgen05.ld of the 128 x BN fp32 accumulator (one TMEM lane = one output row),
+//               + bias + per-image row vector (timestep embedding) + residual, or the GEGLU gate,
+//               converted and stored.
+//
+// A-operand modes (the "implicit im2col" is done by the TMA unit, no im2col buffer exists):
+//   0  linear: A = X[M,K] row-major, optionally concat(X1[:, :K1], X2[:, K1:]) along K (two maps)
+//   1  conv 3x3 stride 1 pad 1, NHWC: one 4-D box {64 ch, Wo, rows, images} per (tap, 64-channel block),
+//      shifted by (ky-1, kx-1); out-of-range rows/columns are zero-filled by TMA = the conv padding.
+//      Two input tensors (skip concat) are two maps split on the channel block.
+//   2  conv 3x3 stride 2 pad 1: four parity maps (even/odd row x even/odd column) so every tap is a
+//      unit-stride box of the half-resolution grid.
+// B = weights [N rows, K] K-major; conv weights packed [Co][ky][kx][Ci] so K order = (tap, channel).
+//
+// Every mbarrier wait is time-bounded (di_common.cuh): on timeout the kernel records an error code,
+// skips the remaining work, frees its TMEM and returns.
+#include <algorithm>
+#include <mutex>
+
+#include "di_common.cuh"
+
+namespace di {
+
+Ctx* ctx_of(di_ctx_t h);
+
+struct GemmParams {
+  CUtensorMap tmA[4];
+  CUtensorMap tmB;
+  int mode;        // 0 linear, 1 conv s1, 2 conv s2
+  int M, N;        // output rows, accumulator columns (geglu: 2F packed columns)
+  int num_k;       // K blocks of 64
+  int k_split;     // K (or channel) blocks served by source 0
+  int cin_blocks;  // conv: channel blocks per tap
+  int HWo, Wo;     // conv: output pixels per image, output width
+  const float* bias;
+  const float* rowvec;  // adds rowvec[(m / rowvec_div) * N + n]
+  int rowvec_div;
+  const void* residual;  // [M, ldr] (out dtype, or fp32 when res_f32)
+  int ldr, res_f32;
+  void* out;
+  int ldo, out_f32;
+  int geglu;
+  int vec_ok;  // 16-byte aligned rows for out / residual: vectorised epilogue
+  int* err;
+};
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+};
+
+__device__ __forceinline__ void store_row32(void* out, size_t off, const float* v, int out_f32, bool bf16) {
+  if (out_f32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + off);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    uint32_t pk[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (bf16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        pk[j] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        pk[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + off);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+  }
+}
+
+__device__ __forceinline__ void load_row32(const void* src, size_t off, float* v, int is_f32, bool bf16) {
+  if (is_f32) {
+    const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(src) + off);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 t = s[j];
+      v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+    }
+  } else {
+    const uint4* s = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(src) + off);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 t = s[j];
+      uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 f;
+        if (bf16) f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[q]));
+        else f = __half22float2(*reinterpret_cast<__half2*>(&w[q]));
+        v[8 * j + 2 * q] = f.x; v[8 * j + 2 * q + 1] = f.y;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float load_one(const void* src, size_t off, int is_f32, bool bf16) {
+  if (is_f32) return static_cast<const float*>(src)[off];
+  if (bf16) return __bfloat162float(static_cast<const __nv_bfloat16*>(src)[off]);
+  return __half2float(static_cast<const __half*>(src)[off]);
+}
+__device__ __forceinline__ void store_one(void* dst, size_t off, float v, int is_f32, bool bf16) {
+  if (is_f32) static_cast<float*>(dst)[off] = v;
+  else if (bf16) static_cast<__nv_bfloat16*>(dst)[off] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(dst)[off] = __float2half_rn(v);
+}
+
+template <int BN, int STAGES, bool BF16>
+__global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
+  using S = GemmSmem<BN, STAGES>;
+  constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
+  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (elect_one()) {
+      for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.tmA[i]);
+      tma_prefetch_desc(&p.tmB);
+      int img = 0, y0 = 0;
+      if (p.mode != 0) { img = m0 / p.HWo; y0 = (m0 % p.HWo) / p.Wo; }
+      for (int kb = 0; kb < p.num_k; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1, p.err, DEVERR_WAIT_TMA)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(&full[s], STAGE_TX);
+        uint8_t* dA = sA + s * S::A_BYTES;
+        if (p.mode == 0) {
+          if (kb < p.k_split) tma_load_2d(dA, &p.tmA[0], &full[s], kb * BK, m0);
+          else tma_load_2d(dA, &p.tmA[1], &full[s], (kb - p.k_split) * BK, m0);
+        } else {
+          const int tap = kb / p.cin_blocks, cb = kb % p.cin_blocks;
+          const int ky = tap / 3, kx = tap % 3;
+          if (p.mode == 1) {
+            const bool first = cb < p.k_split;
+            tma_load_4d(dA, &p.tmA[first ? 0 : 1], &full[s], (first ? cb : cb - p.k_split) * BK, kx - 1,
+                        y0 + ky - 1, img);
+          } else {
+            const int py = ky == 1 ? 0 : 1, px = kx == 1 ? 0 : 1;
+            tma_load_4d(dA, &p.tmA[py * 2 + px], &full[s], cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0), img);
+          }
+        }
+        tma_load_2d(sB + s * S::B_BYTES, &p.tmB, &full[s], kb * BK, n0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_f16(BM, BN, BF16);
+      for (int kb = 0; kb < p.num_k; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (*abort_flag || !mbar_wait(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + s * S::A_BYTES), b0 = smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(b0 + k * 32, 16, 1024);
+          umma_f16(tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const int m = m0 + row;
+    const bool ok = mbar_wait(accum, 0, p.err, DEVERR_WAIT_EPI);
+    tc_fence_after();
+    const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    if (!p.geglu) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + c * 32, r);
+        tmem_wait_ld();
+        const int nb = n0 + c * 32;
+        if (!ok || m >= p.M || nb >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const bool full_chunk = p.vec_ok && nb + 32 <= p.N;
+        if (full_chunk) {
+          if (p.bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
+          }
+          if (p.rowvec) {
+            const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.N + nb;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
+          }
+          if (p.residual) {
+            float rr[32];
+            load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += rr[j];
+          }
+          store_row32(p.out, (size_t)m * p.ldo + nb, v, p.out_f32, BF16);
+        } else {
+          for (int j = 0; j < 32 && nb + j < p.N; ++j) {
+            float x = v[j];
+            if (p.bias) x += p.bias[nb + j];
+            if (p.rowvec) x += p.rowvec[(size_t)(m / p.rowvec_div) * p.N + nb + j];
+            if (p.residual) x += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
+            store_one(p.out, (size_t)m * p.ldo + nb + j, x, p.out_f32, BF16);
+          }
+        }
+      }
+    } else {
+      // GEGLU: accumulator columns [0,64) are value rows, [64,128) the matching gate rows of this tile.
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t rv[32], rg[32];
+        tmem_ld32(trow + c * 32, rv);
+        tmem_ld32(trow + 64 + c * 32, rg);
+        tmem_wait_ld();
+        const int ob = blockIdx.x * 64 + c * 32;  // output column
+        if (!ok || m >= p.M || ob >= p.N / 2) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float a = __uint_as_float(rv[j]), g = __uint_as_float(rg[j]);
+          if (p.bias) { a += __ldg(p.bias + n0 + c * 32 + j); g += __ldg(p.bias + n0 + 64 + c * 32 + j); }
+          v[j] = a * gelu_erf(g);
+        }
+        store_row32(p.out, (size_t)m * p.ldo + ob, v, p.out_f32, BF16);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+template <int BN, int STAGES, bool BF16>
+int launch_variant(Ctx* c, const GemmParams& p) {
+  using S = GemmSmem<BN, STAGES>;
+  auto kern = gemm_tc_kernel<BN, STAGES, BF16>;
+  static unsigned attr_done = 0;  // per-device bit: dynamic smem opt-in is a per-device attribute
+  if (!(attr_done & (1u << (c->device & 31)))) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
+      return set_error(c, DI_ECUDA, "gemm: cudaFuncSetAttribute failed");
+    attr_done |= 1u << (c->device & 31);
+  }
+  const int n_tiles = p.geglu ? (p.N / BN) : (p.N + BN - 1) / BN;
+  dim3 grid(n_tiles, (p.M + BM - 1) / BM);
+  kern<<<grid, 192, S::TOTAL, c->stream>>>(p);
+  return check_launch(c, "gemm_tc_kernel");
+}
+
+}  // namespace
+
+// Chooses the N tile: 128 by default; 64 when the grid would leave most SMs idle.
+int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int force_bn = 0) {
+  p.err = c->d_err;
+  int bn = force_bn;
+  if (!bn) {
+    if (p.geglu) bn = 128;
+    else {
+      const long long tiles128 = (long long)((p.N + 127) / 128) * ((p.M + 127) / 128);
+      bn = (tiles128 < c->num_sms && p.N % 64 == 0) ? 64 : 128;
+    }
+  }
+  // ~97 KB of stages per CTA so two CTAs share an SM: one's epilogue overlaps the other's main loop.
+  if (bn == 64) return bf16 ? launch_variant<64, 4, true>(c, p) : launch_variant<64, 4, false>(c, p);
+  return bf16 ? launch_variant<128, 3, true>(c, p) : launch_variant<128, 3, false>(c, p);
+}
+
+static CUtensorMapDataType tdt(int dtype) {
+  return dtype == DI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// 2-D K-major operand map: rows x cols(K), row stride ld elements, box 64 x box_rows.
+bool tmap_kmajor(CUtensorMap* m, int dtype, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint32_t box_rows, std::string* err) {
+  uint64_t dims[2] = {cols, rows};
+  uint64_t strides[1] = {ld * 2};
+  uint32_t box[2] = {64, box_rows};
+  return make_tmap(m, tdt(dtype), 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, err);
+}
+
+// Conv tile geometry: 128 output pixels = bn images x bh rows x Wo columns.
+static bool conv_box(int Ho, int Wo, uint32_t* bh, uint32_t* bn) {
+  if (Wo <= 0 || Wo > 128 || (128 % Wo) != 0) return false;
+  const int rows = std::min(Ho, 128 / Wo);
+  if ((128 / Wo) % rows != 0) return false;
+  if (Ho % rows != 0) return false;
+  *bh = rows;
+  *bn = 128 / (Wo * rows);
+  return true;
+}
+
+static bool tmap_conv_s1(CUtensorMap* m, int dtype, const void* base, int N, int H, int W, int C, uint32_t bh,
+                         uint32_t bn, std::string* err) {
+  uint64_t dims[4] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)N};
+  uint64_t strides[3] = {(uint64_t)C * 2, (uint64_t)W * C * 2, (uint64_t)H * W * C * 2};
+  uint32_t box[4] = {64, (uint32_t)W, bh, bn};
+  return make_tmap(m, tdt(dtype), 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, err);
+}
+
+static bool tmap_conv_s2(CUtensorMap* m, int dtype, const void* base, int N, int H, int W, int C, int py, int px,
+                         uint32_t bh, uint32_t bn, std::string* err) {
+  const uint16_t* b = static_cast<const uint16_t*>(base) + ((size_t)py * W + px) * C;
+  uint64_t dims[4] = {(uint64_t)C, (uint64_t)(W / 2), (uint64_t)(H / 2), (uint64_t)N};
+  uint64_t strides[3] = {(uint64_t)C * 4, (uint64_t)W * C * 4, (uint64_t)H * W * C * 2};
+  uint32_t box[4] = {64, (uint32_t)(W / 2), bh, bn};
+  return make_tmap(m, tdt(dtype), 4, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, err);
+}
+
+static bool vec_rows_ok(const void* p, int ld, int esz) {
+  return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && ((size_t)ld * esz) % 16 == 0;
+}
+
+static GemmParams base_params() {
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.rowvec_div = 1;
+  return p;
+}
+
+// Public building blocks used by the fused blocks and the U-Net plan ---------------------------
+int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
+                const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
+                int rowvec_div) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % 64 || (X2 && (K1 <= 0 || K1 % 64 || K1 >= K)))
+    return set_error(c, DI_EINVAL, "linear: K and K1 must be multiples of 64");
+  if (geglu && (N % 128)) return set_error(c, DI_EINVAL, "linear_geglu: F must be a multiple of 64");
+  GemmParams p = base_params();
+  std::string err;
+  const int ks = X2 ? K1 : K;
+  if (!tmap_kmajor(&p.tmA[0], dtype, X1, M, ks, ks, 128, &err)) return set_error(c, DI_EINVAL, err);
+  if (X2) {
+    if (!tmap_kmajor(&p.tmA[1], dtype, X2, M, K - K1, K - K1, 128, &err)) return set_error(c, DI_EINVAL, err);
+  } else {
+    p.tmA[1] = p.tmA[0];
+  }
+  p.tmA[2] = p.tmA[0];
+  p.tmA[3] = p.tmA[0];
+  const int bn = geglu ? 128 : 0;
+  p.mode = 0;
+  p.M = M;
+  p.N = N;
+  p.num_k = K / 64;
+  p.k_split = ks / 64;
+  p.bias = bias;
+  p.rowvec = rowvec;
+  p.rowvec_div = rowvec_div > 0 ? rowvec_div : 1;
+  p.residual = R;
+  p.ldr = N;
+  p.res_f32 = res_f32;
+  p.out = Y;
+  p.ldo = geglu ? N / 2 : N;
+  p.out_f32 = out_f32;
+  p.geglu = geglu;
+  p.vec_ok = vec_rows_ok(Y, p.ldo, out_f32 ? 4 : 2) && (!R || vec_rows_ok(R, N, res_f32 ? 4 : 2));
+  int chosen = bn;
+  if (!chosen) {
+    const long long tiles128 = (long long)((N + 127) / 128) * ((M + 127) / 128);
+    chosen = (tiles128 < c->num_sms && N % 64 == 0) ? 64 : 128;
+  }
+  if (!tmap_kmajor(&p.tmB, dtype, W, N, K, K, chosen, &err)) return set_error(c, DI_EINVAL, err);
+  return launch_gemm(c, p, dtype == DI_BF16, chosen);
+}
+
+int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
+                 const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
+                 void* y, int out_f32) {
+  if (C1 <= 0 || C1 % 64 || (x2 && (C2 <= 0 || C2 % 64)) || Co % 16 || (stride != 1 && stride != 2))
+    return set_error(c, DI_EINVAL, "conv3x3: channels must be multiples of 64 (Co of 16), stride 1 or 2");
+  if (stride == 2 && (x2 || (H % 2) || (W % 2)))
+    return set_error(c, DI_EUNSUPPORTED, "conv3x3 stride 2: single input with even H, W");
+  const int Ho = stride == 1 ? H : H / 2, Wo = stride == 1 ? W : W / 2;
+  uint32_t bh, bn;
+  if (!conv_box(Ho, Wo, &bh, &bn)) return set_error(c, DI_EUNSUPPORTED, "conv3x3: output tile geometry");
+  GemmParams p = base_params();
+  std::string err;
+  const int Cin = C1 + (x2 ? C2 : 0);
+  if (stride == 1) {
+    if (!tmap_conv_s1(&p.tmA[0], dtype, x1, N, H, W, C1, bh, bn, &err)) return set_error(c, DI_EINVAL, err);
+    if (x2) {
+      if (!tmap_conv_s1(&p.tmA[1], dtype, x2, N, H, W, C2, bh, bn, &err)) return set_error(c, DI_EINVAL, err);
+    } else p.tmA[1] = p.tmA[0];
+    p.tmA[2] = p.tmA[0];
+    p.tmA[3] = p.tmA[0];
+    p.mode = 1;
+  } else {
+    for (int py = 0; py < 2; ++py)
+      for (int px = 0; px < 2; ++px)
+        if (!tmap_conv_s2(&p.tmA[py * 2 + px], dtype, x1, N, H, W, C1, py, px, bh, bn, &err))
+          return set_error(c, DI_EINVAL, err);
+    p.mode = 2;
+  }
+  p.M = N * Ho * Wo;
+  p.N = Co;
+  p.cin_blocks = Cin / 64;
+  p.k_split = C1 / 64;
+  p.num_k = 9 * p.cin_blocks;
+  p.HWo = Ho * Wo;
+  p.Wo = Wo;
+  p.bias = bias;
+  p.rowvec = temb;
+  p.rowvec_div = Ho * Wo;
+  p.residual = residual;
+  p.ldr = Co;
+  p.res_f32 = res_f32;
+  p.out = y;
+  p.ldo = Co;
+  p.out_f32 = out_f32;
+  p.vec_ok = vec_rows_ok(y, Co, out_f32 ? 4 : 2) && (!residual || vec_rows_ok(residual, Co, res_f32 ? 4 : 2));
+  const long long tiles128 = (long long)((Co + 127) / 128) * ((p.M + 127) / 128);
+  const int chosen = (tiles128 < c->num_sms && Co % 64 == 0) ? 64 : 128;
+  if (!tmap_kmajor(&p.tmB, dtype, Wt, Co, 9 * Cin, 9 * Cin, chosen, &err)) return set_error(c, DI_EINVAL, err);
+  return launch_gemm(c, p, dtype == DI_BF16, chosen);
+}
+
+// Weight repack: [Co][Ci][3][3] fp32 -> [Co][3][3][Ci] fp16/bf16.
+__global__ void pack_conv3x3_kernel(const float* __restrict__ w, int Co, int Ci, void* out, int bf16) {
+  const size_t n = (size_t)Co * Ci * 9;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int ci = i % Ci;
+    const int tap = (i / Ci) % 9;
+    const int co = i / ((size_t)Ci * 9);
+    const float v = w[((size_t)co * Ci + ci) * 9 + tap];
+    if (bf16) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else static_cast<__half*>(out)[i] = __float2half_rn(v);
+  }
+}
+
+int pack_conv3x3(Ctx* c, int dtype, const float* w, int Co, int Ci, void* out) {
+  pack_conv3x3_kernel<<<std::min<size_t>(((size_t)Co * Ci * 9 + 255) / 256, 4096), 256, 0, c->stream>>>(
+      w, Co, Ci, out, dtype == DI_BF16);
+  return check_launch(c, "pack_conv3x3");
+}
+
+}  // namespace di
+
+using namespace di;
+
+extern "C" {
+
+int di_linear(di_ctx_t h, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
+              const float* bias, const void* R, void* Y) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
+  return gemm_linear(c, dtype, X1, K1, X2, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1);
+}
+
+int di_linear_geglu(di_ctx_t h, int dtype, const void* X, int M, int K, const void* W, int F, const float* bias,
+                    void* Y) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16) || F % 64) return DI_EINVAL;
+  return gemm_linear(c, dtype, X, K, nullptr, M, K, W, 2 * F, bias, nullptr, 0, Y, 0, 1, nullptr, 1);
+}
+
+int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,
+                    int stride, const void* Wt, int Co, const float* bias, const float* temb, const void* residual,
+                    void* y) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
+  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0);
+}
+
+int di_pack_conv3x3(di_ctx_t h, int dtype, const float* w, int Co, int Ci, void* out) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
+  return pack_conv3x3(c, dtype, w, Co, Ci, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,319 @@
+// k_norm.cu — GroupNorm / InstanceNorm / LayerNorm (+SiLU) for sm_100a.
+//
+// Bandwidth-bound: each kernel is judged by achieved HBM GB/s.  The reference runs one 256-thread
+// workgroup per (n, group) with a shared-memory tree (wgsl-ops.js:390-458, fused-groupnorm.js:145-227),
+// i.e. 32 workgroups for a whole feature map.  Here statistics are split over many CTAs (per-chunk
+// partial sum / sum-of-squares written to a small scratch buffer, reduced in a fixed order so results
+// are run-to-run deterministic), and the normalise pass is a separate fully parallel, vectorised
+// elementwise kernel that re-derives mean / rstd per CTA from the partials.
+//
+// Numerics follow the reference: mean = sum/n, var = sumsq/n - mean^2 clamped at 0,
+// y = (x - mean) * (1/sqrt(var + eps)) * gamma + beta, optional SiLU x/(1+exp(-x)).
+#include <algorithm>
+
+#include "di_common.cuh"
+
+namespace di {
+
+Ctx* ctx_of(di_ctx_t h);
+void* workspace(Ctx* c, size_t bytes, int slot);
+
+namespace {
+
+template <typename T> struct Vec8 { T v[8]; };
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      T two[2];
+      memcpy(two, &w[q], 4);
+      f[2 * q] = to_f<T>(two[0]);
+      f[2 * q + 1] = to_f<T>(two[1]);
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float* f) {
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      T two[2] = {from_f<T>(f[2 * q]), from_f<T>(f[2 * q + 1])};
+      memcpy(&w[q], two, 4);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// NHWC GroupNorm.  x = concat(x1[P, C1], x2[P, C2]) per pixel; partial[n][chunk][g] = (sum, sumsq).
+// Block = R rows x V vectors (8 channels each); thread (r, v) walks pixels r, r+R, ... of its chunk.
+// ---------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2, int HW,
+                                int chunk_pixels, int G, float2* __restrict__ partial) {
+  extern __shared__ float sh[];
+  const int C = C1 + C2, V = C / 8, R = blockDim.x / V;
+  const int n = blockIdx.y, chunk = blockIdx.x, nchunks = gridDim.x;
+  const int t = threadIdx.x, r = t / V, v = t % V;
+  float* ssum = sh;            // [R][C]
+  float* ssq = sh + R * C;     // [R][C]
+  if (r < R) {
+    float s[8], q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { s[j] = 0.f; q[j] = 0.f; }
+    const int c = v * 8;
+    const int p0 = chunk * chunk_pixels, p1 = min(HW, p0 + chunk_pixels);
+    for (int p = p0 + r; p < p1; p += R) {
+      const size_t pix = (size_t)n * HW + p;
+      float f[8];
+      if (c < C1) load8<T>(x1 + pix * C1 + c, f);
+      else load8<T>(x2 + pix * C2 + (c - C1), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { s[j] += f[j]; q[j] += f[j] * f[j]; }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { ssum[r * C + c + j] = s[j]; ssq[r * C + c + j] = q[j]; }
+  }
+  __syncthreads();
+  const int cpg = C / G;
+  for (int g = t; g < G; g += blockDim.x) {
+    float s = 0.f, q = 0.f;
+    for (int rr = 0; rr < R; ++rr)
+      for (int cc = g * cpg; cc < (g + 1) * cpg; ++cc) { s += ssum[rr * C + cc]; q += ssq[rr * C + cc]; }
+    partial[((size_t)n * nchunks + chunk) * G + g] = make_float2(s, q);
+  }
+}
+
+template <typename Tin, typename Tout>
+__global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __restrict__ x2, int C2, int HW, int G,
+                              const float2* __restrict__ partial, int nchunks, const float* __restrict__ gamma,
+                              const float* __restrict__ beta, float eps, int silu, Tout* __restrict__ y) {
+  __shared__ float s_mean[128], s_rstd[128];
+  const int C = C1 + C2, V = C / 8, cpg = C / G;
+  const int n = blockIdx.y;
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    float s = 0.f, q = 0.f;
+    for (int k = 0; k < nchunks; ++k) {
+      const float2 pq = partial[((size_t)n * nchunks + k) * G + g];
+      s += pq.x; q += pq.y;
+    }
+    const float cnt = (float)cpg * (float)HW;
+    const float mean = s / cnt;
+    const float var = fmaxf(q / cnt - mean * mean, 0.0f);
+    s_mean[g] = mean;
+    s_rstd[g] = 1.0f / sqrtf(var + eps);
+  }
+  __syncthreads();
+  const size_t total = (size_t)HW * V;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int v = e % V;
+    const size_t p = (size_t)n * HW + e / V;
+    const int c = v * 8;
+    float f[8];
+    if (c < C1) load8<Tin>(x1 + p * C1 + c, f);
+    else load8<Tin>(x2 + p * C2 + (c - C1), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int cc = c + j, g = cc / cpg;
+      float o = (f[j] - s_mean[g]) * s_rstd[g] * __ldg(gamma + cc) + __ldg(beta + cc);
+      f[j] = silu ? silu_f(o) : o;
+    }
+    store8<Tout>(y + p * C + c, f);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// NCHW fp32 GroupNorm (op family).  Group (n, g) is the contiguous span [(n*C + g*cpg)*HW, +cpg*HW).
+// ---------------------------------------------------------------------------------------------
+__global__ void gn_nchw_partial(const float* __restrict__ x, int G, size_t gsize, int nchunks,
+                                float2* __restrict__ partial) {
+  const int chunk = blockIdx.x, g = blockIdx.y, n = blockIdx.z;
+  const size_t base = ((size_t)n * G + g) * gsize;
+  const size_t per = (gsize + nchunks - 1) / nchunks;
+  const size_t b0 = chunk * per, b1 = min(gsize, b0 + per);
+  float s = 0.f, q = 0.f;
+  for (size_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) {
+    const float v = x[base + i];
+    s += v; q += v * v;
+  }
+  __shared__ float ws[32], wq[32];
+  for (int o = 16; o; o >>= 1) { s += __shfl_xor_sync(~0u, s, o); q += __shfl_xor_sync(~0u, q, o); }
+  if ((threadIdx.x & 31) == 0) { ws[threadIdx.x / 32] = s; wq[threadIdx.x / 32] = q; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float S = 0.f, Q = 0.f;
+    for (int w = 0; w < (int)blockDim.x / 32; ++w) { S += ws[w]; Q += wq[w]; }
+    partial[((size_t)n * G + g) * nchunks + chunk] = make_float2(S, Q);
+  }
+}
+
+__global__ void gn_nchw_apply(const float* __restrict__ x, int C, int G, int HW, int nchunks,
+                              const float2* __restrict__ partial, const float* __restrict__ gamma,
+                              const float* __restrict__ beta, float eps, int silu, int clamp, size_t total,
+                              float* __restrict__ y) {
+  const int cpg = C / G;
+  const float cnt = (float)cpg * (float)HW;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t nc = i / HW;
+    const int c = nc % C;
+    const size_t n = nc / C;
+    const int g = c / cpg;
+    float s = 0.f, q = 0.f;
+    const float2* pp = partial + ((size_t)n * G + g) * nchunks;
+    for (int k = 0; k < nchunks; ++k) { s += pp[k].x; q += pp[k].y; }
+    const float mean = s / cnt;
+    float var = q / cnt - mean * mean;
+    if (clamp) var = fmaxf(var, 0.0f);
+    const float o = (x[i] - mean) * (1.0f / sqrtf(var + eps)) * gamma[c] + beta[c];
+    y[i] = silu ? silu_f(o) : o;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// LayerNorm: one warp per row.  Token-major [rows, D]; T in/out, gamma/beta fp32.
+// ---------------------------------------------------------------------------------------------
+template <typename Tin, typename Tout>
+__global__ void layer_norm_rows(const Tin* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
+                                Tout* __restrict__ y, int rows, int D, float eps) {
+  const int warps = blockDim.x / 32;
+  const int row = blockIdx.x * warps + threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const Tin* xr = x + (size_t)row * D;
+  float s = 0.f, q = 0.f;
+  for (int i = lane; i < D; i += 32) { const float v = to_f<Tin>(xr[i]); s += v; q += v * v; }
+  for (int o = 16; o; o >>= 1) { s += __shfl_xor_sync(~0u, s, o); q += __shfl_xor_sync(~0u, q, o); }
+  const float mean = s / (float)D;
+  const float var = fmaxf(q / (float)D - mean * mean, 0.0f);
+  const float inv = 1.0f / sqrtf(var + eps);
+  for (int i = lane; i < D; i += 32) y[(size_t)row * D + i] = from_f<Tout>((to_f<Tin>(xr[i]) - mean) * inv * g[i] + b[i]);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------
+// Host entry points (also used by the fused blocks / U-Net plan).
+// ---------------------------------------------------------------------------------------------
+int gn_nhwc_chunks(int HW) { return std::max(1, std::min(64, HW / 64)); }
+
+template <typename Tin, typename Tout>
+static int gn_nhwc_impl(Ctx* c, const Tin* x1, int C1, const Tin* x2, int C2, int N, int HW, int G, float eps,
+                        const float* gamma, const float* beta, int silu, Tout* y, float2* partial) {
+  const int C = C1 + C2;
+  if (C % 8 || C1 % 8 || G <= 0 || G > 128 || C % G) return set_error(c, DI_EINVAL, "group_norm_nhwc: bad channels");
+  const int V = C / 8;
+  const int R = std::max(1, 256 / V);
+  const int threads = R * V;
+  if (threads > 1024) return set_error(c, DI_EUNSUPPORTED, "group_norm_nhwc: too many channels");
+  const int chunks = gn_nhwc_chunks(HW);
+  const int chunk_pixels = (HW + chunks - 1) / chunks;
+  if (!partial) {
+    partial = static_cast<float2*>(workspace(c, sizeof(float2) * (size_t)N * chunks * G, 0));
+    if (!partial) return set_error(c, DI_ENOMEM, "group_norm_nhwc: workspace");
+  }
+  const size_t shm = sizeof(float) * 2 * R * C;
+  gn_nhwc_partial<Tin><<<dim3(chunks, N), threads, shm, c->stream>>>(x1, C1, x2, C2, HW, chunk_pixels, G, partial);
+  const size_t work = (size_t)HW * V;
+  const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)std::max(1, 4 * c->num_sms / std::max(1, N)));
+  gn_nhwc_apply<Tin, Tout><<<dim3(blocks, N), 256, 0, c->stream>>>(x1, C1, x2, C2, HW, G, partial, chunks, gamma,
+                                                                    beta, eps, silu, y);
+  return check_launch(c, "group_norm_nhwc");
+}
+
+int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1, const void* x2, int C2, int N,
+                    int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
+                    void* partial_ws) {
+  float2* pw = static_cast<float2*>(partial_ws);
+#define GN_CASE(TI, TO)                                                                                        \
+  return gn_nhwc_impl<TI, TO>(c, static_cast<const TI*>(x1), C1, static_cast<const TI*>(x2), C2, N, HW, G, eps, \
+                              gamma, beta, silu, static_cast<TO*>(y), pw)
+  if (in_dtype == DI_F16 && out_dtype == DI_F16) GN_CASE(__half, __half);
+  if (in_dtype == DI_BF16 && out_dtype == DI_BF16) GN_CASE(__nv_bfloat16, __nv_bfloat16);
+  if (in_dtype == DI_F32 && out_dtype == DI_F16) GN_CASE(float, __half);
+  if (in_dtype == DI_F32 && out_dtype == DI_BF16) GN_CASE(float, __nv_bfloat16);
+  if (in_dtype == DI_F32 && out_dtype == DI_F32) GN_CASE(float, float);
+#undef GN_CASE
+  return set_error(c, DI_EINVAL, "group_norm_nhwc: dtype combination");
+}
+
+size_t gn_nhwc_ws_bytes(int N, int HW, int G) { return sizeof(float2) * (size_t)N * gn_nhwc_chunks(HW) * G; }
+
+int group_norm_nchw(Ctx* c, const float* x, const float* g, const float* b, float* y, int N, int C, int HW, int G,
+                    float eps, int silu, int clamp) {
+  if (N <= 0 || C <= 0 || HW <= 0 || G <= 0 || C % G) return set_error(c, DI_EINVAL, "group_norm: bad cfg");
+  const size_t gsize = (size_t)(C / G) * HW;
+  const int target = 4 * c->num_sms;
+  int chunks = (int)std::max<size_t>(1, std::min<size_t>((gsize + 2047) / 2048, (size_t)std::max(1, target / (N * G))));
+  float2* partial = static_cast<float2*>(workspace(c, sizeof(float2) * (size_t)N * G * chunks, 0));
+  if (!partial) return set_error(c, DI_ENOMEM, "group_norm: workspace");
+  gn_nchw_partial<<<dim3(chunks, G, N), 256, 0, c->stream>>>(x, G, gsize, chunks, partial);
+  const size_t total = (size_t)N * C * HW;
+  const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
+  gn_nchw_apply<<<blocks, 256, 0, c->stream>>>(x, C, G, HW, chunks, partial, g, b, eps, silu, clamp, total, y);
+  return check_launch(c, "group_norm_nchw");
+}
+
+int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* g, const float* b, void* y, int rows,
+               int D, float eps) {
+  const int blocks = (rows + 7) / 8;
+#define LN_CASE(TI, TO)                                                                                         \
+  layer_norm_rows<TI, TO><<<blocks, 256, 0, c->stream>>>(static_cast<const TI*>(x), g, b, static_cast<TO*>(y), \
+                                                         rows, D, eps);                                         \
+  return check_launch(c, "layer_norm")
+  if (in_dtype == DI_F32 && out_dtype == DI_F32) { LN_CASE(float, float); }
+  if (in_dtype == DI_F16 && out_dtype == DI_F16) { LN_CASE(__half, __half); }
+  if (in_dtype == DI_BF16 && out_dtype == DI_BF16) { LN_CASE(__nv_bfloat16, __nv_bfloat16); }
+#undef LN_CASE
+  return set_error(c, DI_EINVAL, "layer_norm: dtype combination");
+}
+
+}  // namespace di
+
+using namespace di;
+
+extern "C" {
+
+int di_group_norm_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                       float eps, const float* gamma, const float* beta, int fuse_silu, void* y) {
+  Ctx* c = ctx_of(h);
+  if (!c) return DI_EINVAL;
+  return group_norm_nhwc(c, dtype, dtype, x1, C1, x2, x2 ? C2 : 0, N, HW, G, eps, gamma, beta, fuse_silu, y, nullptr);
+}
+
+int di_group_norm(di_ctx_t h, const float* X, const float* gamma, const float* beta, float* Y, const void* cfg32,
+                  int fuse_silu) {
+  Ctx* c = ctx_of(h);
+  if (!c || !cfg32) return DI_EINVAL;
+  const uint32_t* u = static_cast<const uint32_t*>(cfg32);
+  float eps;
+  memcpy(&eps, u + 4, 4);
+  const int N = u[0], G = u[1], cpg = u[2], HW = u[3];
+  return group_norm_nchw(c, X, gamma, beta, Y, N, G * cpg, HW, G, eps, fuse_silu, 1);
+}
+
+int di_instance_norm(di_ctx_t h, const float* X, const float* gamma, const float* beta, float* Y,
+                     const uint32_t cfg[4]) {
+  Ctx* c = ctx_of(h);
+  if (!c || !cfg) return DI_EINVAL;
+  // cfg = {C, HW, N, _}; eps hard-coded 1e-5 as in wgsl-ops.js:313-317.
+  return group_norm_nchw(c, X, gamma, beta, Y, (int)cfg[2], (int)cfg[0], (int)cfg[1], (int)cfg[0], 1e-5f, 0, 1);
+}
+
+int di_layer_norm(di_ctx_t h, const float* X, const float* gamma, const float* beta, float* Y, const uint32_t cfg[2]) {
+  Ctx* c = ctx_of(h);
+  if (!c || !cfg) return DI_EINVAL;
+  // cfg = {innerLen, rows}; eps 1e-5 (wgsl-ops.js:780).
+  return layer_norm(c, DI_F32, DI_F32, X, gamma, beta, Y, (int)cfg[1], (int)cfg[0], 1e-5f);
+}
+
+}  // extern "C"

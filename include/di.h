@@ -1,0 +1,162 @@
+/* di.h — C ABI of libdi, the B200 (sm_100a) kernels for draw-instant's SD-Turbo denoising hot path.
+ *
+ * Plain C: opaque handles, raw device pointers, sizes and the reference's own packed cfg blocks.
+ * Every entry returns DI_OK (0) or a negative DI_E* code and never traps; di_last_error() holds the
+ * message.  Launches are asynchronous on the context's stream; di_wait() is the only host sync
+ * (the analogue of device.queue.onSubmittedWorkDone()).
+ *
+ * Each declaration cites the reference interface it replaces (file:line in abgnydn/draw-instant).
+ */
+#ifndef DI_H_
+#define DI_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DI_API __attribute__((visibility("default")))
+#else
+#define DI_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DI_OK 0
+#define DI_EINVAL (-1)       /* bad argument / shape (the reference throws an Error) */
+#define DI_ECUDA (-2)        /* CUDA runtime / launch error */
+#define DI_ENOMEM (-3)       /* device allocation failed */
+#define DI_EUNSUPPORTED (-4) /* shape outside what a kernel handles (e.g. wgsl-executor.js:1082) */
+#define DI_EFAULT (-5)       /* sticky device fault: a kernel reported a timed-out wait */
+
+/* element types for the fast (NHWC) path */
+#define DI_F32 0
+#define DI_F16 1
+#define DI_BF16 2
+
+typedef struct di_ctx_s* di_ctx_t;
+typedef struct di_buf_s* di_buf_t;
+
+/* ---------------------------------------------------------------------------------------------
+ * Device, buffers, submission — unet-wgsl.js:64-84 (requestDevice + lost/error hooks),
+ * wgsl-ops.js:1172-1210 (createStorage/createOutput/readBack), wgsl-executor.js:1424-1425 (submit).
+ * ------------------------------------------------------------------------------------------- */
+DI_API int di_init(int device_ordinal, di_ctx_t* out);
+DI_API void di_destroy(di_ctx_t ctx);
+DI_API int di_set_stream(di_ctx_t ctx, void* cuda_stream); /* caller's cudaStream_t; NULL = default stream */
+DI_API void* di_get_stream(di_ctx_t ctx);
+DI_API int di_buf_alloc(di_ctx_t ctx, size_t bytes, di_buf_t* out);            /* createOutput */
+DI_API int di_buf_free(di_buf_t buf);                                          /* GPUBuffer.destroy */
+DI_API void* di_buf_ptr(di_buf_t buf);
+DI_API size_t di_buf_size(di_buf_t buf);
+DI_API int di_buf_upload(di_buf_t buf, const void* src, size_t bytes, size_t offset);  /* createStorage */
+DI_API int di_buf_download(di_buf_t buf, void* dst, size_t bytes, size_t offset);      /* readBack */
+DI_API int di_wait(di_ctx_t ctx);                                              /* onSubmittedWorkDone */
+DI_API const char* di_last_error(di_ctx_t ctx);
+/* getUNetGpuFault analogue (unet-wgsl.js:32-38): reads the device error word; >0 = fault flags. */
+DI_API int di_device_fault(di_ctx_t ctx);
+DI_API int di_clear_fault(di_ctx_t ctx);
+
+/* ---------------------------------------------------------------------------------------------
+ * wgsl-ops.js op families: fp32 tensors in the reference's layouts, cfg blocks exactly as the
+ * executor packs them (wgsl-executor.js OPS.* bodies).  Pointers are device pointers.
+ * ------------------------------------------------------------------------------------------- */
+/* unary ops, wgsl-ops.js:58-72 / :110-122 */
+#define DI_SIGMOID 0
+#define DI_SQRT 1
+#define DI_NEG 2
+#define DI_ABS 3
+#define DI_SIN 4
+#define DI_COS 5
+#define DI_EXP 6
+#define DI_LOG 7
+#define DI_SILU 8
+#define DI_GELU 9
+#define DI_ERF 10
+/* binary ops, wgsl-ops.js:130-134 */
+#define DI_ADD 0
+#define DI_SUB 1
+#define DI_MUL 2
+#define DI_DIV 3
+#define DI_POW 4
+#define DI_MAX 5
+#define DI_MIN 6
+
+DI_API int di_unary(di_ctx_t ctx, int op, const float* X, float* Y, uint32_t n);                 /* wgsl-ops.js:110 */
+/* operands wrap at their own length (i % nA, i % nB), wgsl-ops.js:147-151 */
+DI_API int di_binary(di_ctx_t ctx, int op, const float* A, uint32_t nA, const float* B, uint32_t nB, float* Y,
+              uint32_t n);                                                                 /* wgsl-ops.js:250 */
+DI_API int di_binary_bcast(di_ctx_t ctx, int op, const float* A, const float* B, float* Y,
+                    const uint32_t cfg[20]);                                               /* wgsl-ops.js:191 */
+DI_API int di_affine_bcast(di_ctx_t ctx, const float* A, const float* gamma, const float* beta, float* Y,
+                    const uint32_t cfg[20]);                                               /* wgsl-ops.js:239 */
+DI_API int di_softmax(di_ctx_t ctx, const float* X, float* Y, const uint32_t cfg[2]);             /* wgsl-ops.js:285 */
+DI_API int di_instance_norm(di_ctx_t ctx, const float* X, const float* gamma, const float* beta, float* Y,
+                     const uint32_t cfg[4]);                                               /* wgsl-ops.js:374 */
+/* cfg32 = {u32 N, u32 G, u32 cpg, u32 HW, f32 eps, pad x3} (wgsl-executor.js:738-743); fuse_silu applies
+ * x/(1+exp(-x)) after the affine (fused-resnet.js:121-166). */
+DI_API int di_group_norm(di_ctx_t ctx, const float* X, const float* gamma, const float* beta, float* Y,
+                  const void* cfg32, int fuse_silu);                                       /* wgsl-ops.js:460 */
+DI_API int di_layer_norm(di_ctx_t ctx, const float* X, const float* gamma, const float* beta, float* Y,
+                  const uint32_t cfg[2]);                                                  /* wgsl-ops.js:803 */
+/* cfg = {M, N, K, bBatched}; Y[z] = A[z] . B[z|0] (wgsl-ops.js:477-556). */
+DI_API int di_matmul(di_ctx_t ctx, const float* A, const float* B, float* Y, const uint32_t cfg[4], uint32_t batch);
+/* cfg = {M, N, K, transB}; Y = A . B(^T) + C[col] (wgsl-ops.js:821-897). */
+DI_API int di_gemm(di_ctx_t ctx, const float* A, const float* B, const float* C, float* Y, const uint32_t cfg[4]);
+/* cfg = {C_in, C_out, K, K*K, H, W, PAD, S, H_out, W_out, 0, 0} (wgsl-executor.js:1088); NCHW, any batch
+ * (the reference computes batch 0 only, wgsl-executor.js:1082). */
+DI_API int di_conv(di_ctx_t ctx, const float* X, const float* W, const float* bias, float* Y, const uint32_t cfg[12],
+            uint32_t n_batch);                                                             /* wgsl-ops.js:700 */
+DI_API int di_resize_nearest(di_ctx_t ctx, const float* X, float* Y, const uint32_t cfg[8]);     /* wgsl-ops.js:945 */
+DI_API int di_reduce_mean(di_ctx_t ctx, const float* X, float* Y, const uint32_t cfg[2]);        /* wgsl-ops.js:975 */
+DI_API int di_transpose(di_ctx_t ctx, const float* X, float* Y, const uint32_t cfg[20]);         /* wgsl-ops.js:1035 */
+DI_API int di_pow_scalar(di_ctx_t ctx, const float* X, float* Y, float exponent, uint32_t n);    /* wgsl-ops.js:1076 */
+DI_API int di_slice(di_ctx_t ctx, const float* X, float* Y, const uint32_t cfg[20]);             /* wgsl-ops.js:1126 */
+DI_API int di_concat_copy(di_ctx_t ctx, const float* X, float* Y, const uint32_t cfg[4]);        /* wgsl-ops.js:1159 */
+
+/* ---------------------------------------------------------------------------------------------
+ * Fast path: NHWC / token-major activations in fp16 or bf16 (dtype DI_F16 / DI_BF16), fp32
+ * accumulation on the tcgen05 tensor cores.  These are the kernels the fused blocks and the U-Net
+ * plan are built from.
+ * ------------------------------------------------------------------------------------------- */
+/* GroupNorm over channels-last x = concat(x1[..., C1], x2[..., C2]) per image (x2 may be NULL),
+ * y = (x - mean_g) * rsqrt(var_g + eps) * gamma + beta, optional SiLU; var = E[x^2] - mean^2
+ * clamped at 0 (wgsl-ops.js:390-458).  y has C1+C2 channels; in and out dtype = dtype. */
+DI_API int di_group_norm_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW,
+                       int G, float eps, const float* gamma, const float* beta, int fuse_silu, void* y);
+
+/* Linear / 1x1 conv: Y[M,N] = X[M,K] . W[N,K]^T (+ bias[N]) (+ R[M,N]); X = concat(X1[M,K1], X2[M,K-K1])
+ * along K when X2 != NULL (skip-connection concat without a copy).  K, K1 multiples of 64, N multiple of 16.
+ * Replaces the Gemm/MatMul epilogue variants of fused-block-full.js:128-186. */
+DI_API int di_linear(di_ctx_t ctx, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
+              const float* bias, const void* R, void* Y);
+/* GEGLU feed-forward up-projection: Y[M,F] = (X.Wv^T + bv) * gelu_erf(X.Wg^T + bg), W = [Wv; Wg] as [2F,K]
+ * (diffusers GEGLU; erf GELU of wgsl-ops.js:69).  F multiple of 64. */
+DI_API int di_linear_geglu(di_ctx_t ctx, int dtype, const void* X, int M, int K, const void* W, int F, const float* bias,
+                    void* Y);
+/* 3x3 conv, pad 1, stride 1 or 2, NHWC: x = concat(x1[...,C1], x2[...,C2]) (x2 may be NULL), W packed
+ * [Co][ky][kx][C1+C2]; y[N,Ho,Wo,Co] = conv + bias (+ temb[n][co] broadcast) (+ residual).  C1, C2 multiples
+ * of 64, Co multiple of 16, W and Ho*Wo powers of two with Wo <= 128.  (wgsl-ops.js:584-711 + the
+ * fused-resnet.js:173-208 epilogues.) */
+DI_API int di_conv3x3_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,
+                    int stride, const void* Wt, int Co, const float* bias, const float* temb, const void* residual,
+                    void* y);
+/* Packs a reference-layout fp32 conv weight [Co][Ci][3][3] into the [Co][3][3][Ci] dtype layout used above. */
+DI_API int di_pack_conv3x3(di_ctx_t ctx, int dtype, const float* w_oihw, int Co, int Ci, void* w_packed);
+
+/* Attention, head dim 64: O = softmax(Q K^T / 8) V per (b, h).  layout 0 = token-major [B,S,H,64]
+ * (fused-attn.js:46-48), 1 = head-major [B,H,S,64] (fused-cross-attn.js:134).  Any Sq, Skv >= 1.
+ * Replaces WGSL_FUSED_ATTN (fused-attn.js:199-307) and the cross-attention kernel (fused-cross-attn.js:112-173). */
+DI_API int di_attention(di_ctx_t ctx, int dtype, const void* Q, const void* K, const void* V, void* O, int B, int H, int Sq,
+                 int Skv, int layout);
+
+/* Timestep embedding, fused-tembed.js:73-130: y[b] = W2 . silu(W1 . [cos||sin](t_b f) + b1) + b2 with
+ * f_i = exp(-ln(1e4) i / (Din/2)); W1 [Dh,Din], W2 [Dh,Dh] row-major fp32; t, y fp32. */
+DI_API int di_tembed(di_ctx_t ctx, const float* t, int B, const float* W1, const float* b1, const float* W2,
+              const float* b2, int Din, int Dh, float* y);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DI_H_ */

@@ -1,0 +1,195 @@
+"""Parity of the fast-path sm_100a kernels (called through the C ABI) against the CPU oracle.
+
+Tolerance: max|got-ref|/max|ref| <= 1e-2 per block, fp16/bf16 storage with fp32
+accumulation; the oracle computes in fp32 on the same (storage-rounded) inputs."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import cosine, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def _t(a, dtype="f16"):
+    import torch
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dtype]
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dt).cuda().contiguous()
+
+
+def _np(t):
+    return t.float().cpu().numpy()
+
+
+def _round(a, dtype="f16"):
+    return _np(_t(a, dtype))
+
+
+def _code(dtype):
+    return {"f16": 1, "bf16": 2}[dtype]
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (4096, 320, 320), (77, 640, 1024), (64, 1280, 2560),
+                                   (200, 96, 192), (1024, 5120, 640)])
+def test_linear(ctx, dib, M, N, K, dtype):
+    import torch
+    rng = np.random.default_rng(M * 7 + N + K)
+    x = _round(rng.standard_normal((M, K)), dtype)
+    w = _round(rng.standard_normal((N, K)) / np.sqrt(K), dtype)
+    bias = rng.standard_normal(N).astype(np.float32)
+    r = _round(rng.standard_normal((M, N)), dtype)
+    X, W, R = _t(x, dtype), _t(w, dtype), _t(r, dtype)
+    Bi = _t(bias, "f32")
+    Y = torch.empty((M, N), dtype=X.dtype, device="cuda")
+    ctx.check(dib.lib().di_linear(ctx.h, _code(dtype), X.data_ptr(), K, None, M, K, W.data_ptr(), N, Bi.data_ptr(),
+                                  R.data_ptr(), Y.data_ptr()), "di_linear")
+    torch.cuda.synchronize()
+    ref = x @ w.T + bias + r
+    assert rel_err(_np(Y), ref) < TOL
+    assert ctx.fault() == 0
+
+
+def test_linear_concat_k(ctx, dib):
+    """K split over two sources (the skip-connection concat of the up blocks, read without a copy)."""
+    import torch
+    rng = np.random.default_rng(5)
+    M, K1, K2, N = 256, 128, 192, 128
+    a = _round(rng.standard_normal((M, K1)))
+    b = _round(rng.standard_normal((M, K2)))
+    w = _round(rng.standard_normal((N, K1 + K2)) / 16)
+    Y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    A, B, W = _t(a), _t(b), _t(w)
+    ctx.check(dib.lib().di_linear(ctx.h, 1, A.data_ptr(), K1, B.data_ptr(), M, K1 + K2, W.data_ptr(), N, None, None,
+                                  Y.data_ptr()), "di_linear concat")
+    torch.cuda.synchronize()
+    ref = np.concatenate([a, b], 1) @ w.T
+    assert rel_err(_np(Y), ref) < TOL
+
+
+def test_linear_geglu(ctx, dib, oracle):
+    import torch
+    rng = np.random.default_rng(9)
+    M, K, F = 300, 640, 2560
+    x = _round(rng.standard_normal((M, K)))
+    w = _round(rng.standard_normal((2 * F, K)) / np.sqrt(K))
+    bias = (rng.standard_normal(2 * F) * 0.1).astype(np.float32)
+    # packed layout: per 64-column output tile t, rows [128t, 128t+64) = value rows, then the gate rows
+    wp = np.empty_like(w)
+    bp = np.empty_like(bias)
+    for t in range(F // 64):
+        wp[128 * t:128 * t + 64] = w[64 * t:64 * t + 64]
+        wp[128 * t + 64:128 * t + 128] = w[F + 64 * t:F + 64 * t + 64]
+        bp[128 * t:128 * t + 64] = bias[64 * t:64 * t + 64]
+        bp[128 * t + 64:128 * t + 128] = bias[F + 64 * t:F + 64 * t + 64]
+    X, W, Bi = _t(x), _t(wp), _t(bp, "f32")
+    Y = torch.empty((M, F), dtype=torch.float16, device="cuda")
+    ctx.check(dib.lib().di_linear_geglu(ctx.h, 1, X.data_ptr(), M, K, W.data_ptr(), F, Bi.data_ptr(), Y.data_ptr()),
+              "geglu")
+    torch.cuda.synchronize()
+    pr = x @ w.T + bias
+    ref = pr[:, :F] * oracle.unary(9, pr[:, F:])  # erf GELU of wgsl-ops.js:69
+    assert rel_err(_np(Y), ref) < TOL
+
+
+@pytest.mark.parametrize("N,H,W,C1,C2,Co,stride", [
+    (1, 64, 64, 320, 0, 320, 1), (1, 32, 32, 640, 0, 640, 1), (2, 8, 8, 128, 0, 192, 1),
+    (1, 16, 16, 256, 128, 128, 1), (1, 8, 8, 128, 64, 64, 1), (1, 64, 64, 128, 0, 128, 2),
+    (2, 16, 16, 64, 0, 128, 2), (1, 4, 4, 64, 0, 64, 1), (1, 2, 2, 64, 0, 64, 2)])
+def test_conv3x3_nhwc(ctx, dib, oracle, N, H, W, C1, C2, Co, stride):
+    import torch
+    rng = np.random.default_rng(N + H + C1 + C2 + Co + stride)
+    Ci = C1 + C2
+    x = _round(rng.standard_normal((N, Ci, H, W)))
+    w = _round(rng.standard_normal((Co, Ci, 3, 3)) / np.sqrt(9 * Ci))
+    bias = rng.standard_normal(Co).astype(np.float32)
+    temb = rng.standard_normal((N, Co)).astype(np.float32)
+    Ho, Wo = H // stride, W // stride
+    res = _round(rng.standard_normal((N, Ho, Wo, Co)))
+    xh = np.transpose(x, (0, 2, 3, 1))
+    X1 = _t(xh[..., :C1])
+    X2 = _t(xh[..., C1:]) if C2 else None
+    Wf = _t(w, "f32")
+    Wp = torch.empty((Co, 9 * Ci), dtype=torch.float16, device="cuda")
+    L = dib.lib()
+    ctx.check(L.di_pack_conv3x3(ctx.h, 1, Wf.data_ptr(), Co, Ci, Wp.data_ptr()), "pack")
+    Y = torch.empty((N, Ho, Wo, Co), dtype=torch.float16, device="cuda")
+    Bi, Tb, R = _t(bias, "f32"), _t(temb, "f32"), _t(res)
+    ctx.check(L.di_conv3x3_nhwc(ctx.h, 1, X1.data_ptr(), C1, X2.data_ptr() if C2 else None, C2, N, H, W, stride,
+                                Wp.data_ptr(), Co, Bi.data_ptr(), Tb.data_ptr(), R.data_ptr(), Y.data_ptr()), "conv")
+    torch.cuda.synchronize()
+    ref = oracle.conv(x, w, bias, N, Ci, H, W, Co, 3, stride, 1)
+    ref = np.transpose(ref, (0, 2, 3, 1)) + temb[:, None, None, :] + res
+    assert rel_err(_np(Y), ref) < TOL
+    assert ctx.fault() == 0
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("B,H,Sq,Skv,layout", [(1, 2, 128, 128, 0), (2, 5, 256, 256, 1), (1, 3, 200, 77, 0),
+                                               (2, 2, 4096, 77, 1), (1, 2, 300, 1000, 0), (1, 1, 64, 1, 1)])
+def test_attention(ctx, dib, oracle, B, H, Sq, Skv, layout, dtype):
+    import torch
+    rng = np.random.default_rng(B * 100 + Sq + Skv)
+    shp_q = (B, Sq, H, 64) if layout == 0 else (B, H, Sq, 64)
+    shp_k = (B, Skv, H, 64) if layout == 0 else (B, H, Skv, 64)
+    q = _round(rng.standard_normal(shp_q) * 1.5, dtype)
+    k = _round(rng.standard_normal(shp_k) * 1.5, dtype)
+    v = _round(rng.standard_normal(shp_k), dtype)
+    Q, K, V = _t(q, dtype), _t(k, dtype), _t(v, dtype)
+    O = torch.zeros_like(Q)
+    ctx.check(dib.lib().di_attention(ctx.h, _code(dtype), Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), B, H,
+                                     Sq, Skv, layout), "attention")
+    torch.cuda.synchronize()
+    rows = None if Sq <= 512 else np.arange(0, Sq, 37)
+    ref = oracle.attention(q, k, v, B, H, Sq, Skv, layout, rows)
+    got = _np(O)
+    if rows is not None:
+        sel = (slice(None), rows) if layout == 0 else (slice(None), slice(None), rows)
+        got, ref = got[sel], ref[sel]
+    assert rel_err(got, ref) < TOL
+    assert cosine(got, ref) > 0.9999
+
+
+@pytest.mark.parametrize("N,HW,C1,C2,G,silu", [(1, 4096, 320, 0, 32, 1), (2, 256, 1280, 1280, 32, 1),
+                                               (1, 64, 640, 320, 32, 0), (1, 1024, 1920, 0, 32, 1)])
+def test_group_norm_nhwc(ctx, dib, oracle, N, HW, C1, C2, G, silu):
+    import torch
+    rng = np.random.default_rng(HW + C1)
+    C = C1 + C2
+    x = _round(rng.standard_normal((N, HW, C)) * 2 + 0.5)
+    g = (1 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(C)).astype(np.float32)
+    X1 = _t(x[..., :C1])
+    X2 = _t(x[..., C1:]) if C2 else None
+    Y = torch.empty((N, HW, C), dtype=torch.float16, device="cuda")
+    Gt, Bt = _t(g, "f32"), _t(b, "f32")
+    ctx.check(dib.lib().di_group_norm_nhwc(ctx.h, 1, X1.data_ptr(), C1, X2.data_ptr() if C2 else None, C2, N, HW, G,
+                                           1e-5, Gt.data_ptr(), Bt.data_ptr(), silu, Y.data_ptr()), "gn")
+    torch.cuda.synchronize()
+    xn = np.ascontiguousarray(np.transpose(x, (0, 2, 1)))  # NCHW for the oracle
+    ref = oracle.group_norm(xn, g, b, N, C, HW, G, 1e-5, silu=bool(silu))
+    ref = np.transpose(ref, (0, 2, 1))
+    assert rel_err(_np(Y), ref) < TOL
+
+
+def test_tembed(ctx, dib, oracle):
+    import torch
+    rng = np.random.default_rng(3)
+    W1 = (rng.standard_normal((1280, 320)) * 0.05).astype(np.float32)
+    b1 = (rng.standard_normal(1280) * 0.05).astype(np.float32)
+    W2 = (rng.standard_normal((1280, 1280)) * 0.03).astype(np.float32)
+    b2 = (rng.standard_normal(1280) * 0.05).astype(np.float32)
+    t = np.array([999.0, 500.0, 1.0], np.float32)
+    T = _t(t, "f32")
+    Y = torch.empty((3, 1280), dtype=torch.float32, device="cuda")
+    args = [_t(a, "f32") for a in (W1, b1, W2, b2)]
+    ctx.check(dib.lib().di_tembed(ctx.h, T.data_ptr(), 3, *[a.data_ptr() for a in args], 320, 1280, Y.data_ptr()),
+              "tembed")
+    torch.cuda.synchronize()
+    ref = oracle.tembed(t, W1, b1, W2, b2, 320, 1280)
+    assert rel_err(_np(Y), ref) < 1e-4
