@@ -76,7 +76,26 @@ SIGNATURES = {
     "di_pack_conv3x3": (_I, [_P, _I, _P, _I, _I, _P]),
     "di_attention": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I]),
     "di_tembed": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _I, _P]),
+    "di_synth_uniform": (None, [ctypes.c_uint64, ctypes.c_char_p, _SZ, _F, _P]),
+    "di_synth_normal": (None, [ctypes.c_uint64, ctypes.c_char_p, _SZ, _F, _F, _P]),
+    "di_unet_create": (_I, [_P, _I, _I, _I, _I, ctypes.c_uint64, _P, _P, ctypes.POINTER(_P)]),
+    "di_unet_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "di_unet_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "di_unet_forward": (_I, [_P]),
+    "di_unet_forward_host": (_I, [_P, _P, _P, _P, _P]),
+    "di_unet_destroy": (None, [_P]),
+    "di_resnet_block_create": (_I, [_P, _I, _I, _I, _I, _I, ctypes.c_uint64, _F, _I, _P, _P, ctypes.POINTER(_P)]),
+    "di_resnet_block_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "di_resnet_block_run": (_I, [_P]),
+    "di_resnet_block_destroy": (None, [_P]),
+    "di_transformer_block_create": (_I, [_P, _I, _I, _I, _I, _I, ctypes.c_uint64, _P, _P, ctypes.POINTER(_P)]),
+    "di_transformer_block_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "di_transformer_block_run": (_I, [_P]),
+    "di_transformer_block_destroy": (None, [_P]),
 }
+
+WEIGHT_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_float),
+                             ctypes.c_void_p)
 
 _lib = None
 
@@ -109,6 +128,20 @@ def ptr(t) -> int | None:
     if not t.is_contiguous():
         raise DIError("libdi ops take contiguous tensors")
     return t.data_ptr()
+
+
+class DeviceView:
+    """Zero-copy torch view of a libdi-owned device buffer (via __cuda_array_interface__)."""
+
+    def __init__(self, p: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(p), False),
+                                         "version": 3, "strides": None}
+
+
+def view(p, shape, dtype: str = "f32"):
+    import torch
+    ts = {"f32": "<f4", "f16": "<f2"}[dtype]
+    return torch.as_tensor(DeviceView(p if isinstance(p, int) else p.value, shape, ts), device="cuda")
 
 
 def u32(*vals) -> ctypes.Array:

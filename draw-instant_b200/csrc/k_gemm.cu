@@ -41,8 +41,8 @@ struct GemmParams {
   int cin_blocks;  // conv: channel blocks per tap
   int HWo, Wo;     // conv: output pixels per image, output width
   const float* bias;
-  const float* rowvec;  // adds rowvec[(m / rowvec_div) * N + n]
-  int rowvec_div;
+  const float* rowvec;  // adds rowvec[(m / rowvec_div) * rowvec_ld + n]
+  int rowvec_div, rowvec_ld;
   const void* residual;  // [M, ldr] (out dtype, or fp32 when res_f32)
   int ldr, res_f32;
   void* out;
@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
             for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
           }
           if (p.rowvec) {
-            const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.N + nb;
+            const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.rowvec_ld + nb;
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
           }
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
           for (int j = 0; j < 32 && nb + j < p.N; ++j) {
             float x = v[j];
             if (p.bias) x += p.bias[nb + j];
-            if (p.rowvec) x += p.rowvec[(size_t)(m / p.rowvec_div) * p.N + nb + j];
+            if (p.rowvec) x += p.rowvec[(size_t)(m / p.rowvec_div) * p.rowvec_ld + nb + j];
             if (p.residual) x += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
             store_one(p.out, (size_t)m * p.ldo + nb + j, x, p.out_f32, BF16);
           }
@@ -393,6 +393,7 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
   p.bias = bias;
   p.rowvec = rowvec;
   p.rowvec_div = rowvec_div > 0 ? rowvec_div : 1;
+  p.rowvec_ld = N;
   p.residual = R;
   p.ldr = N;
   p.res_f32 = res_f32;
@@ -412,7 +413,7 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
 
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
-                 void* y, int out_f32) {
+                 void* y, int out_f32, int temb_ld) {
   if (C1 <= 0 || C1 % 64 || (x2 && (C2 <= 0 || C2 % 64)) || Co % 16 || (stride != 1 && stride != 2))
     return set_error(c, DI_EINVAL, "conv3x3: channels must be multiples of 64 (Co of 16), stride 1 or 2");
   if (stride == 2 && (x2 || (H % 2) || (W % 2)))
@@ -448,6 +449,7 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
   p.bias = bias;
   p.rowvec = temb;
   p.rowvec_div = Ho * Wo;
+  p.rowvec_ld = temb_ld > 0 ? temb_ld : Co;
   p.residual = residual;
   p.ldr = Co;
   p.res_f32 = res_f32;
@@ -505,7 +507,7 @@ int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x
                     void* y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
-  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0);
+  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0, Co);
 }
 
 int di_pack_conv3x3(di_ctx_t h, int dtype, const float* w, int Co, int Ci, void* out) {

@@ -1,0 +1,922 @@
+// plan.cu — the SD-Turbo U-Net forward (and its ResNet / transformer blocks) as a pre-planned,
+// CUDA-graph-replayed sequence of sm_100a kernels.
+//
+// The reference walks a 5,478-node ONNX graph op by op on every call (Executor.run,
+// wgsl-executor.js:1248-1466): per-node uniform-buffer creation, buffer-pool lookups, NCHW fp32.  Here the
+// architecture (SD2.1 / SD-Turbo: 320/640/1280/1280 channels, 2 ResNet blocks per level, a transformer
+// at the first three levels, head dim 64, cross-attention over a 77x1024 context) is walked once at
+// plan time: weights are drawn (or supplied by the caller by parameter name), converted to fp16 and
+// packed for the kernels; every activation and scratch buffer is placed; each kernel launch is
+// recorded with fixed pointers and TMA descriptors.  The first forward captures the launches into a
+// CUDA graph; every later forward is one graph launch.
+//
+// Data layout in HBM: activations NHWC fp16 (the transformer's token-major [B, H*W, C] is the same
+// memory), weights fp16 K-major ([Co][ky][kx][Ci] for 3x3 convs, [out][in] for linears, Q/K/V stacked
+// into one [3C, C] matrix, cross-attention K/V stacked into [2C, 1024], GEGLU value/gate rows
+// interleaved per 64-column tile), biases and norm affines fp32.
+//
+// Fusions: GroupNorm apply + SiLU in one pass that also materialises the skip concat; bias, the
+// timestep-embedding broadcast and the residual in the conv / linear epilogues; the GEGLU gate in the
+// FF up-projection epilogue; the 1x1 shortcut reads the two concat sources directly; every ResNet
+// block's time projection in one GEMV; Q/K/V in one GEMM; attention as one flash kernel.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "di_common.cuh"
+
+namespace di {
+
+int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
+                const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
+                int rowvec_div);
+int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
+                 const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
+                 void* y, int out_f32, int temb_ld);
+int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1, const void* x2, int C2, int N,
+                    int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
+                    void* partial_ws);
+size_t gn_nhwc_ws_bytes(int N, int HW, int G);
+int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* g, const float* b, void* y, int rows,
+               int D, float eps);
+int attention(Ctx* c, int dtype, const void* Q, const void* K, const void* V, void* O, int B, int H, int Sq, int Skv,
+              int layout, long long ld_q, long long ld_k, long long ld_v, long long ld_o);
+int gemv(Ctx* c, const float* x, int B, int K, const void* W, int w_f16, const float* bias, int N, int silu_in,
+         float* y, int ldy);
+int tembed(Ctx* c, const float* t, int B, const float* W1, const float* b1, const float* W2, const float* b2, int Din,
+           int Dh, float* hidden, float* y);
+int nchw_to_nhwc(Ctx* c, int in_dt, int out_dt, const void* x, void* y, int N, int C, int HW);
+int nhwc_to_nchw(Ctx* c, int in_dt, int out_dt, const void* x, void* y, int N, int C, int HW);
+
+// ---------------------------------------------------------------------------------------------
+// Seeded synthetic parameters (the build's documented scheme, restated independently of the CPU
+// oracle; tests compare the two bit for bit):
+//   key = mix64(seed * 0x9E3779B97F4A7C15 + fnv1a64(name)),
+//   u_i = (mix64(key + (i+1) * 0x9E3779B97F4A7C15) >> 40) * 2^-24,
+//   uniform(b) = (2u - 1) * b in float; normal = Box-Muller (double) on (u_2j, u_2j+1), cos even / sin odd.
+// ---------------------------------------------------------------------------------------------
+static inline uint64_t smix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+static inline uint64_t name_hash(const char* s) {
+  uint64_t h = 0xcbf29ce484222325ULL;
+  while (*s) { h ^= (unsigned char)*s++; h *= 0x100000001b3ULL; }
+  return h;
+}
+static inline float unit24(uint64_t key, uint64_t i) {
+  return (float)(smix(key + (i + 1) * 0x9E3779B97F4A7C15ULL) >> 40) * (1.0f / 16777216.0f);
+}
+template <typename F>
+static void par_for(size_t n, F f) {
+  const unsigned nt = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+  if (n < (1u << 16) || nt == 1) { for (size_t i = 0; i < n; ++i) f(i); return; }
+  std::vector<std::thread> th;
+  const size_t per = (n + nt - 1) / nt;
+  for (unsigned t = 0; t < nt; ++t)
+    th.emplace_back([=] { for (size_t i = t * per; i < std::min(n, (t + 1) * per); ++i) f(i); });
+  for (auto& x : th) x.join();
+}
+void synth_uniform(uint64_t seed, const char* name, size_t n, float bound, float* out) {
+  const uint64_t key = smix(seed * 0x9E3779B97F4A7C15ULL + name_hash(name));
+  par_for(n, [&](size_t i) {
+    const float u = unit24(key, i);
+    const float t = 2.0f * u - 1.0f;
+    out[i] = t * bound;
+  });
+}
+void synth_normal(uint64_t seed, const char* name, size_t n, float mean, float stdv, float* out) {
+  const uint64_t key = smix(seed * 0x9E3779B97F4A7C15ULL + name_hash(name));
+  par_for(n, [&](size_t i) {
+    const uint64_t j = i & ~(size_t)1;
+    double u1 = (double)unit24(key, j), u2 = (double)unit24(key, j + 1);
+    if (u1 < 1.0 / 16777216.0) u1 = 1.0 / 16777216.0;
+    const double r = std::sqrt(-2.0 * std::log(u1));
+    const double z = (i & 1) ? r * std::sin(6.283185307179586 * u2) : r * std::cos(6.283185307179586 * u2);
+    out[i] = (float)((double)mean + (double)stdv * z);
+  });
+}
+
+namespace {
+
+__global__ void latent_in_kernel(const float* __restrict__ x, __half* __restrict__ y, int N, int C, int HW, int Cp) {
+  const size_t total = (size_t)N * HW * Cp;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int c = i % Cp;
+    const size_t np = i / Cp;
+    const int p = np % HW;
+    const size_t n = np / HW;
+    y[i] = __float2half_rn(c < C ? x[(n * C + c) * HW + p] : 0.f);
+  }
+}
+__global__ void latent_out_kernel(const __half* __restrict__ x, int Cp, float* __restrict__ y, int N, int C, int HW) {
+  const size_t total = (size_t)N * C * HW;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int p = i % HW;
+    const size_t nc = i / HW;
+    const int c = nc % C;
+    const size_t n = nc / C;
+    y[i] = __half2float(x[(n * HW + p) * Cp + c]);
+  }
+}
+// Nearest 2x upsample, NHWC, 16-byte vectors (index math of wgsl-ops.js:921-943 with W_out = 2 W_in).
+__global__ void upsample2_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, int N, int H, int W, int Cv) {
+  const size_t total = (size_t)N * 4 * H * W * Cv;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int v = i % Cv;
+    size_t r = i / Cv;
+    const int ox = r % (2 * W);
+    r /= (2 * W);
+    const int oy = r % (2 * H);
+    const size_t n = r / (2 * H);
+    y[i] = x[((n * H + oy / 2) * W + ox / 2) * Cv + v];
+  }
+}
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(x[i]);
+}
+
+}  // namespace
+
+typedef int (*WeightFn)(const char* name, size_t n, float* dst, void* user);
+
+struct Act {
+  void* p = nullptr;
+  int N = 0, H = 0, W = 0, C = 0;
+  size_t bytes() const { return (size_t)N * H * W * C * 2; }
+};
+
+// ---------------------------------------------------------------------------------------------
+// Plan: arenas, parameter loading, recorded launches, CUDA graph.
+// ---------------------------------------------------------------------------------------------
+struct Plan {
+  Ctx* c = nullptr;
+  uint64_t seed = 0;
+  WeightFn wfn = nullptr;
+  void* wuser = nullptr;
+  cudaStream_t stream = nullptr;  // private stream: graph capture needs a non-legacy stream
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  std::vector<void*> blocks;      // cudaMalloc'd regions
+  std::vector<std::function<int()>> ops;
+  cudaGraphExec_t gexec = nullptr;
+  int launches = 0;               // kernels per forward (recorded ops)
+  size_t weight_bytes = 0, act_bytes = 0;
+  int err = DI_OK;
+  std::string errmsg;
+
+  // temporary bump arena (reset per block; stream order makes reuse safe)
+  char* tmp_base = nullptr;
+  size_t tmp_cap = 0, tmp_off = 0, tmp_peak = 0;
+
+  ~Plan() {
+    if (gexec) cudaGraphExecDestroy(gexec);
+    if (stream) { cudaStreamSynchronize(stream); cudaStreamDestroy(stream); }
+    if (ev_in) cudaEventDestroy(ev_in);
+    if (ev_out) cudaEventDestroy(ev_out);
+    for (void* b : blocks) cudaFree(b);
+  }
+
+  void fail(int code, const std::string& m) {
+    if (err == DI_OK) { err = code; errmsg = m; }
+  }
+
+  void* dalloc(size_t bytes) {
+    if (err) return nullptr;
+    void* p = nullptr;
+    if (cudaMalloc(&p, std::max<size_t>(bytes, 256)) != cudaSuccess) {
+      cudaGetLastError();
+      fail(DI_ENOMEM, "plan: cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+      return nullptr;
+    }
+    blocks.push_back(p);
+    return p;
+  }
+  void* act_alloc(size_t bytes) {
+    act_bytes += bytes;
+    return dalloc(bytes);
+  }
+  void* tmp(size_t bytes) {
+    const size_t off = (tmp_off + 255) & ~(size_t)255;
+    if (off + bytes > tmp_cap) {
+      fail(DI_ENOMEM, "plan: temporary arena exhausted");
+      return nullptr;
+    }
+    tmp_off = off + bytes;
+    tmp_peak = std::max(tmp_peak, tmp_off);
+    return tmp_base + off;
+  }
+  void tmp_reset() { tmp_off = 0; }
+
+  // kind 0: uniform weight (fan_out > 0) or bias (fan_out == 0); 1: normal(1, 0.02) (norm gamma);
+  // 2: normal(0, 0.02) (norm beta).  init_mode picks the uniform bound:
+  //   0 torch layer default: +-1/sqrt(fan_in) for weights and biases (the U-Net)
+  //   1 Kaiming-uniform weights +-sqrt(6/fan_in), default biases (config 1)
+  //   2 Xavier-uniform weights +-sqrt(6/(fan_in+fan_out)), zero biases (config 2)
+  int init_mode = 0;
+  std::vector<float> host_param(const std::string& name, size_t n, int kind, int fan_in, int fan_out = 0) {
+    std::vector<float> h(n);
+    if (wfn && wfn(name.c_str(), n, h.data(), wuser) == 0) {
+    } else if (kind == 0) {
+      float bound = 1.0f / std::sqrt((float)fan_in);
+      if (init_mode == 1 && fan_out > 0) bound = std::sqrt(6.0f / (float)fan_in);
+      if (init_mode == 2) bound = fan_out > 0 ? std::sqrt(6.0f / (float)(fan_in + fan_out)) : 0.0f;
+      if (bound == 0.0f) std::fill(h.begin(), h.end(), 0.0f);
+      else synth_uniform(seed, name.c_str(), n, bound, h.data());
+    } else {
+      synth_normal(seed, name.c_str(), n, kind == 1 ? 1.0f : 0.0f, 0.02f, h.data());
+    }
+    return h;
+  }
+  static void round_f16(std::vector<float>& v) {
+    par_for(v.size(), [&](size_t i) { v[i] = __half2float(__float2half_rn(v[i])); });
+  }
+  const float* upload_f32(const std::vector<float>& v) {
+    float* d = static_cast<float*>(dalloc(v.size() * 4));
+    if (!d) return nullptr;
+    cudaMemcpy(d, v.data(), v.size() * 4, cudaMemcpyHostToDevice);
+    weight_bytes += v.size() * 4;
+    return d;
+  }
+  const void* upload_f16(const std::vector<float>& v) {
+    std::vector<__half> h(v.size());
+    par_for(v.size(), [&](size_t i) { h[i] = __float2half_rn(v[i]); });
+    void* d = dalloc(h.size() * 2);
+    if (!d) return nullptr;
+    cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
+    weight_bytes += h.size() * 2;
+    return d;
+  }
+  // fp32 vector of fp16-rounded parameter values (biases, norm affines)
+  const float* vec(const std::string& name, size_t n, int kind, int fan_in) {
+    auto h = host_param(name, n, kind, fan_in);
+    round_f16(h);
+    return upload_f32(h);
+  }
+
+  void record(std::function<int()> f) {
+    ops.push_back(std::move(f));
+    ++launches;
+  }
+
+  int run_ops() {
+    for (auto& f : ops) {
+      int r = f();
+      if (r) return r;
+    }
+    return DI_OK;
+  }
+
+  // Enqueue one forward on the plan's stream, ordered after / before the context stream.
+  int forward() {
+    if (err) return err;
+    cudaEventRecord(ev_in, c->stream);
+    cudaStreamWaitEvent(stream, ev_in, 0);
+    cudaStream_t saved = c->stream;
+    c->stream = stream;
+    int r = DI_OK;
+    if (!gexec) {
+      // One eager pass first: it validates every launch outside capture and performs the one-time
+      // per-kernel attribute set-up, so the captured pass issues kernel launches only.
+      r = run_ops();
+      if (r == DI_OK && cudaStreamSynchronize(stream) != cudaSuccess) r = set_error(c, DI_ECUDA, "plan: eager pass");
+      if (r != DI_OK) {
+        c->stream = saved;
+        return r;
+      }
+      cudaGraph_t g = nullptr;
+      if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        c->stream = saved;
+        return set_error(c, DI_ECUDA, "plan: begin capture failed");
+      }
+      r = run_ops();
+      cudaError_t e = cudaStreamEndCapture(stream, &g);
+      if (r == DI_OK && e == cudaSuccess) {
+        if (cudaGraphInstantiate(&gexec, g, 0) != cudaSuccess) r = set_error(c, DI_ECUDA, "plan: instantiate");
+      } else if (r == DI_OK) {
+        r = set_error(c, DI_ECUDA, std::string("plan: capture failed: ") + cudaGetErrorString(e));
+      }
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+    }
+    if (r == DI_OK && cudaGraphLaunch(gexec, stream) != cudaSuccess) r = set_error(c, DI_ECUDA, "plan: graph launch");
+    c->stream = saved;
+    cudaEventRecord(ev_out, stream);
+    cudaStreamWaitEvent(c->stream, ev_out, 0);
+    return r;
+  }
+
+  bool init(Ctx* ctx, uint64_t sd, WeightFn f, void* u, size_t tmp_bytes) {
+    c = ctx;
+    seed = sd;
+    wfn = f;
+    wuser = u;
+    if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return false;
+    cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+    tmp_cap = tmp_bytes;
+    tmp_base = static_cast<char*>(dalloc(tmp_bytes));
+    act_bytes += tmp_bytes;
+    return tmp_base != nullptr;
+  }
+
+  // ---------------------------------------------------------------------------------------------
+  // Layer builders (parameter names follow diffusers' UNet2DConditionModel).
+  // ---------------------------------------------------------------------------------------------
+  // 3x3 conv weight packed [Co][ky][kx][Cin_padded]; input channels beyond Ci are zero.
+  const void* conv_weight(const std::string& name, int Co, int Ci, int Cip, int Cop) {
+    auto w = host_param(name, (size_t)Co * Ci * 9, 0, Ci * 9, Co * 9);
+    std::vector<float> pk((size_t)Cop * 9 * Cip, 0.0f);
+    par_for((size_t)Co, [&](size_t co) {
+      for (int ci = 0; ci < Ci; ++ci)
+        for (int t = 0; t < 9; ++t) pk[(co * 9 + t) * Cip + ci] = w[(co * Ci + ci) * 9 + t];
+    });
+    return upload_f16(pk);
+  }
+  const float* bias_padded(const std::string& name, int Co, int Cop, int fan_in) {
+    auto b = host_param(name, Co, 0, fan_in);
+    round_f16(b);
+    b.resize(Cop, 0.0f);
+    return upload_f32(b);
+  }
+
+  Act new_act(int N, int H, int W, int C) {
+    Act a;
+    a.N = N; a.H = H; a.W = W; a.C = C;
+    a.p = act_alloc(a.bytes());
+    return a;
+  }
+
+  Act conv3x3(const std::string& pre, const Act& x, int Co, int stride, const Act* x2 = nullptr) {
+    const int Ci = x.C + (x2 ? x2->C : 0);
+    const void* w = conv_weight(pre + ".weight", Co, Ci, Ci, Co);
+    const float* b = bias_padded(pre + ".bias", Co, Co, Ci * 9);
+    Act y = new_act(x.N, x.H / stride, x.W / stride, Co);
+    Ctx* cc = c;
+    const Act xx = x;
+    const void* p2 = x2 ? x2->p : nullptr;
+    const int C2 = x2 ? x2->C : 0;
+    record([=] { return gemm_conv3x3(cc, DI_F16, xx.p, xx.C, p2, C2, xx.N, xx.H, xx.W, stride, w, Co, b, nullptr,
+                                     nullptr, 0, y.p, 0, Co); });
+    return y;
+  }
+
+  Act upsample(const Act& x) {
+    Act y = new_act(x.N, x.H * 2, x.W * 2, x.C);
+    Ctx* cc = c;
+    const Act xx = x;
+    record([=] {
+      const size_t total = (size_t)xx.N * 4 * xx.H * xx.W * (xx.C / 8);
+      upsample2_kernel<<<(int)std::min<size_t>((total + 255) / 256, 16 * cc->num_sms), 256, 0, cc->stream>>>(
+          static_cast<const uint4*>(xx.p), static_cast<uint4*>(y.p), xx.N, xx.H, xx.W, xx.C / 8);
+      return check_launch(cc, "upsample2");
+    });
+    return y;
+  }
+
+  // GroupNorm(+SiLU) of concat(x1, x2) into a temporary.
+  void* gn(const std::string& pre, const Act& x1, const Act* x2, float eps, int silu) {
+    const int C = x1.C + (x2 ? x2->C : 0), HW = x1.H * x1.W;
+    const float* g = vec(pre + ".weight", C, 1, 1);
+    const float* b = vec(pre + ".bias", C, 2, 1);
+    void* y = tmp((size_t)x1.N * HW * C * 2);
+    void* part = tmp(gn_nhwc_ws_bytes(x1.N, HW, 32));
+    Ctx* cc = c;
+    const Act a = x1;
+    const void* p2 = x2 ? x2->p : nullptr;
+    const int C2 = x2 ? x2->C : 0;
+    record([=] { return group_norm_nhwc(cc, DI_F16, DI_F16, a.p, a.C, p2, C2, a.N, HW, 32, eps, g, b, silu, y,
+                                        part); });
+    return y;
+  }
+
+  // Linear on token rows: Y[M, N] = X[M, K] W^T (+b) (+R).
+  const void* lin_weight(const std::string& name, int N, int K) {
+    return upload_f16(host_param(name, (size_t)N * K, 0, K, N));
+  }
+  void linear(const void* X, int M, int K, const void* W, int N, const float* b, const void* R, void* Y,
+              const void* X2 = nullptr, int K1 = 0) {
+    Ctx* cc = c;
+    record([=] { return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1); });
+  }
+
+  // ResnetBlock2D on concat(x1, x2): gn1+silu -> conv1 (+b1 +time proj) -> gn2+silu -> conv2 (+b2 + shortcut).
+  struct TimeSlice { int off, C; };
+  std::vector<float> tproj_w, tproj_b;  // concatenated time projections (host staging)
+  int tproj_rows = 0;
+  float* temb_all = nullptr;            // [B, tproj_rows] fp32, computed once per forward
+  int tproj_ld = 0;
+
+  Act resnet(const std::string& pre, const Act& x1, const Act* x2, int Co) {
+    tmp_reset();
+    const int Ci = x1.C + (x2 ? x2->C : 0);
+    void* a = gn(pre + ".norm1", x1, x2, 1e-5f, 1);
+    // time projection rows appended to the shared GEMV
+    {
+      auto w = host_param(pre + ".time_emb_proj.weight", (size_t)Co * 1280, 0, 1280, Co);
+      auto b = host_param(pre + ".time_emb_proj.bias", Co, 0, 1280);
+      round_f16(w);
+      round_f16(b);
+      tproj_w.insert(tproj_w.end(), w.begin(), w.end());
+      tproj_b.insert(tproj_b.end(), b.begin(), b.end());
+    }
+    const int toff = tproj_rows;
+    tproj_rows += Co;
+    const void* w1 = conv_weight(pre + ".conv1.weight", Co, Ci, Ci, Co);
+    const float* b1 = bias_padded(pre + ".conv1.bias", Co, Co, Ci * 9);
+    Act h;
+    h.N = x1.N; h.H = x1.H; h.W = x1.W; h.C = Co;
+    h.p = tmp(h.bytes());
+    Ctx* cc = c;
+    const int N = x1.N, H = x1.H, W = x1.W;
+    Plan* self = this;
+    record([=] { return gemm_conv3x3(cc, DI_F16, a, Ci, nullptr, 0, N, H, W, 1, w1, Co, b1,
+                                     self->temb_all + toff, nullptr, 0, h.p, 0, self->tproj_ld); });
+    void* a2 = gn(pre + ".norm2", h, nullptr, 1e-5f, 1);
+    const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
+    const float* b2 = bias_padded(pre + ".conv2.bias", Co, Co, Co * 9);
+    const void* res = x1.p;
+    if (Ci != Co) {
+      const void* ws = lin_weight(pre + ".conv_shortcut.weight", Co, Ci);
+      const float* bs = vec(pre + ".conv_shortcut.bias", Co, 0, Ci);
+      void* s = tmp((size_t)N * H * W * Co * 2);
+      linear(x1.p, N * H * W, Ci, ws, Co, bs, nullptr, s, x2 ? x2->p : nullptr, x1.C);
+      res = s;
+    }
+    Act y = new_act(N, H, W, Co);
+    record([=] { return gemm_conv3x3(cc, DI_F16, a2, Co, nullptr, 0, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0,
+                                     Co); });
+    return y;
+  }
+
+  // Transformer2DModel (linear proj_in/out) + BasicTransformerBlock; ctx16 = [N, Sk, Cctx] fp16.
+  Act transformer(const std::string& pre, const Act& x, const void* ctx16, int Sk, int Cctx) {
+    tmp_reset();
+    const int N = x.N, HW = x.H * x.W, C = x.C, M = N * HW, heads = C / 64;
+    const std::string tb = pre + ".transformer_blocks.0";
+    void* a = gn(pre + ".norm", x, nullptr, 1e-6f, 0);
+    const void* wpi = lin_weight(pre + ".proj_in.weight", C, C);
+    const float* bpi = vec(pre + ".proj_in.bias", C, 0, C);
+    void* h0 = tmp((size_t)M * C * 2);
+    linear(a, M, C, wpi, C, bpi, nullptr, h0);
+    Ctx* cc = c;
+    // --- self attention ---
+    const float* g1 = vec(tb + ".norm1.weight", C, 1, 1);
+    const float* be1 = vec(tb + ".norm1.bias", C, 2, 1);
+    void* n1 = tmp((size_t)M * C * 2);
+    record([=] { return layer_norm(cc, DI_F16, DI_F16, h0, g1, be1, n1, M, C, 1e-5f); });
+    std::vector<float> wqkv;
+    for (const char* nm : {".attn1.to_q.weight", ".attn1.to_k.weight", ".attn1.to_v.weight"}) {
+      auto w = host_param(tb + nm, (size_t)C * C, 0, C, C);
+      wqkv.insert(wqkv.end(), w.begin(), w.end());
+    }
+    const void* Wqkv = upload_f16(wqkv);
+    void* qkv = tmp((size_t)M * 3 * C * 2);
+    linear(n1, M, C, Wqkv, 3 * C, nullptr, nullptr, qkv);
+    void* o1 = tmp((size_t)M * C * 2);
+    record([=] {
+      const char* base = static_cast<const char*>(qkv);
+      return attention(cc, DI_F16, base, base + (size_t)C * 2, base + (size_t)2 * C * 2, o1, N, heads, HW, HW, 0,
+                       3 * C, 3 * C, 3 * C, C);
+    });
+    const void* wo1 = lin_weight(tb + ".attn1.to_out.0.weight", C, C);
+    const float* bo1 = vec(tb + ".attn1.to_out.0.bias", C, 0, C);
+    void* h1 = tmp((size_t)M * C * 2);
+    linear(o1, M, C, wo1, C, bo1, h0, h1);
+    // --- cross attention ---
+    const float* g2 = vec(tb + ".norm2.weight", C, 1, 1);
+    const float* be2 = vec(tb + ".norm2.bias", C, 2, 1);
+    void* n2 = tmp((size_t)M * C * 2);
+    record([=] { return layer_norm(cc, DI_F16, DI_F16, h1, g2, be2, n2, M, C, 1e-5f); });
+    const void* wq2 = lin_weight(tb + ".attn2.to_q.weight", C, C);
+    void* q2 = tmp((size_t)M * C * 2);
+    linear(n2, M, C, wq2, C, nullptr, nullptr, q2);
+    std::vector<float> wkv;
+    for (const char* nm : {".attn2.to_k.weight", ".attn2.to_v.weight"}) {
+      auto w = host_param(tb + nm, (size_t)C * Cctx, 0, Cctx, C);
+      wkv.insert(wkv.end(), w.begin(), w.end());
+    }
+    const void* Wkv = upload_f16(wkv);
+    void* kv = tmp((size_t)N * Sk * 2 * C * 2);
+    linear(ctx16, N * Sk, Cctx, Wkv, 2 * C, nullptr, nullptr, kv);
+    void* o2 = tmp((size_t)M * C * 2);
+    record([=] {
+      const char* base = static_cast<const char*>(kv);
+      return attention(cc, DI_F16, q2, base, base + (size_t)C * 2, o2, N, heads, HW, Sk, 0, C, 2 * C, 2 * C, C);
+    });
+    const void* wo2 = lin_weight(tb + ".attn2.to_out.0.weight", C, C);
+    const float* bo2 = vec(tb + ".attn2.to_out.0.bias", C, 0, C);
+    void* h2 = tmp((size_t)M * C * 2);
+    linear(o2, M, C, wo2, C, bo2, h1, h2);
+    // --- GEGLU feed-forward ---
+    const float* g3 = vec(tb + ".norm3.weight", C, 1, 1);
+    const float* be3 = vec(tb + ".norm3.bias", C, 2, 1);
+    void* n3 = tmp((size_t)M * C * 2);
+    record([=] { return layer_norm(cc, DI_F16, DI_F16, h2, g3, be3, n3, M, C, 1e-5f); });
+    const int F = 4 * C;
+    auto wff = host_param(tb + ".ff.net.0.proj.weight", (size_t)2 * F * C, 0, C, 2 * F);
+    auto bff = host_param(tb + ".ff.net.0.proj.bias", (size_t)2 * F, 0, C);
+    round_f16(bff);
+    std::vector<float> wp((size_t)2 * F * C), bp(2 * F);
+    for (int t = 0; t < F / 64; ++t) {
+      for (int r = 0; r < 64; ++r) {
+        std::memcpy(&wp[(size_t)(128 * t + r) * C], &wff[(size_t)(64 * t + r) * C], sizeof(float) * C);
+        std::memcpy(&wp[(size_t)(128 * t + 64 + r) * C], &wff[(size_t)(F + 64 * t + r) * C], sizeof(float) * C);
+        bp[128 * t + r] = bff[64 * t + r];
+        bp[128 * t + 64 + r] = bff[F + 64 * t + r];
+      }
+    }
+    const void* Wff = upload_f16(wp);
+    const float* Bff = upload_f32(bp);
+    void* g = tmp((size_t)M * F * 2);
+    record([=] { return gemm_linear(cc, DI_F16, n3, C, nullptr, M, C, Wff, 2 * F, Bff, nullptr, 0, g, 0, 1, nullptr,
+                                    1); });
+    const void* wf2 = lin_weight(tb + ".ff.net.2.weight", C, F);
+    const float* bf2 = vec(tb + ".ff.net.2.bias", C, 0, F);
+    void* h3 = tmp((size_t)M * C * 2);
+    linear(g, M, F, wf2, C, bf2, h2, h3);
+    // --- proj_out + block residual ---
+    const void* wpo = lin_weight(pre + ".proj_out.weight", C, C);
+    const float* bpo = vec(pre + ".proj_out.bias", C, 0, C);
+    Act y = new_act(N, x.H, x.W, C);
+    linear(h3, M, C, wpo, C, bpo, x.p, y.p);
+    return y;
+  }
+
+  // Builds the time-projection GEMV once every ResNet block has appended its rows; `at` is the op
+  // index it must run at (right after the timestep embedding).
+  void finish_time_proj(size_t at, const float* temb, int B) {
+    const void* W = upload_f16(tproj_w);
+    const float* b = upload_f32(tproj_b);
+    temb_all = static_cast<float*>(act_alloc(sizeof(float) * (size_t)B * tproj_rows));
+    tproj_ld = tproj_rows;
+    Ctx* cc = c;
+    const int rows = tproj_rows;
+    float* out = temb_all;
+    ops.insert(ops.begin() + at, [=] {
+      for (int b0 = 0; b0 < B; b0 += 8) {
+        const int nb = std::min(8, B - b0);
+        int r = gemv(cc, temb + (size_t)b0 * 1280, nb, 1280, W, 1, b, rows, 1, out + (size_t)b0 * rows, rows);
+        if (r) return r;
+      }
+      return DI_OK;
+    });
+    ++launches;
+    tproj_w.clear();
+    tproj_w.shrink_to_fit();
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// The three plans.
+// ---------------------------------------------------------------------------------------------
+struct UNetPlan {
+  Plan P;
+  int B = 1, H = 64, W = 64, Sk = 77;
+  float* latent = nullptr;  // [B,4,H,W] fp32 NCHW (input)
+  float* tvals = nullptr;   // [B] fp32
+  float* ctx32 = nullptr;   // [B,Sk,1024] fp32
+  float* out = nullptr;     // [B,4,H,W] fp32 NCHW
+  double gflop = 0;
+};
+
+static size_t unet_tmp_bytes(int B, int H, int W) {
+  // largest block working set: the 64x64 transformer (GEGLU hidden 4C plus QKV 3C and six C-wide temps)
+  const size_t M = (size_t)B * H * W;
+  return M * 320 * 2 * (16 + 3 + 8) + (size_t)B * 77 * 2 * 1280 * 2 + (64 << 20);
+}
+
+static int build_unet(UNetPlan* u) {
+  Plan& P = u->P;
+  const int B = u->B, H = u->H, W = u->W, Sk = u->Sk;
+  Ctx* cc = P.c;
+  u->latent = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 4 * H * W));
+  u->tvals = static_cast<float*>(P.act_alloc(sizeof(float) * B));
+  u->ctx32 = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * Sk * 1024));
+  u->out = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 4 * H * W));
+  __half* ctx16 = static_cast<__half*>(P.act_alloc(sizeof(__half) * (size_t)B * Sk * 1024));
+  if (P.err) return P.err;
+  // inputs: ctx fp32 -> fp16, latent NCHW fp32 -> NHWC fp16 padded to 64 channels
+  {
+    const float* src = u->ctx32;
+    const size_t n = (size_t)B * Sk * 1024;
+    P.record([=] {
+      f32_to_f16_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream>>>(src, ctx16, n);
+      return check_launch(cc, "ctx_to_f16");
+    });
+  }
+  Act lat;
+  lat.N = B; lat.H = H; lat.W = W; lat.C = 64;
+  lat.p = P.act_alloc(lat.bytes());
+  {
+    const float* src = u->latent;
+    void* dst = lat.p;
+    P.record([=] {
+      const size_t n = (size_t)B * H * W * 64;
+      latent_in_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, cc->stream>>>(
+          src, static_cast<__half*>(dst), B, 4, H * W, 64);
+      return check_launch(cc, "latent_in");
+    });
+  }
+  // timestep embedding (fp32 weights, fp16-rounded values)
+  float* temb = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 1280));
+  float* thid = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 1280));
+  {
+    auto w1 = P.host_param("time_embedding.linear_1.weight", (size_t)1280 * 320, 0, 320, 1280);
+    Plan::round_f16(w1);
+    const float* W1 = P.upload_f32(w1);
+    const float* b1 = P.vec("time_embedding.linear_1.bias", 1280, 0, 320);
+    auto w2 = P.host_param("time_embedding.linear_2.weight", (size_t)1280 * 1280, 0, 1280, 1280);
+    Plan::round_f16(w2);
+    const float* W2 = P.upload_f32(w2);
+    const float* b2 = P.vec("time_embedding.linear_2.bias", 1280, 0, 1280);
+    const float* tv = u->tvals;
+    P.record([=] {
+      for (int b0 = 0; b0 < B; b0 += 8) {
+        const int nb = std::min(8, B - b0);
+        int r = tembed(cc, tv + b0, nb, W1, b1, W2, b2, 320, 1280, thid + (size_t)b0 * 1280, temb + (size_t)b0 * 1280);
+        if (r) return r;
+      }
+      return DI_OK;
+    });
+  }
+  const size_t tproj_at = P.ops.size();
+
+  // conv_in: 4 (padded to 64) -> 320
+  Act h;
+  {
+    const void* w = P.conv_weight("conv_in.weight", 320, 4, 64, 320);
+    const float* b = P.bias_padded("conv_in.bias", 320, 320, 36);
+    h = P.new_act(B, H, W, 320);
+    const Act x = lat;
+    const Act y = h;
+    P.record([=] { return gemm_conv3x3(cc, DI_F16, x.p, 64, nullptr, 0, B, H, W, 1, w, 320, b, nullptr, nullptr, 0,
+                                       y.p, 0, 320); });
+  }
+  const int ch[4] = {320, 640, 1280, 1280};
+  std::vector<Act> skips{h};
+  for (int i = 0; i < 4; ++i) {
+    const std::string pre = "down_blocks." + std::to_string(i);
+    for (int j = 0; j < 2; ++j) {
+      h = P.resnet(pre + ".resnets." + std::to_string(j), h, nullptr, ch[i]);
+      if (i < 3) h = P.transformer(pre + ".attentions." + std::to_string(j), h, ctx16, Sk, 1024);
+      skips.push_back(h);
+    }
+    if (i < 3) {
+      P.tmp_reset();
+      h = P.conv3x3(pre + ".downsamplers.0.conv", h, ch[i], 2);
+      skips.push_back(h);
+    }
+  }
+  h = P.resnet("mid_block.resnets.0", h, nullptr, 1280);
+  h = P.transformer("mid_block.attentions.0", h, ctx16, Sk, 1024);
+  h = P.resnet("mid_block.resnets.1", h, nullptr, 1280);
+  const int rch[4] = {1280, 1280, 640, 320};
+  for (int i = 0; i < 4; ++i) {
+    const std::string pre = "up_blocks." + std::to_string(i);
+    for (int j = 0; j < 3; ++j) {
+      Act s = skips.back();
+      skips.pop_back();
+      h = P.resnet(pre + ".resnets." + std::to_string(j), h, &s, rch[i]);
+      if (i > 0) h = P.transformer(pre + ".attentions." + std::to_string(j), h, ctx16, Sk, 1024);
+    }
+    if (i < 3) {
+      P.tmp_reset();
+      h = P.conv3x3(pre + ".upsamplers.0.conv", P.upsample(h), rch[i], 1);
+    }
+  }
+  // conv_norm_out + SiLU, conv_out 320 -> 4 (padded to 16)
+  P.tmp_reset();
+  void* a = P.gn("conv_norm_out", h, nullptr, 1e-5f, 1);
+  {
+    const void* w = P.conv_weight("conv_out.weight", 4, 320, 320, 16);
+    const float* b = P.bias_padded("conv_out.bias", 4, 16, 320 * 9);
+    void* y16 = P.act_alloc((size_t)B * H * W * 16 * 2);
+    P.record([=] { return gemm_conv3x3(cc, DI_F16, a, 320, nullptr, 0, B, H, W, 1, w, 16, b, nullptr, nullptr, 0, y16,
+                                       0, 16); });
+    float* out = u->out;
+    P.record([=] {
+      const size_t n = (size_t)B * 4 * H * W;
+      latent_out_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream>>>(
+          static_cast<const __half*>(y16), 16, out, B, 4, H * W);
+      return check_launch(cc, "latent_out");
+    });
+  }
+  P.finish_time_proj(tproj_at, temb, B);
+  cudaDeviceSynchronize();
+  return P.err;
+}
+
+// Config-1 ResNet block: fp32 NCHW in / out (fused-resnet.js drop-in, plus the timestep add).
+struct ResPlan {
+  Plan P;
+  int N = 1, C = 320, H = 64, W = 64, Tdim = 1280;
+  float* x = nullptr;      // [N,C,H,W]
+  float* temb = nullptr;   // [N,Tdim]
+  float* y = nullptr;      // [N,C,H,W]
+};
+
+static int build_resnet(ResPlan* r, float eps, int temb_silu) {
+  Plan& P = r->P;
+  const int N = r->N, C = r->C, H = r->H, W = r->W, HW = H * W, T = r->Tdim;
+  Ctx* cc = P.c;
+  r->x = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * C * HW));
+  r->temb = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * T));
+  r->y = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * C * HW));
+  float* xh = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * C * HW));   // NHWC fp32 copy of x
+  float* yh = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * C * HW));   // NHWC fp32 result
+  void* a = P.act_alloc((size_t)N * HW * C * 2);
+  void* hbuf = P.act_alloc((size_t)N * HW * C * 2);
+  void* part = P.act_alloc(gn_nhwc_ws_bytes(N, HW, 32));
+  float* tp = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * C));
+  if (P.err) return P.err;
+  auto up32 = [&](const std::string& nm, size_t n, int kind, int fan, int fan_out = 0) {
+    return P.upload_f32(P.host_param(nm, n, kind, fan, fan_out));
+  };
+  const float* G1 = up32("norm1.weight", C, 1, 1);
+  const float* Be1 = up32("norm1.bias", C, 2, 1);
+  const void* W1 = P.conv_weight("conv1.weight", C, C, C, C);
+  const float* B1 = up32("conv1.bias", C, 0, 9 * C);
+  const float* Wt = up32("time_emb_proj.weight", (size_t)C * T, 0, T, C);
+  const float* Bt = up32("time_emb_proj.bias", C, 0, T);
+  const float* G2 = up32("norm2.weight", C, 1, 1);
+  const float* Be2 = up32("norm2.bias", C, 2, 1);
+  const void* W2 = P.conv_weight("conv2.weight", C, C, C, C);
+  const float* B2 = up32("conv2.bias", C, 0, 9 * C);
+  const float* x = r->x;
+  const float* te = r->temb;
+  float* y = r->y;
+  P.record([=] { return nchw_to_nhwc(cc, DI_F32, DI_F32, x, xh, N, C, HW); });
+  P.record([=] { return group_norm_nhwc(cc, DI_F32, DI_F16, xh, C, nullptr, 0, N, HW, 32, eps, G1, Be1, 1, a, part); });
+  P.record([=] { return gemv(cc, te, N, T, Wt, 0, Bt, C, temb_silu, tp, C); });
+  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W1, C, B1, tp, nullptr, 0, hbuf, 0, C); });
+  P.record([=] { return group_norm_nhwc(cc, DI_F16, DI_F16, hbuf, C, nullptr, 0, N, HW, 32, eps, G2, Be2, 1, a, part); });
+  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W2, C, B2, nullptr, xh, 1, yh, 1, C); });
+  P.record([=] { return nhwc_to_nchw(cc, DI_F32, DI_F32, yh, y, N, C, HW); });
+  cudaDeviceSynchronize();
+  return P.err;
+}
+
+// Config-2 transformer block: token-major fp16 hidden [B,S,C] and context [B,Sk,Cctx].
+struct TBPlan {
+  Plan P;
+  int B = 2, S = 1024, C = 640, Sk = 77, Cctx = 1024;
+  void* hidden = nullptr;  // fp16 [B,S,C]
+  void* ctx = nullptr;     // fp16 [B,Sk,Cctx]
+  void* out = nullptr;     // fp16 [B,S,C]
+};
+
+static int build_tblock(TBPlan* t) {
+  Plan& P = t->P;
+  Act x;
+  x.N = t->B; x.H = t->S; x.W = 1; x.C = t->C;
+  x.p = P.act_alloc(x.bytes());
+  t->hidden = x.p;
+  t->ctx = P.act_alloc((size_t)t->B * t->Sk * t->Cctx * 2);
+  if (P.err) return P.err;
+  Act y = P.transformer("block", x, t->ctx, t->Sk, t->Cctx);
+  t->out = y.p;
+  cudaDeviceSynchronize();
+  return P.err;
+}
+
+}  // namespace di
+
+// ---------------------------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------------------------
+using namespace di;
+
+struct di_unet_s { UNetPlan u; };
+struct di_resnet_s { ResPlan r; };
+struct di_tblock_s { TBPlan t; };
+
+extern "C" {
+
+DI_API void di_synth_uniform(uint64_t seed, const char* name, size_t n, float bound, float* out) {
+  synth_uniform(seed, name, n, bound, out);
+}
+DI_API void di_synth_normal(uint64_t seed, const char* name, size_t n, float mean, float stdv, float* out) {
+  synth_normal(seed, name, n, mean, stdv, out);
+}
+
+DI_API int di_unet_create(di_ctx_t h, int B, int H, int W, int ctx_len, uint64_t seed, di_weight_fn fn, void* user,
+                          di_unet_t* out) {
+  Ctx* c = ctx_of(h);
+  if (!c || !out || B <= 0 || H <= 0 || W <= 0 || ctx_len <= 0 || (H % 8) || (W % 8))
+    return DI_EINVAL;
+  *out = nullptr;
+  auto* s = new di_unet_s();
+  s->u.B = B; s->u.H = H; s->u.W = W; s->u.Sk = ctx_len;
+  cudaSetDevice(c->device);
+  if (!s->u.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, unet_tmp_bytes(B, H, W))) {
+    delete s;
+    return set_error(c, DI_ENOMEM, "unet: init");
+  }
+  int r = build_unet(&s->u);
+  if (r) {
+    std::string m = s->u.P.errmsg;
+    delete s;
+    return set_error(c, r, "unet build: " + m);
+  }
+  *out = s;
+  return DI_OK;
+}
+
+DI_API int di_unet_io(di_unet_t u, float** latent, float** t, float** ctx, float** out) {
+  if (!u) return DI_EINVAL;
+  if (latent) *latent = u->u.latent;
+  if (t) *t = u->u.tvals;
+  if (ctx) *ctx = u->u.ctx32;
+  if (out) *out = u->u.out;
+  return DI_OK;
+}
+
+DI_API int di_unet_info(di_unet_t u, int* launches, size_t* weight_bytes, size_t* act_bytes) {
+  if (!u) return DI_EINVAL;
+  if (launches) *launches = u->u.P.launches;
+  if (weight_bytes) *weight_bytes = u->u.P.weight_bytes;
+  if (act_bytes) *act_bytes = u->u.P.act_bytes;
+  return DI_OK;
+}
+
+DI_API int di_unet_forward(di_unet_t u) {
+  if (!u) return DI_EINVAL;
+  return u->u.P.forward();
+}
+
+DI_API int di_unet_forward_host(di_unet_t u, const float* latent, const float* t, const float* ctx, float* out) {
+  if (!u || !latent || !t || !ctx || !out) return DI_EINVAL;
+  UNetPlan& p = u->u;
+  Ctx* c = p.P.c;
+  const size_t nl = (size_t)p.B * 4 * p.H * p.W, nc = (size_t)p.B * p.Sk * 1024;
+  cudaMemcpyAsync(p.latent, latent, nl * 4, cudaMemcpyHostToDevice, c->stream);
+  cudaMemcpyAsync(p.tvals, t, p.B * 4, cudaMemcpyHostToDevice, c->stream);
+  cudaMemcpyAsync(p.ctx32, ctx, nc * 4, cudaMemcpyHostToDevice, c->stream);
+  int r = p.P.forward();
+  if (r) return r;
+  cudaMemcpyAsync(out, p.out, nl * 4, cudaMemcpyDeviceToHost, c->stream);
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return set_error(c, DI_ECUDA, "unet forward_host sync");
+  return DI_OK;
+}
+
+DI_API void di_unet_destroy(di_unet_t u) { delete u; }
+
+DI_API int di_resnet_block_create(di_ctx_t h, int N, int C, int H, int W, int Tdim, uint64_t seed, float eps,
+                                  int temb_silu, di_weight_fn fn, void* user, di_resnet_t* out) {
+  Ctx* c = ctx_of(h);
+  if (!c || !out || N <= 0 || C % 64 || Tdim <= 0) return DI_EINVAL;
+  *out = nullptr;
+  auto* s = new di_resnet_s();
+  s->r.N = N; s->r.C = C; s->r.H = H; s->r.W = W; s->r.Tdim = Tdim;
+  if (!s->r.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, 1 << 20)) { delete s; return DI_ENOMEM; }
+  s->r.P.init_mode = 1;  // Kaiming-uniform weights
+  int r = build_resnet(&s->r, eps, temb_silu);
+  if (r) { std::string m = s->r.P.errmsg; delete s; return set_error(c, r, "resnet build: " + m); }
+  *out = s;
+  return DI_OK;
+}
+DI_API int di_resnet_block_io(di_resnet_t r, float** x, float** temb, float** y) {
+  if (!r) return DI_EINVAL;
+  if (x) *x = r->r.x;
+  if (temb) *temb = r->r.temb;
+  if (y) *y = r->r.y;
+  return DI_OK;
+}
+DI_API int di_resnet_block_run(di_resnet_t r) { return r ? r->r.P.forward() : DI_EINVAL; }
+DI_API void di_resnet_block_destroy(di_resnet_t r) { delete r; }
+
+DI_API int di_transformer_block_create(di_ctx_t h, int B, int S, int C, int Sk, int Cctx, uint64_t seed,
+                                       di_weight_fn fn, void* user, di_tblock_t* out) {
+  Ctx* c = ctx_of(h);
+  if (!c || !out || B <= 0 || S <= 0 || C % 64 || Cctx % 64 || Sk <= 0) return DI_EINVAL;
+  *out = nullptr;
+  auto* s = new di_tblock_s();
+  s->t.B = B; s->t.S = S; s->t.C = C; s->t.Sk = Sk; s->t.Cctx = Cctx;
+  const size_t M = (size_t)B * S;
+  if (!s->t.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, M * C * 2 * 27 + (size_t)B * Sk * 2 * C * 2 + (16 << 20))) {
+    delete s;
+    return DI_ENOMEM;
+  }
+  s->t.P.init_mode = 2;  // Xavier-uniform weights, zero biases
+  int r = build_tblock(&s->t);
+  if (r) { std::string m = s->t.P.errmsg; delete s; return set_error(c, r, "transformer build: " + m); }
+  *out = s;
+  return DI_OK;
+}
+DI_API int di_transformer_block_io(di_tblock_t t, void** hidden, void** ctx, void** out) {
+  if (!t) return DI_EINVAL;
+  if (hidden) *hidden = t->t.hidden;
+  if (ctx) *ctx = t->t.ctx;
+  if (out) *out = t->t.out;
+  return DI_OK;
+}
+DI_API int di_transformer_block_run(di_tblock_t t) { return t ? t->t.P.forward() : DI_EINVAL; }
+DI_API void di_transformer_block_destroy(di_tblock_t t) { delete t; }
+
+}  // extern "C"

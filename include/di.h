@@ -156,6 +156,54 @@ DI_API int di_attention(di_ctx_t ctx, int dtype, const void* Q, const void* K, c
 DI_API int di_tembed(di_ctx_t ctx, const float* t, int B, const float* W1, const float* b1, const float* W2,
               const float* b2, int Din, int Dh, float* y);
 
+/* ---------------------------------------------------------------------------------------------
+ * Planned fused blocks and the U-Net.  A plan is built once (weights drawn from the seeded generator
+ * or supplied per parameter name by `fn`, packed fp16; every buffer and launch fixed) and replayed as
+ * one CUDA graph.  Parameter names follow diffusers' UNet2DConditionModel ("down_blocks.0.resnets.0.
+ * conv1.weight", ...), values in the reference (PyTorch / ONNX) layouts; `fn` returns 0 when it filled
+ * dst with n floats, nonzero to fall back to the generator.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct di_unet_s* di_unet_t;
+typedef struct di_resnet_s* di_resnet_t;
+typedef struct di_tblock_s* di_tblock_t;
+typedef int (*di_weight_fn)(const char* name, size_t n, float* dst, void* user);
+
+/* The seeded parameter generator: key = mix64(seed*0x9E3779B97F4A7C15 + fnv1a64(name)),
+ * u_i = (mix64(key + (i+1)*0x9E3779B97F4A7C15) >> 40) * 2^-24; uniform = (2u-1)*bound (float);
+ * normal = Box-Muller (double) on (u_2j, u_2j+1).  Host-only; no GPU needed. */
+DI_API void di_synth_uniform(uint64_t seed, const char* name, size_t n, float bound, float* out);
+DI_API void di_synth_normal(uint64_t seed, const char* name, size_t n, float mean, float stdv, float* out);
+
+/* SD-Turbo (SD2.1) U-Net, fp16 weights / activations, fp32 accumulation: replaces unetForwardWGSL
+ * (unet-wgsl.js:145-195) and the Executor.run walk it drives (wgsl-executor.js:1248-1466).
+ * Latent [B,4,H,W] fp32 NCHW, t [B] fp32, context [B,ctx_len,1024] fp32, output [B,4,H,W] fp32. */
+DI_API int di_unet_create(di_ctx_t ctx, int B, int H, int W, int ctx_len, uint64_t seed, di_weight_fn fn, void* user,
+                          di_unet_t* out);
+DI_API int di_unet_io(di_unet_t u, float** latent, float** t, float** context, float** out); /* device buffers */
+DI_API int di_unet_info(di_unet_t u, int* launches, size_t* weight_bytes, size_t* act_bytes);
+DI_API int di_unet_forward(di_unet_t u);  /* enqueue one forward on the context stream (graph replay) */
+/* host buffers in, host buffer out, synchronous: the unetForwardWGSL(sample, timestep, cond) shape */
+DI_API int di_unet_forward_host(di_unet_t u, const float* latent, const float* t, const float* context, float* out);
+DI_API void di_unet_destroy(di_unet_t u);
+
+/* Config-1 ResNet block, fp32 NCHW in and out (fused-resnet.js:121-208 + the timestep add it omits,
+ * fused-resnet.js:9-12): y = conv2(silu(gn2(conv1(silu(gn1(x))) + Wt.act(temb) + bt))) + x;
+ * act = SiLU when temb_silu (diffusers), identity otherwise.  Names: norm1/conv1/time_emb_proj/norm2/conv2. */
+DI_API int di_resnet_block_create(di_ctx_t ctx, int N, int C, int H, int W, int Tdim, uint64_t seed, float eps,
+                                  int temb_silu, di_weight_fn fn, void* user, di_resnet_t* out);
+DI_API int di_resnet_block_io(di_resnet_t r, float** x, float** temb, float** y);
+DI_API int di_resnet_block_run(di_resnet_t r); /* runResNetBench's fused path (fused-resnet.js:340-350) */
+DI_API void di_resnet_block_destroy(di_resnet_t r);
+
+/* Config-2 SD2.1 transformer block (GN + proj_in, self-attn, cross-attn, GEGLU FF, proj_out + residual),
+ * fp16 token-major hidden [B,S,C] and context [B,Sk,Cctx]; parameter names prefixed "block."
+ * (runBlockBench's fused path, fused-block-full.js:456-686). */
+DI_API int di_transformer_block_create(di_ctx_t ctx, int B, int S, int C, int Sk, int Cctx, uint64_t seed,
+                                       di_weight_fn fn, void* user, di_tblock_t* out);
+DI_API int di_transformer_block_io(di_tblock_t t, void** hidden, void** context, void** out);
+DI_API int di_transformer_block_run(di_tblock_t t);
+DI_API void di_transformer_block_destroy(di_tblock_t t);
+
 #ifdef __cplusplus
 }
 #endif

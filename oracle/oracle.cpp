@@ -281,21 +281,39 @@ void sinusoid(float t, int dim, float* out) {
 // SD2.1-architecture U-Net (SD-Turbo), NCHW fp32, weights drawn from the seeded generator and
 // rounded through fp16 (the ONNX fp16 weights of the reference, converted by f16BytesToF32).
 // ------------------------------------------------------------------------------------------
+// Parameters by diffusers name.  kind 0 = uniform weight (fan_out > 0) or bias (fan_out == 0), 1 = norm
+// gamma ~ N(1, 0.02), 2 = norm beta ~ N(0, 0.02).  mode selects the uniform bound: 0 torch layer default
+// +-1/sqrt(fan_in) (weights and biases); 1 Kaiming-uniform weights +-sqrt(6/fan_in); 2 Xavier-uniform
+// weights +-sqrt(6/(fan_in+fan_out)) with zero biases.  Only the most recent tensors are kept alive (each
+// layer uses its parameters right after fetching them), which bounds host memory for the full U-Net.
 struct Params {
   uint64_t seed;
   bool fp16_round;
+  int mode = 0;
   std::vector<std::vector<float>> store;
-  const float* get(const std::string& name, size_t n, int kind, int fan_in) {
-    store.emplace_back(n);
-    float* p = store.back().data();
+  size_t next = 0;
+  const float* get(const std::string& name, size_t n, int kind, int fan_in, int fan_out = 0) {
+    if (store.size() < 64) store.emplace_back();
+    std::vector<float>& slot = store[next++ % 64];
+    slot.assign(n, 0.0f);
+    float* p = slot.data();
     const char* nm = name.c_str();
-    if (kind == 0) gen_uniform(seed, nm, n, 1.0f / std::sqrt((float)fan_in), p);  // weight / bias
-    else if (kind == 1) gen_normal(seed, nm, n, 1.0f, 0.02f, p);                   // norm gamma
-    else gen_normal(seed, nm, n, 0.0f, 0.02f, p);                                  // norm beta
-    if (fp16_round) for (size_t i = 0; i < n; ++i) p[i] = round_h(p[i]);
+    if (kind == 0) {
+      float bound = 1.0f / std::sqrt((float)fan_in);
+      if (mode == 1 && fan_out > 0) bound = std::sqrt(6.0f / (float)fan_in);
+      if (mode == 2) bound = fan_out > 0 ? std::sqrt(6.0f / (float)(fan_in + fan_out)) : 0.0f;
+      if (bound != 0.0f) gen_uniform(seed, nm, n, bound, p);
+    } else if (kind == 1) {
+      gen_normal(seed, nm, n, 1.0f, 0.02f, p);
+    } else {
+      gen_normal(seed, nm, n, 0.0f, 0.02f, p);
+    }
+    if (fp16_round) {
+#pragma omp parallel for schedule(static)
+      for (long long i = 0; i < (long long)n; ++i) p[i] = round_h(p[i]);
+    }
     return p;
   }
-  void release() { store.clear(); }
 };
 
 struct Tensor4 { int N, C, H, W; std::vector<float> d; size_t size() const { return (size_t)N * C * H * W; } };
@@ -304,7 +322,7 @@ Tensor4 t4(int N, int C, int H, int W) { Tensor4 t{N, C, H, W, {}}; t.d.assign((
 
 Tensor4 conv_p(Params& P, const std::string& pre, const Tensor4& x, int Co, int K, int S) {
   const int fan = x.C * K * K;
-  const float* w = P.get(pre + ".weight", (size_t)Co * fan, 0, fan);
+  const float* w = P.get(pre + ".weight", (size_t)Co * fan, 0, fan, Co * K * K);
   const float* b = P.get(pre + ".bias", Co, 0, fan);
   const int pad = K / 2;
   Tensor4 y = t4(x.N, Co, (x.H + 2 * pad - K) / S + 1, (x.W + 2 * pad - K) / S + 1);
@@ -327,7 +345,7 @@ Tensor4 resnet(Params& P, const std::string& pre, const Tensor4& x, const std::v
   h = conv_p(P, pre + ".conv1", h, Co, 3, 1);
   {
     const int TD = (int)(temb_silu.size() / x.N);
-    const float* w = P.get(pre + ".time_emb_proj.weight", (size_t)Co * TD, 0, TD);
+    const float* w = P.get(pre + ".time_emb_proj.weight", (size_t)Co * TD, 0, TD, Co);
     const float* b = P.get(pre + ".time_emb_proj.bias", Co, 0, TD);
     std::vector<float> tp((size_t)x.N * Co);
     linear(temb_silu.data(), w, b, tp.data(), x.N, Co, TD);
@@ -349,7 +367,7 @@ Tensor4 resnet(Params& P, const std::string& pre, const Tensor4& x, const std::v
 
 std::vector<float> linear_p(Params& P, const std::string& pre, const std::vector<float>& x, int M, int K,
                             int N, bool bias) {
-  const float* w = P.get(pre + ".weight", (size_t)N * K, 0, K);
+  const float* w = P.get(pre + ".weight", (size_t)N * K, 0, K, N);
   const float* b = bias ? P.get(pre + ".bias", N, 0, K) : nullptr;
   std::vector<float> y((size_t)M * N);
   linear(x.data(), w, b, y.data(), M, N, K);
@@ -713,7 +731,7 @@ void o_resnet_block(const float* x, const float* temb, int N, int C, int H, int 
 // hidden [B,S,C] in and out; weights by name from the seeded generator (fp16-rounded when asked).
 void o_transformer_block(const float* hidden, const float* ctx, int B, int S, int C, int Sk, int Cctx,
                          uint64_t seed, int fp16_weights, float* out) {
-  Params P{seed, fp16_weights != 0, {}};
+  Params P{seed, fp16_weights != 0, 2, {}, 0};  // Xavier-uniform weights, zero biases (config 2)
   Tensor4 x = t4(B, C, S, 1);
   for (int b = 0; b < B; ++b)
     for (int s = 0; s < S; ++s)
@@ -730,7 +748,7 @@ void o_transformer_block(const float* hidden, const float* ctx, int B, int S, in
 // ctx [B,Sk,1024]; out [B,4,H,W].
 void o_unet_forward(const float* latent, const float* tvals, const float* ctx, int B, int H, int W, int Sk,
                     uint64_t seed, float* out) {
-  Params P{seed, true, {}};
+  Params P{seed, true, 0, {}, 0};
   const int ch[4] = {320, 640, 1280, 1280};
   const int Cctx = 1024;
   std::vector<float> cv(ctx, ctx + (size_t)B * Sk * Cctx);

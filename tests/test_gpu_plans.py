@@ -1,0 +1,95 @@
+"""End-to-end parity of the planned blocks and the U-Net (2 and 4) against the CPU
+oracle, with weights drawn from the same seeded generator on both sides.
+
+Bars (north star): max|Δ|/max|ref| <= 1e-2 per block; cosine >= 0.999 on the U-Net noise prediction."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import cosine, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _np(t):
+    return t.float().cpu().numpy()
+
+
+def test_resnet_block_config1(ctx, dib, oracle):
+    """Config 1: [1,320,64,64] fp32, GN(32, 1e-5), Kaiming-uniform weights, seed 0."""
+    import importlib
+    import torch
+    blocks = importlib.import_module("draw_instant_b200.blocks")
+    N, C, H, W, T, seed = 1, 320, 64, 64, 1280, 0
+    blk = blocks.ResNetBlock(ctx, N, C, H, W, T, seed=seed)
+    x = oracle.gen_normal(seed, "x", N * C * H * W).reshape(N, C, H, W)
+    temb = oracle.gen_normal(seed, "temb", N * T).reshape(N, T)
+    kb = lambda fan: np.sqrt(6.0 / fan)  # Kaiming-uniform weight bound
+    db = lambda fan: 1.0 / np.sqrt(fan)  # torch default bias bound
+    w = dict(
+        g1=oracle.gen_normal(seed, "norm1.weight", C, 1.0, 0.02), be1=oracle.gen_normal(seed, "norm1.bias", C, 0.0, 0.02),
+        w1=oracle.gen_uniform(seed, "conv1.weight", C * C * 9, kb(9 * C)), bb1=oracle.gen_uniform(seed, "conv1.bias", C, db(9 * C)),
+        wt=oracle.gen_uniform(seed, "time_emb_proj.weight", C * T, kb(T)), bt=oracle.gen_uniform(seed, "time_emb_proj.bias", C, db(T)),
+        g2=oracle.gen_normal(seed, "norm2.weight", C, 1.0, 0.02), be2=oracle.gen_normal(seed, "norm2.bias", C, 0.0, 0.02),
+        w2=oracle.gen_uniform(seed, "conv2.weight", C * C * 9, kb(9 * C)), bb2=oracle.gen_uniform(seed, "conv2.bias", C, db(9 * C)))
+    ref = oracle.resnet_block(x, temb, **w)
+    y = blk(torch.from_numpy(x).cuda(), torch.from_numpy(temb).cuda())
+    torch.cuda.synchronize()
+    got = _np(y)
+    assert rel_err(got, ref) < 1e-2
+    assert cosine(got, ref) > 0.9999
+    # a second run on the replayed graph gives the same bits
+    y2 = blk(torch.from_numpy(x).cuda(), torch.from_numpy(temb).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(_np(y2), got)
+
+
+def test_transformer_block_config2(ctx, dib, oracle):
+    """Config 2: hidden [2,1024,640], context [2,77,1024], 10 heads x 64, GEGLU 640->5120, Xavier, seed 1."""
+    import importlib
+    import torch
+    blocks = importlib.import_module("draw_instant_b200.blocks")
+    B, S, C, Sk, Cc, seed = 2, 1024, 640, 77, 1024, 1
+    blk = blocks.TransformerBlock(ctx, B, S, C, Sk, Cc, seed=seed)
+    hid = oracle.gen_normal(seed, "hidden", B * S * C).reshape(B, S, C)
+    cx = oracle.gen_normal(seed, "context", B * Sk * Cc).reshape(B, Sk, Cc)
+    hid16 = hid.astype(np.float16)
+    cx16 = cx.astype(np.float16)
+    out = blk(torch.from_numpy(hid16).cuda(), torch.from_numpy(cx16).cuda())
+    torch.cuda.synchronize()
+    ref = oracle.transformer_block(hid16.astype(np.float32), cx16.astype(np.float32), seed, True)
+    got = _np(out)
+    assert rel_err(got, ref) < 1e-2
+    assert cosine(got, ref) > 0.9999
+
+
+@pytest.mark.parametrize("B,H,W", [(1, 8, 8), (2, 16, 16)])
+def test_unet_config4_small(ctx, dib, oracle, B, H, W):
+    """Config 4 architecture at small latents (the reference's own U-Net check runs an 8x8 latent,
+    unet-wgsl-test.html:84-208): cosine >= 0.999 and max-rel-err <= 1e-2 on the noise prediction."""
+    import importlib
+    unet = importlib.import_module("draw_instant_b200.unet")
+    seed = 3
+    u = unet.UNet(ctx, B=B, H=H, W=W, seed=seed)
+    lat = oracle.gen_normal(seed, "latent", B * 4 * H * W).reshape(B, 4, H, W)
+    cx = oracle.gen_normal(seed, "context", B * 77 * 1024).reshape(B, 77, 1024)
+    got = u.forward_host(lat, 999.0, cx)
+    ref = oracle.unet_forward(lat, 999.0, cx.astype(np.float16).astype(np.float32), seed)
+    assert np.all(np.isfinite(got))
+    assert cosine(got, ref) >= 0.999
+    assert rel_err(got, ref) <= 1e-2
+    assert ctx.fault() == 0
+
+
+def test_unet_full_size_properties(ctx, dib, oracle):
+    """Config 4 at its full 64x64 latent: finite, deterministic across graph replays, batch-consistent."""
+    import importlib
+    unet = importlib.import_module("draw_instant_b200.unet")
+    u = unet.UNet(ctx, B=1, H=64, W=64, seed=3)
+    lat = oracle.gen_normal(3, "latent", 4 * 64 * 64).reshape(1, 4, 64, 64)
+    cx = oracle.gen_normal(3, "context", 77 * 1024).reshape(1, 77, 1024)
+    a = u.forward_host(lat, 999.0, cx)
+    b = u.forward_host(lat, 999.0, cx)
+    assert np.all(np.isfinite(a)) and np.array_equal(a, b)
+    assert u.launches > 100
