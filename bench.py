@@ -1,0 +1,405 @@
+#!/usr/bin/env python3
+"""bench.py — SD-Turbo 512² U-Net steps/s on N B200s, one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+
+Under torchrun (N > 1) every rank owns one GPU and one full U-Net replica (weak scaling: batch B per GPU,
+the latent batch sharded across GPUs); the only collective is an NCCL all-gather of the predicted latents
+at the end of the job.  A "step" is one U-Net forward over the GPU's batch.  K steps are timed on the
+device with CUDA events between barrier + synchronize pairs; the job time is the max over ranks.
+
+Reported besides the headline value:
+  e2e           the same metric through the public host call (di_unet_forward_host: pinned host inputs
+                copied in, forward, output copied out, every step)
+  roofline      the tensor-core GEMM / implicit-GEMM conv kernel (the dominant kernel): algorithmic FLOPs
+                over its device time inside the step (profiling-graph replay), against the measured
+                sustained tensor peak
+  cpu_baseline  the CPU oracle (C++/OpenMP restatement of the reference's math) on a bounded sample
+  blocks        per-block ms vs roofline for BASELINE configs 1-3 (rank 0, N = 1 only)
+  clocks        nvidia-smi samples taken during the timed region
+
+--impl reference times the reference path's CPU implementation (the oracle port; the reference itself is
+JavaScript/WGSL needing a WebGPU adapter, unavailable on this box) on the same metric and config.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SD-Turbo 512² U-Net steps/s at 1/2/4/8 B200; per-block ms vs roofline"
+WORKLOAD = ("config 4: SD-Turbo (SD2.1) U-Net single denoising step, 64x64 latent (512x512 image), t=999, "
+            "context 77x1024")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes per launch of the dominant kernel from the committed ncu capture
+# (profiles/gemm_tc_kernel_unet_conv.md); None until that capture exists.
+GEMM_TRAFFIC = None
+
+
+def load_package():
+    name = "draw_instant_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg_dir = ROOT / "draw-instant_b200"
+    spec = importlib.util.spec_from_file_location(name, pkg_dir / "__init__.py",
+                                                  submodule_search_locations=[str(pkg_dir)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region (reads only; changes nothing)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = Path(f"/tmp/di_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = [[x.strip() for x in r.split(",")] for r in self.path.read_text().strip().splitlines() if r.strip()]
+        rows = [r for r in rows if len(r) >= 9]
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        loaded = [s for s in sm if s > 0.5 * max(sm)] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def synth(dib, seed, name, n):
+    a = np.empty(n, np.float32)
+    dib.lib().di_synth_normal(seed, name.encode(), n, 0.0, 1.0, a.ctypes.data)
+    return a
+
+
+def _oracle_step(oracle, h, seed=3):
+    lat = oracle.gen_normal(seed, "latent", 4 * h * h).reshape(1, 4, h, h)
+    cx = oracle.gen_normal(seed, "context", 77 * 1024).reshape(1, 77, 1024)
+    oracle.unet_forward(lat, 999.0, cx, seed)  # draws and caches the weights
+    p0 = oracle.param_seconds()
+    t0 = time.perf_counter()
+    oracle.unet_forward(lat, 999.0, cx, seed)
+    return time.perf_counter() - t0 - (oracle.param_seconds() - p0), lat, cx
+
+
+def cpu_baseline(unet_mod, budget_s=25.0):
+    """CPU oracle U-Net (weights cached, generation excluded) on a bounded sample -> steps/s of the 64x64 step."""
+    import oracle
+    oracle.build()
+    t16, _, _ = _oracle_step(oracle, 16)
+    f64 = unet_mod.unet_flops(1, 64, 64)
+    proj = t16 * f64 / unet_mod.unet_flops(1, 16, 16)
+    h = 64 if proj <= budget_s else (32 if proj / 4 <= budget_s else 16)
+    t = t16 if h == 16 else _oracle_step(oracle, h)[0]
+    scale = f64 / unet_mod.unet_flops(1, h, h)
+    sample = (f"one CPU-oracle U-Net forward at a {h}x{h} latent (batch 1), {t:.2f} s"
+              + ("" if h == 64 else f", scaled x{scale:.2f} by algorithmic FLOPs to the 64x64 step"))
+    oracle.clear_cache()
+    return 1.0 / (t * scale), sample, oracle.num_threads()
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the CPU restatement of the reference's path (oracle port), rank 0 only."""
+    if rank != 0:
+        return
+    import oracle
+    oracle.build()
+    load_package()
+    unet_mod = importlib.import_module("draw_instant_b200.unet")
+    seed = 3
+    t16, _, cx = _oracle_step(oracle, 16, seed)
+    budget = 180.0 / max(1, args.steps + args.warmup)  # whole run within ~3 minutes
+    h = 16
+    for cand in (64, 32):
+        if t16 * unet_mod.unet_flops(1, cand, cand) / unet_mod.unet_flops(1, 16, 16) <= budget:
+            h = cand
+            break
+    lat = oracle.gen_normal(seed, "latent", 4 * h * h).reshape(1, 4, h, h)
+    for _ in range(args.warmup):
+        oracle.unet_forward(lat, 999.0, cx, seed)
+    p0 = oracle.param_seconds()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.unet_forward(lat, 999.0, cx, seed)
+    dt = time.perf_counter() - t0 - (oracle.param_seconds() - p0)
+    scale = unet_mod.unet_flops(1, 64, 64) / unet_mod.unet_flops(1, h, h)
+    per_step = dt / args.steps * scale
+    value = 1.0 / per_step
+    sample = (f"CPU oracle (C++/OpenMP restatement of the reference WGSL math) U-Net forward at a {h}x{h} latent per "
+              f"step" + ("" if h == 64 else f", scaled x{scale:.2f} by algorithmic FLOPs to the 64x64 step"))
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": {"workload": WORKLOAD, "global_batch": 1, "latent": [1, 4, 64, 64], "parallelism": "cpu",
+                       "reference_runtime": "unavailable on this box: the reference path is WGSL on WebGPU "
+                                            "(Deno/wgpu lavapipe); no JS runtime and no graphics stack here"},
+            "cpu_baseline": {"value": value, "unit": "steps/s", "cores": oracle.num_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    oracle.clear_cache()
+    print(json.dumps(line), flush=True)
+
+
+def time_events(fn, iters, stream):
+    import torch
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(iters):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def block_results(dib, ctx, pk, peak_src):
+    """Per-block ms vs roofline for BASELINE configs 1-3 (N = 1)."""
+    import torch
+    blocks = importlib.import_module("draw_instant_b200.blocks")
+    out = {}
+    tpeak = pk["bf16_tflops"] * 1e12
+    hbm = pk["hbm_gbs"] * 1e9
+    st = torch.cuda.current_stream()
+    r = blocks.ResNetBlock(ctx, 1, 320, 64, 64, 1280, seed=0)
+    r.x.copy_(torch.from_numpy(synth(dib, 0, "x", 320 * 64 * 64).reshape(1, 320, 64, 64)).cuda())
+    r.temb.copy_(torch.from_numpy(synth(dib, 0, "temb", 1280).reshape(1, 1280)).cuda())
+    for _ in range(5):
+        r.run()
+    ms = time_events(r.run, 50, st)
+    fl = 2 * 2.0 * 4096 * 320 * 320 * 9
+    out["resnet_cfg1"] = {"ms": ms, "tflops": fl / ms / 1e9, "frac": fl / ms * 1e3 / tpeak, "flops": fl,
+                          "bound": "tensor", "dtype": "fp32 io, fp16 tensor-core operands"}
+    del r
+    t = blocks.TransformerBlock(ctx, 2, 1024, 640, 77, 1024, seed=1)
+    t.hidden.copy_(torch.from_numpy(synth(dib, 1, "hidden", 2 * 1024 * 640).reshape(2, 1024, 640)).cuda().half())
+    t.context.copy_(torch.from_numpy(synth(dib, 1, "context", 2 * 77 * 1024).reshape(2, 77, 1024)).cuda().half())
+    for _ in range(5):
+        t.run()
+    ms = time_events(t.run, 50, st)
+    M, C = 2048, 640
+    fl = (2.0 * M * C * C * 8 + 2.0 * M * 12 * C * C + 2 * 2.0 * 77 * 2 * C * 1024 + 4.0 * 2 * C * 1024 * 1024 +
+          4.0 * 2 * C * 1024 * 77)
+    out["transformer_cfg2"] = {"ms": ms, "tflops": fl / ms / 1e9, "frac": fl / ms * 1e3 / tpeak, "flops": fl,
+                               "bound": "tensor", "dtype": "fp16"}
+    del t
+    L = dib.lib()
+    g = torch.Generator(device="cuda").manual_seed(2)
+    mk = lambda *s: (torch.randn(*s, device="cuda", generator=g) / 8).bfloat16()
+    q, k, v = mk(8, 5, 4096, 64), mk(8, 5, 4096, 64), mk(8, 5, 4096, 64)
+    kc, vc = mk(8, 5, 77, 64), mk(8, 5, 77, 64)
+    o = torch.empty_like(q)
+
+    def self_attn():
+        ctx.check(L.di_attention(ctx.h, 2, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 8, 5, 4096, 4096, 1))
+
+    def cross_attn():
+        ctx.check(L.di_attention(ctx.h, 2, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), 8, 5, 4096, 77, 1))
+
+    for _ in range(5):
+        self_attn()
+    ms = time_events(self_attn, 30, st)
+    fl = 4.0 * 8 * 5 * 4096 * 4096 * 64
+    out["flash_self_cfg3"] = {"ms": ms, "tflops": fl / ms / 1e9, "frac": fl / ms * 1e3 / tpeak, "flops": fl,
+                              "bound": "tensor", "dtype": "bf16"}
+    for _ in range(5):
+        cross_attn()
+    ms = time_events(cross_attn, 50, st)
+    by = 2.0 * (2 * 8 * 5 * 4096 * 64 + 2 * 8 * 5 * 77 * 64)
+    out["flash_cross_cfg3"] = {"ms": ms, "gbs": by / ms / 1e6, "frac": by / ms * 1e3 / hbm, "bytes": by,
+                               "bound": "hbm", "dtype": "bf16"}
+    out["peak_source"] = f"{peak_src} (burst peaks: blocks are timed alone)"
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=1, help="latents per GPU")
+    ap.add_argument("--no-extras", action="store_true", help="skip e2e, roofline, blocks, cpu baseline")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dib = load_package()
+    unet_mod = importlib.import_module("draw_instant_b200.unet")
+    ctx = dib.Context(local)
+    B = args.batch
+    u = unet_mod.UNet(ctx, B=B, H=64, W=64, seed=3)
+    lat = synth(dib, 3 + rank, "latent", B * 4 * 64 * 64).reshape(B, 4, 64, 64)
+    cx = synth(dib, 3 + rank, "context", B * 77 * 1024).reshape(B, 77, 1024)
+    u.latent.copy_(torch.from_numpy(lat).cuda())
+    u.t.fill_(999.0)
+    u.context.copy_(torch.from_numpy(cx).cuda())
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        u.forward()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            u.forward()
+        if world > 1:  # the job's one collective: gather every replica's predicted latents (NCCL / NVLink)
+            gathered = [torch.empty_like(u.out) for _ in range(world)]
+            dist.all_gather(gathered, u.out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    value = world * args.steps / (ms_total / 1e3)
+    ms_step = ms_total / args.steps
+    step_flops = unet_mod.unet_flops(B, 64, 64)
+    line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic: seeded N(0,1) latent and context, seeded random-init SD2.1 U-Net weights",
+            "config": {"workload": WORKLOAD, "global_batch": B * world, "batch_per_gpu": B, "latent": [B, 4, 64, 64],
+                       "parallelism": f"replicas x{world} (batch sharded, NCCL all-gather of outputs)",
+                       "l2": "inputs larger than L2: 1.73 GB of fp16 weights streamed per step",
+                       "step_gflop": step_flops / 1e9, "step_tflops": step_flops / (ms_step / 1e3) / 1e12},
+            "clocks": sampler.summary(), "gpu_launches": int(u.launches * args.steps), "device_fault": ctx.fault()}
+
+    if not args.no_extras:
+        # e2e through the public host call (pinned host buffers; H2D + forward + D2H every step)
+        h_lat = torch.from_numpy(lat).pin_memory()
+        h_ctx = torch.from_numpy(cx).pin_memory()
+        h_t = torch.full((B,), 999.0).pin_memory()
+        h_out = torch.empty((B, 4, 64, 64)).pin_memory()
+        L = dib.lib()
+
+        def host_step():
+            ctx.check(L.di_unet_forward_host(u.h, h_lat.data_ptr(), h_t.data_ptr(), h_ctx.data_ptr(),
+                                             h_out.data_ptr()), "di_unet_forward_host")
+
+        for _ in range(3):
+            host_step()
+        e2e_steps = max(10, min(args.steps, 200))
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            host_step()
+        te = torch.tensor([time.perf_counter() - t0], device="cuda")
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        line["e2e"] = {"value": world * e2e_steps / float(te.item()), "unit": "steps/s",
+                       "h2d_bytes_per_step": int(h_lat.numel() * 4 + B * 4 + h_ctx.numel() * 4),
+                       "d2h_bytes_per_step": int(h_out.numel() * 4)}
+
+        ops = u.ops()
+        op_ms = u.profile(reps=10)
+        kinds = ops["kind"]
+        gemm = kinds == 0
+        gemm_flops = float(ops["flops"][gemm].sum())
+        gemm_ms = float(op_ms[gemm].sum())
+        n_gemm = int(ops["kernels"][gemm].sum())
+        pk, src = peaks()
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+        names = ["gemm", "attention", "norm", "other"]
+        line["roofline"] = {
+            "bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 implicit-GEMM conv3x3 + linear)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak if achieved else None,
+            "peak_source": f"{src} bf16_tflops_sustained (fp16 runs at the bf16 tensor rate; timed inside the step)",
+            "traffic": GEMM_TRAFFIC, "launches_per_step": n_gemm,
+            "flops_per_launch": gemm_flops / max(1, n_gemm), "ms_per_launch": gemm_ms / max(1, n_gemm),
+            "share_of_profiled_step": gemm_ms / max(1e-9, float(op_ms.sum())),
+            "profiled_step_ms": float(op_ms.sum()),
+            "time_by_kind_ms": {names[int(k)]: float(op_ms[kinds == k].sum()) for k in np.unique(kinds)}}
+        if rank == 0 and world == 1:
+            line["blocks"] = block_results(dib, ctx, pk, src)
+            try:
+                v, sample, cores = cpu_baseline(unet_mod)
+                line["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": cores, "kind": "port",
+                                        "sample": sample}
+            except Exception as e:  # a reported figure; never fail the bench line on it
+                line["cpu_baseline"] = {"value": None, "unit": "steps/s", "cores": None, "kind": "port",
+                                        "sample": f"failed: {e}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

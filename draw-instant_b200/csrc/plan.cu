@@ -176,6 +176,8 @@ struct Plan {
 
   ~Plan() {
     if (gexec) cudaGraphExecDestroy(gexec);
+    if (pexec) cudaGraphExecDestroy(pexec);
+    for (auto& e : pev) cudaEventDestroy(e);
     if (stream) { cudaStreamSynchronize(stream); cudaStreamDestroy(stream); }
     if (ev_in) cudaEventDestroy(ev_in);
     if (ev_out) cudaEventDestroy(ev_out);
@@ -259,9 +261,69 @@ struct Plan {
     return upload_f32(h);
   }
 
-  void record(std::function<int()> f) {
+  // Per-op metadata: kind (0 tensor-core GEMM / conv, 1 attention, 2 normalisation, 3 other),
+  // algorithmic FLOPs and HBM bytes, and how many kernels the op launches.
+  struct OpInfo { int kind; double flops, bytes; int kernels; };
+  std::vector<OpInfo> info;
+
+  void record(std::function<int()> f, int kind = 3, double flops = 0, double bytes = 0, int kernels = 1) {
     ops.push_back(std::move(f));
-    ++launches;
+    info.push_back({kind, flops, bytes, kernels});
+    launches += kernels;
+  }
+
+  // LOG.profile analogue (wgsl-executor.js:1380-1390): a second graph with an event-record node between
+  // every op, replayed `reps` times; op_ms[i] = mean device time of op i.
+  cudaGraphExec_t pexec = nullptr;
+  std::vector<cudaEvent_t> pev;
+  int profile(int reps, float* op_ms) {
+    if (err) return err;
+    if (!gexec) {
+      int r = forward();
+      if (r) return r;
+      cudaStreamSynchronize(stream);
+    }
+    cudaStream_t saved = c->stream;
+    c->stream = stream;
+    if (!pexec) {
+      pev.resize(ops.size() + 1);
+      for (auto& e : pev) cudaEventCreate(&e);
+      cudaGraph_t g = nullptr;
+      if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        c->stream = saved;
+        return set_error(c, DI_ECUDA, "profile: capture");
+      }
+      int r = DI_OK;
+      // External records become event-record nodes of the captured graph (plain records inside a
+      // capture only express dependencies).
+      cudaEventRecordWithFlags(pev[0], stream, cudaEventRecordExternal);
+      for (size_t i = 0; i < ops.size() && r == DI_OK; ++i) {
+        r = ops[i]();
+        cudaEventRecordWithFlags(pev[i + 1], stream, cudaEventRecordExternal);
+      }
+      cudaError_t e = cudaStreamEndCapture(stream, &g);
+      if (r != DI_OK || e != cudaSuccess || cudaGraphInstantiate(&pexec, g, 0) != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        c->stream = saved;
+        cudaGetLastError();
+        return set_error(c, DI_ECUDA, "profile: graph");
+      }
+      cudaGraphDestroy(g);
+    }
+    std::vector<double> acc(ops.size(), 0.0);
+    for (int rep = 0; rep < reps; ++rep) {
+      cudaGraphLaunch(pexec, stream);
+      cudaStreamSynchronize(stream);
+      for (size_t i = 0; i < ops.size(); ++i) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, pev[i], pev[i + 1]);
+        acc[i] += ms;
+      }
+    }
+    c->stream = saved;
+    if (cudaGetLastError() != cudaSuccess) return set_error(c, DI_ECUDA, "profile: replay");
+    for (size_t i = 0; i < ops.size(); ++i) op_ms[i] = (float)(acc[i] / std::max(1, reps));
+    return DI_OK;
   }
 
   int run_ops() {
@@ -362,7 +424,8 @@ struct Plan {
     const void* p2 = x2 ? x2->p : nullptr;
     const int C2 = x2 ? x2->C : 0;
     record([=] { return gemm_conv3x3(cc, DI_F16, xx.p, xx.C, p2, C2, xx.N, xx.H, xx.W, stride, w, Co, b, nullptr,
-                                     nullptr, 0, y.p, 0, Co); });
+                                     nullptr, 0, y.p, 0, Co); },
+           0, 2.0 * y.N * y.H * y.W * Co * 9 * Ci, (double)x.bytes() + 18.0 * Co * Ci + (double)y.bytes());
     return y;
   }
 
@@ -375,7 +438,7 @@ struct Plan {
       upsample2_kernel<<<(int)std::min<size_t>((total + 255) / 256, 16 * cc->num_sms), 256, 0, cc->stream>>>(
           static_cast<const uint4*>(xx.p), static_cast<uint4*>(y.p), xx.N, xx.H, xx.W, xx.C / 8);
       return check_launch(cc, "upsample2");
-    });
+    }, 3, 0, 5.0 * x.bytes());
     return y;
   }
 
@@ -391,7 +454,8 @@ struct Plan {
     const void* p2 = x2 ? x2->p : nullptr;
     const int C2 = x2 ? x2->C : 0;
     record([=] { return group_norm_nhwc(cc, DI_F16, DI_F16, a.p, a.C, p2, C2, a.N, HW, 32, eps, g, b, silu, y,
-                                        part); });
+                                        part); },
+           2, 0, 3.0 * x1.N * HW * C * 2, 2);
     return y;
   }
 
@@ -402,7 +466,8 @@ struct Plan {
   void linear(const void* X, int M, int K, const void* W, int N, const float* b, const void* R, void* Y,
               const void* X2 = nullptr, int K1 = 0) {
     Ctx* cc = c;
-    record([=] { return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1); });
+    record([=] { return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1); },
+           0, 2.0 * M * N * K, 2.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1)));
   }
 
   // ResnetBlock2D on concat(x1, x2): gn1+silu -> conv1 (+b1 +time proj) -> gn2+silu -> conv2 (+b2 + shortcut).
@@ -436,7 +501,8 @@ struct Plan {
     const int N = x1.N, H = x1.H, W = x1.W;
     Plan* self = this;
     record([=] { return gemm_conv3x3(cc, DI_F16, a, Ci, nullptr, 0, N, H, W, 1, w1, Co, b1,
-                                     self->temb_all + toff, nullptr, 0, h.p, 0, self->tproj_ld); });
+                                     self->temb_all + toff, nullptr, 0, h.p, 0, self->tproj_ld); },
+           0, 2.0 * N * H * W * Co * 9 * Ci, 2.0 * ((double)N * H * W * (Ci + Co) + 9.0 * Co * Ci));
     void* a2 = gn(pre + ".norm2", h, nullptr, 1e-5f, 1);
     const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
     const float* b2 = bias_padded(pre + ".conv2.bias", Co, Co, Co * 9);
@@ -450,7 +516,8 @@ struct Plan {
     }
     Act y = new_act(N, H, W, Co);
     record([=] { return gemm_conv3x3(cc, DI_F16, a2, Co, nullptr, 0, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0,
-                                     Co); });
+                                     Co); },
+           0, 2.0 * N * H * W * Co * 9 * Co, 2.0 * ((double)N * H * W * 3 * Co + 9.0 * Co * Co));
     return y;
   }
 
@@ -469,7 +536,7 @@ struct Plan {
     const float* g1 = vec(tb + ".norm1.weight", C, 1, 1);
     const float* be1 = vec(tb + ".norm1.bias", C, 2, 1);
     void* n1 = tmp((size_t)M * C * 2);
-    record([=] { return layer_norm(cc, DI_F16, DI_F16, h0, g1, be1, n1, M, C, 1e-5f); });
+    record([=] { return layer_norm(cc, DI_F16, DI_F16, h0, g1, be1, n1, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
     std::vector<float> wqkv;
     for (const char* nm : {".attn1.to_q.weight", ".attn1.to_k.weight", ".attn1.to_v.weight"}) {
       auto w = host_param(tb + nm, (size_t)C * C, 0, C, C);
@@ -483,7 +550,7 @@ struct Plan {
       const char* base = static_cast<const char*>(qkv);
       return attention(cc, DI_F16, base, base + (size_t)C * 2, base + (size_t)2 * C * 2, o1, N, heads, HW, HW, 0,
                        3 * C, 3 * C, 3 * C, C);
-    });
+    }, 1, 4.0 * N * heads * HW * (double)HW * 64, 2.0 * 4 * M * C);
     const void* wo1 = lin_weight(tb + ".attn1.to_out.0.weight", C, C);
     const float* bo1 = vec(tb + ".attn1.to_out.0.bias", C, 0, C);
     void* h1 = tmp((size_t)M * C * 2);
@@ -492,7 +559,7 @@ struct Plan {
     const float* g2 = vec(tb + ".norm2.weight", C, 1, 1);
     const float* be2 = vec(tb + ".norm2.bias", C, 2, 1);
     void* n2 = tmp((size_t)M * C * 2);
-    record([=] { return layer_norm(cc, DI_F16, DI_F16, h1, g2, be2, n2, M, C, 1e-5f); });
+    record([=] { return layer_norm(cc, DI_F16, DI_F16, h1, g2, be2, n2, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
     const void* wq2 = lin_weight(tb + ".attn2.to_q.weight", C, C);
     void* q2 = tmp((size_t)M * C * 2);
     linear(n2, M, C, wq2, C, nullptr, nullptr, q2);
@@ -508,7 +575,7 @@ struct Plan {
     record([=] {
       const char* base = static_cast<const char*>(kv);
       return attention(cc, DI_F16, q2, base, base + (size_t)C * 2, o2, N, heads, HW, Sk, 0, C, 2 * C, 2 * C, C);
-    });
+    }, 1, 4.0 * N * heads * HW * (double)Sk * 64, 2.0 * (2.0 * M * C + 2.0 * N * Sk * C));
     const void* wo2 = lin_weight(tb + ".attn2.to_out.0.weight", C, C);
     const float* bo2 = vec(tb + ".attn2.to_out.0.bias", C, 0, C);
     void* h2 = tmp((size_t)M * C * 2);
@@ -517,7 +584,7 @@ struct Plan {
     const float* g3 = vec(tb + ".norm3.weight", C, 1, 1);
     const float* be3 = vec(tb + ".norm3.bias", C, 2, 1);
     void* n3 = tmp((size_t)M * C * 2);
-    record([=] { return layer_norm(cc, DI_F16, DI_F16, h2, g3, be3, n3, M, C, 1e-5f); });
+    record([=] { return layer_norm(cc, DI_F16, DI_F16, h2, g3, be3, n3, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
     const int F = 4 * C;
     auto wff = host_param(tb + ".ff.net.0.proj.weight", (size_t)2 * F * C, 0, C, 2 * F);
     auto bff = host_param(tb + ".ff.net.0.proj.bias", (size_t)2 * F, 0, C);
@@ -535,7 +602,8 @@ struct Plan {
     const float* Bff = upload_f32(bp);
     void* g = tmp((size_t)M * F * 2);
     record([=] { return gemm_linear(cc, DI_F16, n3, C, nullptr, M, C, Wff, 2 * F, Bff, nullptr, 0, g, 0, 1, nullptr,
-                                    1); });
+                                    1); },
+           0, 2.0 * M * 2 * F * C, 2.0 * ((double)M * C + 2.0 * F * C + (double)M * F));
     const void* wf2 = lin_weight(tb + ".ff.net.2.weight", C, F);
     const float* bf2 = vec(tb + ".ff.net.2.bias", C, 0, F);
     void* h3 = tmp((size_t)M * C * 2);
@@ -558,6 +626,7 @@ struct Plan {
     Ctx* cc = c;
     const int rows = tproj_rows;
     float* out = temb_all;
+    info.insert(info.begin() + at, OpInfo{3, 2.0 * B * rows * 1280, 2.0 * rows * 1280, (B + 7) / 8});
     ops.insert(ops.begin() + at, [=] {
       for (int b0 = 0; b0 < B; b0 += 8) {
         const int nb = std::min(8, B - b0);
@@ -566,7 +635,7 @@ struct Plan {
       }
       return DI_OK;
     });
-    ++launches;
+    launches += (B + 7) / 8;
     tproj_w.clear();
     tproj_w.shrink_to_fit();
   }
@@ -608,7 +677,7 @@ static int build_unet(UNetPlan* u) {
     P.record([=] {
       f32_to_f16_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream>>>(src, ctx16, n);
       return check_launch(cc, "ctx_to_f16");
-    });
+    }, 3, 0, 6.0 * n);
   }
   Act lat;
   lat.N = B; lat.H = H; lat.W = W; lat.C = 64;
@@ -621,7 +690,7 @@ static int build_unet(UNetPlan* u) {
       latent_in_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, cc->stream>>>(
           src, static_cast<__half*>(dst), B, 4, H * W, 64);
       return check_launch(cc, "latent_in");
-    });
+    }, 3, 0, (double)B * H * W * (16 + 128));
   }
   // timestep embedding (fp32 weights, fp16-rounded values)
   float* temb = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 1280));
@@ -643,7 +712,7 @@ static int build_unet(UNetPlan* u) {
         if (r) return r;
       }
       return DI_OK;
-    });
+    }, 3, 2.0 * B * 1280 * (320 + 1280), 4.0 * 1280 * (320 + 1280), 2 * ((B + 7) / 8));
   }
   const size_t tproj_at = P.ops.size();
 
@@ -656,7 +725,8 @@ static int build_unet(UNetPlan* u) {
     const Act x = lat;
     const Act y = h;
     P.record([=] { return gemm_conv3x3(cc, DI_F16, x.p, 64, nullptr, 0, B, H, W, 1, w, 320, b, nullptr, nullptr, 0,
-                                       y.p, 0, 320); });
+                                       y.p, 0, 320); },
+             0, 2.0 * B * H * W * 320 * 9 * 4, (double)B * H * W * (128 + 640));
   }
   const int ch[4] = {320, 640, 1280, 1280};
   std::vector<Act> skips{h};
@@ -698,14 +768,15 @@ static int build_unet(UNetPlan* u) {
     const float* b = P.bias_padded("conv_out.bias", 4, 16, 320 * 9);
     void* y16 = P.act_alloc((size_t)B * H * W * 16 * 2);
     P.record([=] { return gemm_conv3x3(cc, DI_F16, a, 320, nullptr, 0, B, H, W, 1, w, 16, b, nullptr, nullptr, 0, y16,
-                                       0, 16); });
+                                       0, 16); },
+             0, 2.0 * B * H * W * 4 * 9 * 320, (double)B * H * W * (640 + 32));
     float* out = u->out;
     P.record([=] {
       const size_t n = (size_t)B * 4 * H * W;
       latent_out_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream>>>(
           static_cast<const __half*>(y16), 16, out, B, 4, H * W);
       return check_launch(cc, "latent_out");
-    });
+    }, 3, 0, (double)B * H * W * (32 + 16));
   }
   P.finish_time_proj(tproj_at, temb, B);
   cudaDeviceSynchronize();
@@ -751,13 +822,19 @@ static int build_resnet(ResPlan* r, float eps, int temb_silu) {
   const float* x = r->x;
   const float* te = r->temb;
   float* y = r->y;
-  P.record([=] { return nchw_to_nhwc(cc, DI_F32, DI_F32, x, xh, N, C, HW); });
-  P.record([=] { return group_norm_nhwc(cc, DI_F32, DI_F16, xh, C, nullptr, 0, N, HW, 32, eps, G1, Be1, 1, a, part); });
-  P.record([=] { return gemv(cc, te, N, T, Wt, 0, Bt, C, temb_silu, tp, C); });
-  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W1, C, B1, tp, nullptr, 0, hbuf, 0, C); });
-  P.record([=] { return group_norm_nhwc(cc, DI_F16, DI_F16, hbuf, C, nullptr, 0, N, HW, 32, eps, G2, Be2, 1, a, part); });
-  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W2, C, B2, nullptr, xh, 1, yh, 1, C); });
-  P.record([=] { return nhwc_to_nchw(cc, DI_F32, DI_F32, yh, y, N, C, HW); });
+  const double act = (double)N * HW * C;
+  const double conv_flops = 2.0 * act * C * 9;
+  P.record([=] { return nchw_to_nhwc(cc, DI_F32, DI_F32, x, xh, N, C, HW); }, 3, 0, 8.0 * act);
+  P.record([=] { return group_norm_nhwc(cc, DI_F32, DI_F16, xh, C, nullptr, 0, N, HW, 32, eps, G1, Be1, 1, a, part); },
+           2, 0, 10.0 * act, 2);
+  P.record([=] { return gemv(cc, te, N, T, Wt, 0, Bt, C, temb_silu, tp, C); }, 3, 2.0 * N * C * T, 4.0 * C * T);
+  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W1, C, B1, tp, nullptr, 0, hbuf, 0, C); },
+           0, conv_flops, 4.0 * act + 18.0 * C * C);
+  P.record([=] { return group_norm_nhwc(cc, DI_F16, DI_F16, hbuf, C, nullptr, 0, N, HW, 32, eps, G2, Be2, 1, a, part); },
+           2, 0, 6.0 * act, 2);
+  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W2, C, B2, nullptr, xh, 1, yh, 1, C); },
+           0, conv_flops, 10.0 * act + 18.0 * C * C);
+  P.record([=] { return nhwc_to_nchw(cc, DI_F32, DI_F32, yh, y, N, C, HW); }, 3, 0, 8.0 * act);
   cudaDeviceSynchronize();
   return P.err;
 }
@@ -843,6 +920,24 @@ DI_API int di_unet_info(di_unet_t u, int* launches, size_t* weight_bytes, size_t
   if (weight_bytes) *weight_bytes = u->u.P.weight_bytes;
   if (act_bytes) *act_bytes = u->u.P.act_bytes;
   return DI_OK;
+}
+
+DI_API int di_unet_ops(di_unet_t u, int* n_ops, int* kinds, double* flops, double* bytes, int* kernels) {
+  if (!u || !n_ops) return DI_EINVAL;
+  const auto& I = u->u.P.info;
+  *n_ops = (int)I.size();
+  for (size_t i = 0; i < I.size(); ++i) {
+    if (kinds) kinds[i] = I[i].kind;
+    if (flops) flops[i] = I[i].flops;
+    if (bytes) bytes[i] = I[i].bytes;
+    if (kernels) kernels[i] = I[i].kernels;
+  }
+  return DI_OK;
+}
+
+DI_API int di_unet_profile(di_unet_t u, int reps, float* op_ms) {
+  if (!u || !op_ms || reps <= 0) return DI_EINVAL;
+  return u->u.P.profile(reps, op_ms);
 }
 
 DI_API int di_unet_forward(di_unet_t u) {

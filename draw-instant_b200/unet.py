@@ -55,6 +55,25 @@ class UNet:
         lib().di_unet_info(self.h, ctypes.byref(n), ctypes.byref(wb), ctypes.byref(ab))
         self.launches, self.weight_bytes, self.act_bytes = n.value, wb.value, ab.value
 
+    def ops(self):
+        """Per-op metadata: dict of numpy arrays kind / flops / bytes / kernels (one entry per recorded op)."""
+        n = ctypes.c_int()
+        lib().di_unet_ops(self.h, ctypes.byref(n), None, None, None, None)
+        k = np.zeros(n.value, np.int32)
+        f = np.zeros(n.value, np.float64)
+        b = np.zeros(n.value, np.float64)
+        kn = np.zeros(n.value, np.int32)
+        self.ctx.check(lib().di_unet_ops(self.h, ctypes.byref(n), k.ctypes.data, f.ctypes.data, b.ctypes.data,
+                                         kn.ctypes.data), "di_unet_ops")
+        return {"kind": k, "flops": f, "bytes": b, "kernels": kn}
+
+    def profile(self, reps: int = 10) -> np.ndarray:
+        """Mean device ms of every op (a profiling graph with an event-record node between ops)."""
+        n = len(self.ops()["kind"])
+        ms = np.zeros(n, np.float32)
+        self.ctx.check(lib().di_unet_profile(self.h, reps, ms.ctypes.data), "di_unet_profile")
+        return ms
+
     def forward(self) -> None:
         """Enqueue one forward on the context stream (reads self.latent / t / context, writes self.out)."""
         self.ctx.check(lib().di_unet_forward(self.h), "di_unet_forward")
@@ -87,6 +106,48 @@ class UNet:
             self.close()
         except Exception:
             pass
+
+
+def unet_flops(B: int = 1, H: int = 64, W: int = 64, Sk: int = 77) -> float:
+    """Algorithmic FLOPs (2 per MAC) of one SD2.1 U-Net forward: convs, linears, attention QK^T and PV."""
+    f = 2.0 * B * H * W * 320 * 9 * 4 + 2.0 * B * H * W * 4 * 9 * 320 + 2.0 * B * 1280 * (320 + 1280)
+
+    def res(ci, co, h, w):
+        x = 2.0 * B * h * w * co * 9 * (ci + co) + 2.0 * B * co * 1280
+        return x + (2.0 * B * h * w * co * ci if ci != co else 0.0)
+
+    def tr(c, h, w):
+        m, hw = B * h * w, h * w
+        lin = 2.0 * m * c * c * (1 + 3 + 1 + 1 + 1 + 1) + 2.0 * m * 8 * c * c + 2.0 * m * 4 * c * c
+        return lin + 2.0 * B * Sk * 2 * c * 1024 + 4.0 * B * c * hw * hw + 4.0 * B * c * hw * Sk
+
+    ch = [320, 640, 1280, 1280]
+    h, w, c = H, W, 320
+    skips = [320]
+    for i in range(4):
+        for _ in range(2):
+            f += res(c, ch[i], h, w)
+            c = ch[i]
+            if i < 3:
+                f += tr(c, h, w)
+            skips.append(c)
+        if i < 3:
+            f += 2.0 * B * (h // 2) * (w // 2) * c * 9 * c
+            h, w = h // 2, w // 2
+            skips.append(c)
+    f += res(1280, 1280, h, w) * 2 + tr(1280, h, w)
+    rch = [1280, 1280, 640, 320]
+    for i in range(4):
+        for _ in range(3):
+            s = skips.pop()
+            f += res(c + s, rch[i], h, w)
+            c = rch[i]
+            if i > 0:
+                f += tr(c, h, w)
+        if i < 3:
+            h, w = h * 2, w * 2
+            f += 2.0 * B * h * w * c * 9 * c
+    return f
 
 
 _plans = {}

@@ -181,6 +181,12 @@ DI_API int di_unet_create(di_ctx_t ctx, int B, int H, int W, int ctx_len, uint64
                           di_unet_t* out);
 DI_API int di_unet_io(di_unet_t u, float** latent, float** t, float** context, float** out); /* device buffers */
 DI_API int di_unet_info(di_unet_t u, int* launches, size_t* weight_bytes, size_t* act_bytes);
+/* Per-op metadata of the plan (kind 0 GEMM/conv, 1 attention, 2 norm, 3 other; algorithmic FLOPs and HBM
+ * bytes; kernels launched).  Arrays may be NULL; call with NULLs first to get n_ops. */
+DI_API int di_unet_ops(di_unet_t u, int* n_ops, int* kinds, double* flops, double* bytes, int* kernels);
+/* LOG.profile analogue (wgsl-executor.js:1380-1390): replays a graph with an event between every op
+ * `reps` times and writes each op's mean device time (ms) to op_ms[n_ops]. */
+DI_API int di_unet_profile(di_unet_t u, int reps, float* op_ms);
 DI_API int di_unet_forward(di_unet_t u);  /* enqueue one forward on the context stream (graph replay) */
 /* host buffers in, host buffer out, synchronous: the unetForwardWGSL(sample, timestep, cond) shape */
 DI_API int di_unet_forward_host(di_unet_t u, const float* latent, const float* t, const float* context, float* out);

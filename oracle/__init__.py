@@ -55,7 +55,10 @@ _SIGS = {
     "o_transformer_block": [_f, _f, _I, _I, _I, _I, _I, _U64, _I, _f],
     "o_unet_forward": [_f, _f, _f, _I, _I, _I, _I, _U64, _f],
     "o_num_threads": [],
+    "o_param_seconds": [],
+    "o_clear_cache": [],
 }
+_RES = {"o_num_threads": ctypes.c_int, "o_param_seconds": ctypes.c_double}
 
 
 def build() -> Path:
@@ -75,7 +78,7 @@ def lib() -> ctypes.CDLL:
         for n, a in _SIGS.items():
             fn = getattr(L, n)
             fn.argtypes = a
-            fn.restype = ctypes.c_int if n == "o_num_threads" else None
+            fn.restype = _RES.get(n)
         _lib = L
     return _lib
 
@@ -297,3 +300,12 @@ def unet_forward(latent, t, ctx, seed):
 
 def num_threads() -> int:
     return lib().o_num_threads()
+
+
+def param_seconds() -> float:
+    """Cumulative seconds spent drawing parameters (the U-Net keeps them cached per seed)."""
+    return lib().o_param_seconds()
+
+
+def clear_cache() -> None:
+    lib().o_clear_cache()

@@ -19,6 +19,8 @@
 #include <vector>
 #include <string>
 #include <algorithm>
+#include <chrono>
+#include <unordered_map>
 
 #ifdef _OPENMP
 #include <omp.h>
@@ -286,15 +288,29 @@ void sinusoid(float t, int dim, float* out) {
 // +-1/sqrt(fan_in) (weights and biases); 1 Kaiming-uniform weights +-sqrt(6/fan_in); 2 Xavier-uniform
 // weights +-sqrt(6/(fan_in+fan_out)) with zero biases.  Only the most recent tensors are kept alive (each
 // layer uses its parameters right after fetching them), which bounds host memory for the full U-Net.
+double g_param_seconds = 0.0;  // time spent drawing parameters (excluded from CPU-baseline timings)
+
 struct Params {
   uint64_t seed;
   bool fp16_round;
   int mode = 0;
   std::vector<std::vector<float>> store;
   size_t next = 0;
+  std::unordered_map<std::string, std::vector<float>>* cache = nullptr;  // keep every tensor (repeat runs)
   const float* get(const std::string& name, size_t n, int kind, int fan_in, int fan_out = 0) {
-    if (store.size() < 64) store.emplace_back();
-    std::vector<float>& slot = store[next++ % 64];
+    if (cache) {
+      auto it = cache->find(name);
+      if (it != cache->end() && it->second.size() == n) return it->second.data();
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    std::vector<float>* slotp;
+    if (cache) {
+      slotp = &(*cache)[name];
+    } else {
+      if (store.size() < 64) store.emplace_back();
+      slotp = &store[next++ % 64];
+    }
+    std::vector<float>& slot = *slotp;
     slot.assign(n, 0.0f);
     float* p = slot.data();
     const char* nm = name.c_str();
@@ -312,9 +328,12 @@ struct Params {
 #pragma omp parallel for schedule(static)
       for (long long i = 0; i < (long long)n; ++i) p[i] = round_h(p[i]);
     }
+    g_param_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     return p;
   }
 };
+
+std::unordered_map<uint64_t, std::unordered_map<std::string, std::vector<float>>> g_unet_cache;
 
 struct Tensor4 { int N, C, H, W; std::vector<float> d; size_t size() const { return (size_t)N * C * H * W; } };
 
@@ -748,7 +767,7 @@ void o_transformer_block(const float* hidden, const float* ctx, int B, int S, in
 // ctx [B,Sk,1024]; out [B,4,H,W].
 void o_unet_forward(const float* latent, const float* tvals, const float* ctx, int B, int H, int W, int Sk,
                     uint64_t seed, float* out) {
-  Params P{seed, true, 0, {}, 0};
+  Params P{seed, true, 0, {}, 0, &g_unet_cache[seed]};
   const int ch[4] = {320, 640, 1280, 1280};
   const int Cctx = 1024;
   std::vector<float> cv(ctx, ctx + (size_t)B * Sk * Cctx);
@@ -797,6 +816,9 @@ void o_unet_forward(const float* latent, const float* tvals, const float* ctx, i
   h = conv_p(P, "conv_out", h, 4, 3, 1);
   std::memcpy(out, h.d.data(), sizeof(float) * h.size());
 }
+
+double o_param_seconds() { return g_param_seconds; }
+void o_clear_cache() { g_unet_cache.clear(); }
 
 int o_num_threads() {
 #ifdef _OPENMP
