@@ -70,6 +70,7 @@ SIGNATURES = {
     "di_slice": (_I, [_P, _P, _P, _P]),
     "di_concat_copy": (_I, [_P, _P, _P, _P]),
     "di_group_norm_nhwc": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _F, _P, _P, _I, _P]),
+    "di_group_norm_nhwc_noalloc": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _F, _P, _P, _I, _P]),
     "di_linear": (_I, [_P, _I, _P, _I, _P, _I, _I, _P, _I, _P, _P, _P]),
     "di_linear_geglu": (_I, [_P, _I, _P, _I, _I, _P, _I, _P, _P]),
     "di_conv3x3_nhwc": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P]),

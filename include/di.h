@@ -126,6 +126,19 @@ DI_API int di_concat_copy(di_ctx_t ctx, const float* X, float* Y, const uint32_t
 DI_API int di_group_norm_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW,
                        int G, float eps, const float* gamma, const float* beta, int fuse_silu, void* y);
 
+/* Same as di_group_norm_nhwc, but it allocates no device memory, for callers that cannot let a library
+ * call cudaMalloc (a fixed, pre-reserved memory budget, an external allocator that owns the device
+ * memory, or latency-critical code that must not take allocation locks).  No counterpart in the
+ * reference.  Its scratch is a fixed 1 MiB array inside the library (kept on every GPU that loads the
+ * library until the process exits): sizes needing more than N * min(64, max(1, HW/64)) * G * 8 =
+ * 1 MiB are rejected with DI_EINVAL.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.  All calls share the one
+ * array: calls that may overlap on the GPU (different streams or contexts on the same device) race and
+ * must be serialised by the caller. */
+DI_API int di_group_norm_nhwc_noalloc(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N,
+                                      int HW, int G, float eps, const float* gamma, const float* beta, int fuse_silu,
+                                      void* y);
+
 /* Linear / 1x1 conv: Y[M,N] = X[M,K] . W[N,K]^T (+ bias[N]) (+ R[M,N]); X = concat(X1[M,K1], X2[M,K-K1])
  * along K when X2 != NULL (skip-connection concat without a copy).  K, K1 multiples of 64, N multiple of 16.
  * Replaces the Gemm/MatMul epilogue variants of fused-block-full.js:128-186. */
