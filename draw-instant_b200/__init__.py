@@ -84,6 +84,7 @@ SIGNATURES = {
     "di_unet_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
     "di_unet_ops": (_I, [_P, ctypes.POINTER(_I), _P, _P, _P, _P]),
     "di_unet_profile": (_I, [_P, _I, _P]),
+    "di_unet_profile_kind": (_I, [_P, _I, _I, ctypes.POINTER(_F)]),
     "di_unet_forward": (_I, [_P]),
     "di_unet_forward_host": (_I, [_P, _P, _P, _P, _P]),
     "di_unet_destroy": (None, [_P]),

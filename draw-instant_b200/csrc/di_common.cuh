@@ -33,7 +33,7 @@ struct Ctx {
   std::string last_error;
   int sticky = 0;                // sticky fault (device lost / kernel error), like unet-wgsl.js _gpuError
   int num_sms = 148;
-  struct Scratch { void* ptr = nullptr; size_t bytes = 0; } ws[4];  // library-owned workspace slots
+  struct Scratch { void* ptr = nullptr; size_t bytes = 0; } ws[6];  // library-owned workspace slots
 };
 
 Ctx* ctx_of(di_ctx_t h);

@@ -49,6 +49,8 @@ struct GemmParams {
   int ldo, out_f32;
   int geglu;
   int vec_ok;  // 16-byte aligned rows for out / residual: vectorised epilogue
+  int splits;      // K splits (grid.z); > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
+  float* partial;  // [splits][M][N] fp32 when splits > 1
   int* err;
 };
 
@@ -139,6 +141,8 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int kper = (p.num_k + p.splits - 1) / p.splits;
+  const int kb0 = blockIdx.z * kper, kb1 = min(p.num_k, kb0 + kper);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -159,9 +163,9 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
       tma_prefetch_desc(&p.tmB);
       int img = 0, y0 = 0;
       if (p.mode != 0) { img = m0 / p.HWo; y0 = (m0 % p.HWo) / p.Wo; }
-      for (int kb = 0; kb < p.num_k; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
+      for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
         if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1, p.err, DEVERR_WAIT_TMA)) { *abort_flag = 1; break; }
         mbar_arrive_expect_tx(&full[s], STAGE_TX);
         uint8_t* dA = sA + s * S::A_BYTES;
@@ -187,9 +191,9 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_f16(BM, BN, BF16);
-      for (int kb = 0; kb < p.num_k; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
+      for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
         if (*abort_flag || !mbar_wait(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t a0 = smem_u32(sA + s * S::A_BYTES), b0 = smem_u32(sB + s * S::B_BYTES);
@@ -197,7 +201,7 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
         for (int k = 0; k < BK / 16; ++k) {
           const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(b0 + k * 32, 16, 1024);
-          umma_f16(tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_f16(tmem, ad, bd, idesc, (it | k) != 0 ? 1u : 0u);
         }
         umma_commit(&empty[s]);
       }
@@ -211,7 +215,26 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
     const bool ok = mbar_wait(accum, 0, p.err, DEVERR_WAIT_EPI);
     tc_fence_after();
     const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    if (!p.geglu) {
+    if (p.splits > 1) {
+      // split-K: raw fp32 partial sums; splitk_reduce adds the splits and applies the epilogue
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + c * 32, r);
+        tmem_wait_ld();
+        const int nb = n0 + c * 32;
+        if (!ok || m >= p.M || nb >= p.N) continue;
+        float* dst = p.partial + ((size_t)blockIdx.z * p.M + m) * p.N + nb;
+        if (nb + 32 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            reinterpret_cast<float4*>(dst)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        } else {
+          for (int j = 0; j < 32 && nb + j < p.N; ++j) dst[j] = __uint_as_float(r[j]);
+        }
+      }
+    } else if (!p.geglu) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -291,16 +314,86 @@ int launch_variant(Ctx* c, const GemmParams& p) {
     attr_done |= 1u << (c->device & 31);
   }
   const int n_tiles = p.geglu ? (p.N / BN) : (p.N + BN - 1) / BN;
-  dim3 grid(n_tiles, (p.M + BM - 1) / BM);
+  dim3 grid(n_tiles, (p.M + BM - 1) / BM, p.splits);
   kern<<<grid, 192, S::TOTAL, c->stream>>>(p);
   return check_launch(c, "gemm_tc_kernel");
 }
 
+// Sums the split-K partials and applies the epilogue (bias, per-image row vector, residual or GEGLU).
+__global__ void splitk_reduce(const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
+                              const float* __restrict__ rowvec, int rowvec_div, int rowvec_ld, const void* residual,
+                              int ldr, int res_f32, void* out, int ldo, int out_f32, int geglu, int bf16) {
+  const size_t slice = (size_t)M * N;
+  const int NO = geglu ? N / 2 : N;
+  const size_t total = (size_t)M * NO;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int m = i / NO, o = i % NO;
+    if (!geglu) {
+      float v = 0.f;
+      for (int z = 0; z < splits; ++z) v += part[z * slice + (size_t)m * N + o];
+      if (bias) v += bias[o];
+      if (rowvec) v += rowvec[(size_t)(m / rowvec_div) * rowvec_ld + o];
+      if (residual) v += load_one(residual, (size_t)m * ldr + o, res_f32, bf16);
+      store_one(out, (size_t)m * ldo + o, v, out_f32, bf16);
+    } else {
+      const int nv = (o / 64) * 128 + (o % 64), ng = nv + 64;
+      float a = 0.f, g = 0.f;
+      for (int z = 0; z < splits; ++z) {
+        a += part[z * slice + (size_t)m * N + nv];
+        g += part[z * slice + (size_t)m * N + ng];
+      }
+      if (bias) { a += bias[nv]; g += bias[ng]; }
+      store_one(out, (size_t)m * ldo + o, a * gelu_erf(g), out_f32, bf16);
+    }
+  }
+}
+
 }  // namespace
 
+// Tiling: N tile (64 / 128) and K splits.  Large grids: 128-wide tiles.  Few tiles with a long K on a
+// small M (the low-resolution levels at batch 1, where the weights stream from HBM once per step):
+// 128-wide tiles split along K so that about two CTAs per SM stream disjoint weight slices.  Few tiles
+// with a short K: 64-wide tiles for more CTAs.
+void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits) {
+  const long long tiles128 = (long long)((N + 127) / 128) * ((M + 127) / 128);
+  *splits = 1;
+  if (geglu || tiles128 >= c->num_sms) { *bn = 128; }
+  else if (M <= 512 && num_k >= 16) {
+    *bn = 128;
+    int s = (int)std::min<long long>(num_k / 4, (2LL * c->num_sms + tiles128 - 1) / tiles128);
+    s = std::max(1, s);
+    const int per = (num_k + s - 1) / s;
+    *splits = (num_k + per - 1) / per;
+  } else {
+    *bn = (N % 64 == 0) ? 64 : 128;
+  }
+  if (geglu && M <= 512 && num_k >= 16 && tiles128 < c->num_sms) {
+    int s = (int)std::min<long long>(num_k / 4, (2LL * c->num_sms + tiles128 - 1) / tiles128);
+    s = std::max(1, s);
+    const int per = (num_k + s - 1) / s;
+    *splits = (num_k + per - 1) / per;
+  }
+}
+
 // Chooses the N tile: 128 by default; 64 when the grid would leave most SMs idle.
-int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int force_bn = 0) {
+int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int force_bn, int splits, void* splitk_ws) {
   p.err = c->d_err;
+  p.splits = std::max(1, splits);
+  if (p.splits > 1) {
+    const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
+    p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
+    if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
+    const int bnv = force_bn;
+    int r = bnv == 64 ? (bf16 ? launch_variant<64, 4, true>(c, p) : launch_variant<64, 4, false>(c, p))
+                      : (bf16 ? launch_variant<128, 3, true>(c, p) : launch_variant<128, 3, false>(c, p));
+    if (r) return r;
+    const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
+    splitk_reduce<<<blocks, 256, 0, c->stream>>>(p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,
+                                                 p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32,
+                                                 p.geglu, bf16);
+    return check_launch(c, "splitk_reduce");
+  }
   int bn = force_bn;
   if (!bn) {
     if (p.geglu) bn = 128;
@@ -363,13 +456,14 @@ static GemmParams base_params() {
   GemmParams p;
   memset(&p, 0, sizeof(p));
   p.rowvec_div = 1;
+  p.splits = 1;
   return p;
 }
 
 // Public building blocks used by the fused blocks and the U-Net plan ---------------------------
 int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
                 const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
-                int rowvec_div) {
+                int rowvec_div, void* splitk_ws) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 64 || (X2 && (K1 <= 0 || K1 % 64 || K1 >= K)))
     return set_error(c, DI_EINVAL, "linear: K and K1 must be multiples of 64");
   if (geglu && (N % 128)) return set_error(c, DI_EINVAL, "linear_geglu: F must be a multiple of 64");
@@ -402,18 +496,16 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
   p.out_f32 = out_f32;
   p.geglu = geglu;
   p.vec_ok = vec_rows_ok(Y, p.ldo, out_f32 ? 4 : 2) && (!R || vec_rows_ok(R, N, res_f32 ? 4 : 2));
-  int chosen = bn;
-  if (!chosen) {
-    const long long tiles128 = (long long)((N + 127) / 128) * ((M + 127) / 128);
-    chosen = (tiles128 < c->num_sms && N % 64 == 0) ? 64 : 128;
-  }
+  (void)bn;
+  int chosen, splits;
+  choose_tiling(c, M, N, p.num_k, geglu, &chosen, &splits);
   if (!tmap_kmajor(&p.tmB, dtype, W, N, K, K, chosen, &err)) return set_error(c, DI_EINVAL, err);
-  return launch_gemm(c, p, dtype == DI_BF16, chosen);
+  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, splitk_ws);
 }
 
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
-                 void* y, int out_f32, int temb_ld) {
+                 void* y, int out_f32, int temb_ld, void* splitk_ws) {
   if (C1 <= 0 || C1 % 64 || (x2 && (C2 <= 0 || C2 % 64)) || Co % 16 || (stride != 1 && stride != 2))
     return set_error(c, DI_EINVAL, "conv3x3: channels must be multiples of 64 (Co of 16), stride 1 or 2");
   if (stride == 2 && (x2 || (H % 2) || (W % 2)))
@@ -457,10 +549,10 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
   p.ldo = Co;
   p.out_f32 = out_f32;
   p.vec_ok = vec_rows_ok(y, Co, out_f32 ? 4 : 2) && (!residual || vec_rows_ok(residual, Co, res_f32 ? 4 : 2));
-  const long long tiles128 = (long long)((Co + 127) / 128) * ((p.M + 127) / 128);
-  const int chosen = (tiles128 < c->num_sms && Co % 64 == 0) ? 64 : 128;
+  int chosen, splits;
+  choose_tiling(c, p.M, Co, p.num_k, 0, &chosen, &splits);
   if (!tmap_kmajor(&p.tmB, dtype, Wt, Co, 9 * Cin, 9 * Cin, chosen, &err)) return set_error(c, DI_EINVAL, err);
-  return launch_gemm(c, p, dtype == DI_BF16, chosen);
+  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, splitk_ws);
 }
 
 // Weight repack: [Co][Ci][3][3] fp32 -> [Co][3][3][Ci] fp16/bf16.
@@ -492,14 +584,14 @@ int di_linear(di_ctx_t h, int dtype, const void* X1, int K1, const void* X2, int
               const float* bias, const void* R, void* Y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
-  return gemm_linear(c, dtype, X1, K1, X2, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1);
+  return gemm_linear(c, dtype, X1, K1, X2, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1, nullptr);
 }
 
 int di_linear_geglu(di_ctx_t h, int dtype, const void* X, int M, int K, const void* W, int F, const float* bias,
                     void* Y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16) || F % 64) return DI_EINVAL;
-  return gemm_linear(c, dtype, X, K, nullptr, M, K, W, 2 * F, bias, nullptr, 0, Y, 0, 1, nullptr, 1);
+  return gemm_linear(c, dtype, X, K, nullptr, M, K, W, 2 * F, bias, nullptr, 0, Y, 0, 1, nullptr, 1, nullptr);
 }
 
 int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,
@@ -507,7 +599,7 @@ int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x
                     void* y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
-  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0, Co);
+  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr);
 }
 
 int di_pack_conv3x3(di_ctx_t h, int dtype, const float* w, int Co, int Ci, void* out) {

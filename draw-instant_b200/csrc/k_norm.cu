@@ -74,11 +74,21 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
     for (int j = 0; j < 8; ++j) { s[j] = 0.f; q[j] = 0.f; }
     const int c = v * 8;
     const int p0 = chunk * chunk_pixels, p1 = min(HW, p0 + chunk_pixels);
-    for (int p = p0 + r; p < p1; p += R) {
-      const size_t pix = (size_t)n * HW + p;
+    const T* base = c < C1 ? x1 + (size_t)n * HW * C1 + c : x2 + (size_t)n * HW * C2 + (c - C1);
+    const size_t ld = c < C1 ? C1 : C2;
+    int p = p0 + r;
+    for (; p + 3 * R < p1; p += 4 * R) {  // four independent loads in flight per thread
+      float f[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) load8<T>(base + (size_t)(p + u * R) * ld, f[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { s[j] += f[u][j]; q[j] += f[u][j] * f[u][j]; }
+    }
+    for (; p < p1; p += R) {
       float f[8];
-      if (c < C1) load8<T>(x1 + pix * C1 + c, f);
-      else load8<T>(x2 + pix * C2 + (c - C1), f);
+      load8<T>(base + (size_t)p * ld, f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) { s[j] += f[j]; q[j] += f[j] * f[j]; }
     }
@@ -86,11 +96,17 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
     for (int j = 0; j < 8; ++j) { ssum[r * C + c + j] = s[j]; ssq[r * C + c + j] = q[j]; }
   }
   __syncthreads();
+  for (int cc = t; cc < C; cc += blockDim.x) {  // fold the R rows per channel (fixed order)
+    float s = 0.f, q = 0.f;
+    for (int rr = 0; rr < R; ++rr) { s += ssum[rr * C + cc]; q += ssq[rr * C + cc]; }
+    ssum[cc] = s;
+    ssq[cc] = q;
+  }
+  __syncthreads();
   const int cpg = C / G;
   for (int g = t; g < G; g += blockDim.x) {
     float s = 0.f, q = 0.f;
-    for (int rr = 0; rr < R; ++rr)
-      for (int cc = g * cpg; cc < (g + 1) * cpg; ++cc) { s += ssum[rr * C + cc]; q += ssq[rr * C + cc]; }
+    for (int cc = g * cpg; cc < (g + 1) * cpg; ++cc) { s += ssum[cc]; q += ssq[cc]; }
     partial[((size_t)n * nchunks + chunk) * G + g] = make_float2(s, q);
   }
 }
@@ -100,14 +116,25 @@ __global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __r
                               const float2* __restrict__ partial, int nchunks, const float* __restrict__ gamma,
                               const float* __restrict__ beta, float eps, int silu, Tout* __restrict__ y) {
   __shared__ float s_mean[128], s_rstd[128];
+  __shared__ float2 s_part[256];
   const int C = C1 + C2, V = C / 8, cpg = C / G;
   const int n = blockIdx.y;
-  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+  // Group statistics from the partials: blockDim/G threads per group each fold a strided subset of the
+  // chunks, then one thread per group folds those in a fixed order (deterministic).
+  const int tpg = blockDim.x / G;  // blockDim (256) >= G
+  if ((int)threadIdx.x < tpg * G) {
+    const int g = threadIdx.x / tpg, sub = threadIdx.x % tpg;
     float s = 0.f, q = 0.f;
-    for (int k = 0; k < nchunks; ++k) {
+    for (int k = sub; k < nchunks; k += tpg) {
       const float2 pq = partial[((size_t)n * nchunks + k) * G + g];
       s += pq.x; q += pq.y;
     }
+    s_part[threadIdx.x] = make_float2(s, q);
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    float s = 0.f, q = 0.f;
+    for (int u = 0; u < tpg; ++u) { s += s_part[g * tpg + u].x; q += s_part[g * tpg + u].y; }
     const float cnt = (float)cpg * (float)HW;
     const float mean = s / cnt;
     const float var = fmaxf(q / cnt - mean * mean, 0.0f);
@@ -204,7 +231,7 @@ __global__ void layer_norm_rows(const Tin* __restrict__ x, const float* __restri
 // ---------------------------------------------------------------------------------------------
 // Host entry points (also used by the fused blocks / U-Net plan).
 // ---------------------------------------------------------------------------------------------
-int gn_nhwc_chunks(int HW) { return std::max(1, std::min(64, HW / 64)); }
+int gn_nhwc_chunks(int HW) { return std::max(1, std::min(64, HW / 16)); }
 
 template <typename Tin, typename Tout>
 static int gn_nhwc_impl(Ctx* c, const Tin* x1, int C1, const Tin* x2, int C2, int N, int HW, int G, float eps,
@@ -212,7 +239,7 @@ static int gn_nhwc_impl(Ctx* c, const Tin* x1, int C1, const Tin* x2, int C2, in
   const int C = C1 + C2;
   if (C % 8 || C1 % 8 || G <= 0 || G > 128 || C % G) return set_error(c, DI_EINVAL, "group_norm_nhwc: bad channels");
   const int V = C / 8;
-  const int R = std::max(1, 256 / V);
+  const int R = std::max(1, 6144 / C);  // 2*R*C floats of shared memory <= 48 KB
   const int threads = R * V;
   if (threads > 1024) return set_error(c, DI_EUNSUPPORTED, "group_norm_nhwc: too many channels");
   const int chunks = gn_nhwc_chunks(HW);

@@ -11,7 +11,7 @@ namespace di {
 
 int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
                 const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
-                int rowvec_div);
+                int rowvec_div, void* splitk_ws = nullptr);
 int cast_rows_f16(Ctx* c, const float* x, int rows, int cols, int ld_in, void* y, int ld_out, int transpose);
 
 namespace {

@@ -33,10 +33,10 @@ namespace di {
 
 int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
                 const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
-                int rowvec_div);
+                int rowvec_div, void* splitk_ws = nullptr);
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
-                 void* y, int out_f32, int temb_ld);
+                 void* y, int out_f32, int temb_ld, void* splitk_ws = nullptr);
 int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1, const void* x2, int C2, int N,
                     int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
                     void* partial_ws);
@@ -170,6 +170,11 @@ struct Plan {
   int err = DI_OK;
   std::string errmsg;
 
+  // split-K partial sums of the GEMM kernel (at most ~2 CTAs per SM x 128x128 fp32 tiles); ops run
+  // in stream order, so one buffer serves every launch of the plan
+  void* splitk = nullptr;
+  static constexpr size_t kSplitKBytes = 32u << 20;
+
   // temporary bump arena (reset per block; stream order makes reuse safe)
   char* tmp_base = nullptr;
   size_t tmp_cap = 0, tmp_off = 0, tmp_peak = 0;
@@ -177,6 +182,8 @@ struct Plan {
   ~Plan() {
     if (gexec) cudaGraphExecDestroy(gexec);
     if (pexec) cudaGraphExecDestroy(pexec);
+    for (auto& k : kexec)
+      if (k) cudaGraphExecDestroy(k);
     for (auto& e : pev) cudaEventDestroy(e);
     if (stream) { cudaStreamSynchronize(stream); cudaStreamDestroy(stream); }
     if (ev_in) cudaEventDestroy(ev_in);
@@ -270,6 +277,56 @@ struct Plan {
     ops.push_back(std::move(f));
     info.push_back({kind, flops, bytes, kernels});
     launches += kernels;
+  }
+
+  // Device time of the ops of one kind alone: a graph holding only those launches (same buffers, same
+  // order) replayed `reps` times between two events; *ms = mean per replay.  Used to time the GEMM
+  // kernel inside the step without per-op event nodes.
+  cudaGraphExec_t kexec[4] = {nullptr, nullptr, nullptr, nullptr};
+  int profile_kind(int kind, int reps, float* ms) {
+    if (err) return err;
+    if (kind < 0 || kind > 3) return DI_EINVAL;
+    if (!gexec) {
+      int r = forward();
+      if (r) return r;
+      cudaStreamSynchronize(stream);
+    }
+    cudaStream_t saved = c->stream;
+    c->stream = stream;
+    int r = DI_OK;
+    if (!kexec[kind]) {
+      cudaGraph_t g = nullptr;
+      if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        c->stream = saved;
+        return set_error(c, DI_ECUDA, "profile_kind: capture");
+      }
+      for (size_t i = 0; i < ops.size() && r == DI_OK; ++i)
+        if (info[i].kind == kind) r = ops[i]();
+      cudaError_t e = cudaStreamEndCapture(stream, &g);
+      if (r != DI_OK || e != cudaSuccess || cudaGraphInstantiate(&kexec[kind], g, 0) != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        c->stream = saved;
+        cudaGetLastError();
+        return set_error(c, DI_ECUDA, "profile_kind: graph");
+      }
+      cudaGraphDestroy(g);
+    }
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaGraphLaunch(kexec[kind], stream);  // warm
+    cudaEventRecord(e0, stream);
+    for (int i = 0; i < reps; ++i) cudaGraphLaunch(kexec[kind], stream);
+    cudaEventRecord(e1, stream);
+    cudaEventSynchronize(e1);
+    float t = 0.f;
+    cudaEventElapsedTime(&t, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    c->stream = saved;
+    if (cudaGetLastError() != cudaSuccess) return set_error(c, DI_ECUDA, "profile_kind: replay");
+    *ms = t / std::max(1, reps);
+    return DI_OK;
   }
 
   // LOG.profile analogue (wgsl-executor.js:1380-1390): a second graph with an event-record node between
@@ -381,6 +438,7 @@ struct Plan {
     if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return false;
     cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
     cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+    splitk = dalloc(kSplitKBytes);
     tmp_cap = tmp_bytes;
     tmp_base = static_cast<char*>(dalloc(tmp_bytes));
     act_bytes += tmp_bytes;
@@ -424,7 +482,7 @@ struct Plan {
     const void* p2 = x2 ? x2->p : nullptr;
     const int C2 = x2 ? x2->C : 0;
     record([=] { return gemm_conv3x3(cc, DI_F16, xx.p, xx.C, p2, C2, xx.N, xx.H, xx.W, stride, w, Co, b, nullptr,
-                                     nullptr, 0, y.p, 0, Co); },
+                                     nullptr, 0, y.p, 0, Co, splitk); },
            0, 2.0 * y.N * y.H * y.W * Co * 9 * Ci, (double)x.bytes() + 18.0 * Co * Ci + (double)y.bytes());
     return y;
   }
@@ -466,7 +524,7 @@ struct Plan {
   void linear(const void* X, int M, int K, const void* W, int N, const float* b, const void* R, void* Y,
               const void* X2 = nullptr, int K1 = 0) {
     Ctx* cc = c;
-    record([=] { return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1); },
+    record([=] { return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1, splitk); },
            0, 2.0 * M * N * K, 2.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1)));
   }
 
@@ -501,7 +559,7 @@ struct Plan {
     const int N = x1.N, H = x1.H, W = x1.W;
     Plan* self = this;
     record([=] { return gemm_conv3x3(cc, DI_F16, a, Ci, nullptr, 0, N, H, W, 1, w1, Co, b1,
-                                     self->temb_all + toff, nullptr, 0, h.p, 0, self->tproj_ld); },
+                                     self->temb_all + toff, nullptr, 0, h.p, 0, self->tproj_ld, splitk); },
            0, 2.0 * N * H * W * Co * 9 * Ci, 2.0 * ((double)N * H * W * (Ci + Co) + 9.0 * Co * Ci));
     void* a2 = gn(pre + ".norm2", h, nullptr, 1e-5f, 1);
     const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
@@ -516,7 +574,7 @@ struct Plan {
     }
     Act y = new_act(N, H, W, Co);
     record([=] { return gemm_conv3x3(cc, DI_F16, a2, Co, nullptr, 0, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0,
-                                     Co); },
+                                     Co, splitk); },
            0, 2.0 * N * H * W * Co * 9 * Co, 2.0 * ((double)N * H * W * 3 * Co + 9.0 * Co * Co));
     return y;
   }
@@ -602,7 +660,7 @@ struct Plan {
     const float* Bff = upload_f32(bp);
     void* g = tmp((size_t)M * F * 2);
     record([=] { return gemm_linear(cc, DI_F16, n3, C, nullptr, M, C, Wff, 2 * F, Bff, nullptr, 0, g, 0, 1, nullptr,
-                                    1); },
+                                    1, splitk); },
            0, 2.0 * M * 2 * F * C, 2.0 * ((double)M * C + 2.0 * F * C + (double)M * F));
     const void* wf2 = lin_weight(tb + ".ff.net.2.weight", C, F);
     const float* bf2 = vec(tb + ".ff.net.2.bias", C, 0, F);
@@ -664,6 +722,7 @@ static int build_unet(UNetPlan* u) {
   Plan& P = u->P;
   const int B = u->B, H = u->H, W = u->W, Sk = u->Sk;
   Ctx* cc = P.c;
+  void* sk = P.splitk;
   u->latent = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 4 * H * W));
   u->tvals = static_cast<float*>(P.act_alloc(sizeof(float) * B));
   u->ctx32 = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * Sk * 1024));
@@ -725,7 +784,7 @@ static int build_unet(UNetPlan* u) {
     const Act x = lat;
     const Act y = h;
     P.record([=] { return gemm_conv3x3(cc, DI_F16, x.p, 64, nullptr, 0, B, H, W, 1, w, 320, b, nullptr, nullptr, 0,
-                                       y.p, 0, 320); },
+                                       y.p, 0, 320, sk); },
              0, 2.0 * B * H * W * 320 * 9 * 4, (double)B * H * W * (128 + 640));
   }
   const int ch[4] = {320, 640, 1280, 1280};
@@ -768,7 +827,7 @@ static int build_unet(UNetPlan* u) {
     const float* b = P.bias_padded("conv_out.bias", 4, 16, 320 * 9);
     void* y16 = P.act_alloc((size_t)B * H * W * 16 * 2);
     P.record([=] { return gemm_conv3x3(cc, DI_F16, a, 320, nullptr, 0, B, H, W, 1, w, 16, b, nullptr, nullptr, 0, y16,
-                                       0, 16); },
+                                       0, 16, sk); },
              0, 2.0 * B * H * W * 4 * 9 * 320, (double)B * H * W * (640 + 32));
     float* out = u->out;
     P.record([=] {
@@ -796,6 +855,7 @@ static int build_resnet(ResPlan* r, float eps, int temb_silu) {
   Plan& P = r->P;
   const int N = r->N, C = r->C, H = r->H, W = r->W, HW = H * W, T = r->Tdim;
   Ctx* cc = P.c;
+  void* sk = P.splitk;
   r->x = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * C * HW));
   r->temb = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * T));
   r->y = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)N * C * HW));
@@ -828,11 +888,11 @@ static int build_resnet(ResPlan* r, float eps, int temb_silu) {
   P.record([=] { return group_norm_nhwc(cc, DI_F32, DI_F16, xh, C, nullptr, 0, N, HW, 32, eps, G1, Be1, 1, a, part); },
            2, 0, 10.0 * act, 2);
   P.record([=] { return gemv(cc, te, N, T, Wt, 0, Bt, C, temb_silu, tp, C); }, 3, 2.0 * N * C * T, 4.0 * C * T);
-  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W1, C, B1, tp, nullptr, 0, hbuf, 0, C); },
+  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W1, C, B1, tp, nullptr, 0, hbuf, 0, C, sk); },
            0, conv_flops, 4.0 * act + 18.0 * C * C);
   P.record([=] { return group_norm_nhwc(cc, DI_F16, DI_F16, hbuf, C, nullptr, 0, N, HW, 32, eps, G2, Be2, 1, a, part); },
            2, 0, 6.0 * act, 2);
-  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W2, C, B2, nullptr, xh, 1, yh, 1, C); },
+  P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W2, C, B2, nullptr, xh, 1, yh, 1, C, sk); },
            0, conv_flops, 10.0 * act + 18.0 * C * C);
   P.record([=] { return nhwc_to_nchw(cc, DI_F32, DI_F32, yh, y, N, C, HW); }, 3, 0, 8.0 * act);
   cudaDeviceSynchronize();
@@ -938,6 +998,11 @@ DI_API int di_unet_ops(di_unet_t u, int* n_ops, int* kinds, double* flops, doubl
 DI_API int di_unet_profile(di_unet_t u, int reps, float* op_ms) {
   if (!u || !op_ms || reps <= 0) return DI_EINVAL;
   return u->u.P.profile(reps, op_ms);
+}
+
+DI_API int di_unet_profile_kind(di_unet_t u, int kind, int reps, float* ms) {
+  if (!u || !ms || reps <= 0) return DI_EINVAL;
+  return u->u.P.profile_kind(kind, reps, ms);
 }
 
 DI_API int di_unet_forward(di_unet_t u) {

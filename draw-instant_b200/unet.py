@@ -74,6 +74,12 @@ class UNet:
         self.ctx.check(lib().di_unet_profile(self.h, reps, ms.ctypes.data), "di_unet_profile")
         return ms
 
+    def profile_kind(self, kind: int, reps: int = 20) -> float:
+        """Mean device ms per step of the ops of one kind (0 GEMM/conv, 1 attention, 2 norm, 3 other) alone."""
+        ms = ctypes.c_float()
+        self.ctx.check(lib().di_unet_profile_kind(self.h, kind, reps, ctypes.byref(ms)), "di_unet_profile_kind")
+        return ms.value
+
     def forward(self) -> None:
         """Enqueue one forward on the context stream (reads self.latent / t / context, writes self.out)."""
         self.ctx.check(lib().di_unet_forward(self.h), "di_unet_forward")

@@ -130,7 +130,7 @@ DI_API int di_group_norm_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, c
  * call cudaMalloc (a fixed, pre-reserved memory budget, an external allocator that owns the device
  * memory, or latency-critical code that must not take allocation locks).  No counterpart in the
  * reference.  Its scratch is a fixed 1 MiB array inside the library (kept on every GPU that loads the
- * library until the process exits): sizes needing more than N * min(64, max(1, HW/64)) * G * 8 =
+ * library until the process exits): sizes needing more than N * min(64, max(1, HW/16)) * G * 8 =
  * 1 MiB are rejected with DI_EINVAL.  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress), so make that first call before any stream capture.  All calls share the one
  * array: calls that may overlap on the GPU (different streams or contexts on the same device) race and
@@ -200,6 +200,8 @@ DI_API int di_unet_ops(di_unet_t u, int* n_ops, int* kinds, double* flops, doubl
 /* LOG.profile analogue (wgsl-executor.js:1380-1390): replays a graph with an event between every op
  * `reps` times and writes each op's mean device time (ms) to op_ms[n_ops]. */
 DI_API int di_unet_profile(di_unet_t u, int reps, float* op_ms);
+/* Mean device ms of all ops of one kind replayed alone, in plan order (a graph of just those launches). */
+DI_API int di_unet_profile_kind(di_unet_t u, int kind, int reps, float* ms);
 DI_API int di_unet_forward(di_unet_t u);  /* enqueue one forward on the context stream (graph replay) */
 /* host buffers in, host buffer out, synchronous: the unetForwardWGSL(sample, timestep, cond) shape */
 DI_API int di_unet_forward_host(di_unet_t u, const float* latent, const float* t, const float* context, float* out);

@@ -72,10 +72,10 @@ def test_linear_concat_k(ctx, dib):
     assert rel_err(_np(Y), ref) < TOL
 
 
-def test_linear_geglu(ctx, dib, oracle):
+@pytest.mark.parametrize("M,K,F", [(300, 640, 2560), (64, 1280, 5120)])  # the second runs split-K
+def test_linear_geglu(ctx, dib, oracle, M, K, F):
     import torch
     rng = np.random.default_rng(9)
-    M, K, F = 300, 640, 2560
     x = _round(rng.standard_normal((M, K)))
     w = _round(rng.standard_normal((2 * F, K)) / np.sqrt(K))
     bias = (rng.standard_normal(2 * F) * 0.1).astype(np.float32)
