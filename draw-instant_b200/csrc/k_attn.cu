@@ -3,19 +3,21 @@
 // Replaces the reference's per-query-row workgroups (WGSL_FUSED_ATTN fused-attn.js:199-307, which
 // re-reads all of K for every query row and holds a full score row in workgroup memory, and the
 // cross-attention kernel fused-cross-attn.js:112-173 with its single-thread softmax) by a tiled,
-// online-softmax kernel: one CTA per (128 queries, head, image).
+// online-softmax kernel: one CTA per (128 queries, head, image), keys in tiles of 64.
 //
-//   warp 0      TMA: Q tile once, then K/V tiles of 128 keys into a 2-stage ring
-//   warp 1      MMA: S_j = Q K_j^T (M=128, N=128, K=64) into a double-buffered TMEM tile, so the
-//               product for tile j+1 runs while the softmax warps work on tile j; then
-//               O += P_j V_j (M=128, N=64, K=128) with O resident in TMEM for the whole row block
+//   warp 0      TMA: Q tile once, then K/V tiles of 64 keys into a 3-stage ring
+//   warp 1      MMA: S_j = Q K_j^T (M=128, N=64, K=64) into a double-buffered TMEM tile, so the product
+//               for tile j+1 runs while the softmax warps work on tile j; then O += P_j V_j
+//               (M=128, N=64, K=64) with O resident in TMEM for the whole row block
 //   warps 2..5  softmax, one query row per thread (= one TMEM lane): running max / sum in the exp2
 //               domain, rescale of O in TMEM when the max moves, P written to shared memory as fp16/bf16
 //               in the 128B-swizzled K-major layout the MMA reads; finally O / l is stored.
 //
+// Footprint: ~81 KB shared memory and 256 TMEM columns (S0 [0,64), S1 [64,128), O [128,192)), so two
+// CTAs share an SM: one CTA's softmax overlaps the other's tensor-core work, and the U-Net's
+// 160-CTA attention grids are resident in a single wave.
 // Scores are scaled by 1/sqrt(64) as in the reference.  Keys past Skv (the zero-filled tail of the last
-// TMA box) are masked to -inf.  TMEM: S0 [0,128), S1 [128,256), O [256,320) of a 512-column allocation.
-// All waits are time-bounded; no multicast loads.
+// TMA box) are masked to -inf.  All waits are time-bounded; no multicast loads.
 #include <algorithm>
 
 #include "di_common.cuh"
@@ -34,26 +36,28 @@ struct AttnParams {
 
 namespace {
 
-constexpr int QT = 128, KT = 128, HD = 64;
-constexpr uint32_t TILE_BYTES = QT * HD * 2;  // 16 KB
-constexpr uint32_t SMEM_ATTN = 1024 + TILE_BYTES * 5 + 2 * TILE_BYTES + 512;
+constexpr int QT = 128, KT = 64, HD = 64, KV_STAGES = 3;
+constexpr uint32_t Q_BYTES = QT * HD * 2;   // 16 KB
+constexpr uint32_t KV_BYTES = KT * HD * 2;  // 8 KB per K or V tile
+constexpr uint32_t P_BYTES = QT * KT * 2;   // 16 KB
+constexpr uint32_t SMEM_ATTN = 1024 + Q_BYTES + 2 * KV_STAGES * KV_BYTES + P_BYTES + 512;
 
 template <bool BF16>
-__global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + TILE_BYTES;        // 2 stages
-  uint8_t* sV = sK + 2 * TILE_BYTES;    // 2 stages
-  uint8_t* sP = sV + 2 * TILE_BYTES;    // 128 x 128 fp16: two 64-key K-major blocks
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE_BYTES);
+  uint8_t* sK = sQ + Q_BYTES;               // KV_STAGES tiles
+  uint8_t* sV = sK + KV_STAGES * KV_BYTES;  // KV_STAGES tiles
+  uint8_t* sP = sV + KV_STAGES * KV_BYTES;  // 128 x 64, one 128B-swizzled K-major block
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;
-  uint64_t* o_done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* kv_full = bars + 1;                // [KV_STAGES]
+  uint64_t* kv_empty = kv_full + KV_STAGES;    // [KV_STAGES]
+  uint64_t* s_full = kv_empty + KV_STAGES;     // [2]
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -62,18 +66,19 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); mbar_init(&s_full[i], 1); }
+    for (int i = 0; i < KV_STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) mbar_init(&s_full[i], 1);
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  if (warp == 1) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS0 = tmem, tO = tmem + 256;
+  const uint32_t tS0 = tmem, tO = tmem + 128;
 
   if (warp == 0) {
     if (elect_one()) {
@@ -81,19 +86,19 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
       tma_prefetch_desc(&p.tmK);
       tma_prefetch_desc(&p.tmV);
       const int c1q = p.layout == 0 ? h : q0, c2q = p.layout == 0 ? q0 : h;
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      mbar_arrive_expect_tx(q_full, Q_BYTES);
       tma_load_4d(sQ, &p.tmQ, q_full, 0, c1q, c2q, b);
       for (int j = 0; j < nt; ++j) {
-        const int st = j & 1;
-        if (*abort_flag || !mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, p.err, DEVERR_WAIT_TMA)) {
+        const int st = j % KV_STAGES;
+        if (*abort_flag || !mbar_wait(&kv_empty[st], ((j / KV_STAGES) & 1) ^ 1, p.err, DEVERR_WAIT_TMA)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * KV_BYTES);
         const int k0 = j * KT;
         const int c1 = p.layout == 0 ? h : k0, c2 = p.layout == 0 ? k0 : h;
-        tma_load_4d(sK + st * TILE_BYTES, &p.tmK, &kv_full[st], 0, c1, c2, b);
-        tma_load_4d(sV + st * TILE_BYTES, &p.tmV, &kv_full[st], 0, c1, c2, b);
+        tma_load_4d(sK + st * KV_BYTES, &p.tmK, &kv_full[st], 0, c1, c2, b);
+        tma_load_4d(sV + st * KV_BYTES, &p.tmV, &kv_full[st], 0, c1, c2, b);
       }
     }
   } else if (warp == 1) {
@@ -103,11 +108,11 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
       const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, p.err, DEVERR_WAIT_MMA);
       auto issue_pv = [&](int jj) {
-        const int st = jj & 1;
-        const uint32_t aV = smem_u32(sV + st * TILE_BYTES);
+        const int st = jj % KV_STAGES;
+        const uint32_t aV = smem_u32(sV + st * KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(aP + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = sdesc_sw128(aP + kk * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(aV + kk * 2048, 8192, 1024);
           umma_f16(tO, ad, bd, idO, (jj | kk) != 0 ? 1u : 0u);
         }
@@ -115,17 +120,20 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
         umma_commit(&kv_empty[st]);
       };
       for (int j = 0; ok && j < nt; ++j) {
-        const int st = j & 1;
-        if (*abort_flag || !mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, DEVERR_WAIT_MMA)) { ok = false; break; }
+        const int st = j % KV_STAGES;
+        if (*abort_flag || !mbar_wait(&kv_full[st], (j / KV_STAGES) & 1, p.err, DEVERR_WAIT_MMA)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t aK = smem_u32(sK + st * TILE_BYTES);
+        const uint32_t aK = smem_u32(sK + st * KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint64_t ad = sdesc_sw128(aQ + kk * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(aK + kk * 32, 16, 1024);
-          umma_f16(tS0 + st * 128, ad, bd, idS, kk != 0 ? 1u : 0u);
+          umma_f16(tS0 + (j & 1) * KT, ad, bd, idS, kk != 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[j & 1]);
         if (j > 0) {
           if (!mbar_wait(p_full, (j - 1) & 1, p.err, DEVERR_WAIT_MMA)) { ok = false; break; }
           tc_fence_after();
@@ -149,15 +157,15 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
     bool ok = true;
     uint8_t* prow = sP + row * 128;
     for (int j = 0; j < nt; ++j) {
-      const int st = j & 1;
-      ok = ok && mbar_wait(&s_full[st], (j >> 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
+      const int sb = j & 1;
+      ok = ok && mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
       tc_fence_after();
-      float s[128];
+      float s[KT];
       {
         uint32_t r[32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tS0 + st * 128 + lane_off + c * 32, r);
+        for (int c = 0; c < KT / 32; ++c) {
+          tmem_ld32(tS0 + sb * KT + lane_off + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
       const int kvalid = p.Skv - j * KT;
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
+      for (int i = 0; i < KT; ++i) {
         s[i] = i < kvalid ? s[i] * p.scale_log2 : -INFINITY;
         mx = fmaxf(mx, s[i]);
       }
@@ -174,7 +182,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
       const float alpha = exp2f(m_run - m_new);
       float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
+      for (int i = 0; i < KT; ++i) {
         s[i] = exp2f(s[i] - m_new);
         sum += s[i];
       }
@@ -187,7 +195,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
           uint32_t r[32];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < HD / 32; ++c) {
             tmem_ld32(tO + lane_off + c * 32, r);
             tmem_wait_ld();
 #pragma unroll
@@ -199,7 +207,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
       }
       // P row -> shared memory, 128B swizzle: 16-byte chunk c of row r lands at chunk c ^ (r % 8).
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < KT / 8; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -212,8 +220,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
             w[e] = *reinterpret_cast<uint32_t*>(&v);
           }
         }
-        const int blk = c >> 3, ch = (c & 7) ^ (row & 7);
-        *reinterpret_cast<uint4*>(prow + blk * TILE_BYTES + ch * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       fence_async_smem();
       tc_fence_before();
@@ -254,12 +261,13 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_kernel(const __grid_constant_
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 256);
   }
 }
 
-bool attn_map(CUtensorMap* m, int dtype, const void* base, int B, int H, int S, int layout, long long ld) {
-  // layout 0: token-major rows of ld elements holding H heads of 64; layout 1: [B][H][S][64].
+// layout 0: token-major rows of ld elements holding H heads of 64; layout 1: [B][H][S][64].
+bool attn_map(CUtensorMap* m, int dtype, const void* base, int B, int H, int S, int layout, long long ld,
+              uint32_t rows) {
   const CUtensorMapDataType dt =
       dtype == DI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   uint64_t dims[4], strides[3];
@@ -267,11 +275,11 @@ bool attn_map(CUtensorMap* m, int dtype, const void* base, int B, int H, int S, 
   if (layout == 0) {
     dims[0] = 64; dims[1] = H; dims[2] = S; dims[3] = B;
     strides[0] = 128; strides[1] = (uint64_t)ld * 2; strides[2] = (uint64_t)S * ld * 2;
-    box[0] = 64; box[1] = 1; box[2] = 128; box[3] = 1;
+    box[0] = 64; box[1] = 1; box[2] = rows; box[3] = 1;
   } else {
     dims[0] = 64; dims[1] = S; dims[2] = H; dims[3] = B;
     strides[0] = 128; strides[1] = (uint64_t)S * 128; strides[2] = (uint64_t)H * S * 128;
-    box[0] = 64; box[1] = 128; box[2] = 1; box[3] = 1;
+    box[0] = 64; box[1] = rows; box[2] = 1; box[3] = 1;
   }
   std::string err;
   return make_tmap(m, dt, 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &err);
@@ -286,8 +294,8 @@ int attention(Ctx* c, int dtype, const void* Q, const void* K, const void* V, vo
     return set_error(c, DI_EINVAL, "attention: bad shape");
   AttnParams p;
   memset(&p, 0, sizeof p);
-  if (!attn_map(&p.tmQ, dtype, Q, B, H, Sq, layout, ld_q) || !attn_map(&p.tmK, dtype, K, B, H, Skv, layout, ld_k) ||
-      !attn_map(&p.tmV, dtype, V, B, H, Skv, layout, ld_v))
+  if (!attn_map(&p.tmQ, dtype, Q, B, H, Sq, layout, ld_q, QT) || !attn_map(&p.tmK, dtype, K, B, H, Skv, layout, ld_k, KT) ||
+      !attn_map(&p.tmV, dtype, V, B, H, Skv, layout, ld_v, KT))
     return set_error(c, DI_EINVAL, "attention: tensor map (pointers and row strides must be 16-byte aligned)");
   p.out = O;
   if (layout == 0) { p.o_sb = (long long)Sq * ld_o; p.o_ss = ld_o; p.o_sh = 64; }

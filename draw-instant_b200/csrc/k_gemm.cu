@@ -325,6 +325,27 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
                               int ldr, int res_f32, void* out, int ldo, int out_f32, int geglu, int bf16) {
   const size_t slice = (size_t)M * N;
   const int NO = geglu ? N / 2 : N;
+  if (!geglu && (N & 3) == 0 && (ldo & 3) == 0 && (!residual || (ldr & 3) == 0)) {
+    // four columns per thread: float4 partial loads
+    const size_t total4 = (size_t)M * N / 4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total4; i += (size_t)gridDim.x * blockDim.x) {
+      const int m = (int)((i * 4) / N), o = (int)((i * 4) % N);
+      float4 v = reinterpret_cast<const float4*>(part)[i];
+      for (int z = 1; z < splits; ++z) {
+        const float4 w = reinterpret_cast<const float4*>(part + z * slice)[i];
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+      }
+      float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (bias) f[j] += bias[o + j];
+        if (rowvec) f[j] += rowvec[(size_t)(m / rowvec_div) * rowvec_ld + o + j];
+        if (residual) f[j] += load_one(residual, (size_t)m * ldr + o + j, res_f32, bf16);
+        store_one(out, (size_t)m * ldo + o + j, f[j], out_f32, bf16);
+      }
+    }
+    return;
+  }
   const size_t total = (size_t)M * NO;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int m = i / NO, o = i % NO;
@@ -355,24 +376,24 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
 // 128-wide tiles split along K so that about two CTAs per SM stream disjoint weight slices.  Few tiles
 // with a short K: 64-wide tiles for more CTAs.
 void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits) {
-  const long long tiles128 = (long long)((N + 127) / 128) * ((M + 127) / 128);
+  const int tiles128 = ((N + 127) / 128) * ((M + 127) / 128);
   *splits = 1;
-  if (geglu || tiles128 >= c->num_sms) { *bn = 128; }
-  else if (M <= 512 && num_k >= 16) {
-    *bn = 128;
-    int s = (int)std::min<long long>(num_k / 4, (2LL * c->num_sms + tiles128 - 1) / tiles128);
-    s = std::max(1, s);
+  *bn = 128;
+  if (tiles128 >= c->num_sms) return;
+  // at most two resident CTAs per SM: keep tiles x splits within one wave of 2 * SMs
+  int s = std::min(num_k / 4, (2 * c->num_sms) / tiles128);
+  if (num_k >= 16 && s >= 2) {
     const int per = (num_k + s - 1) / s;
     *splits = (num_k + per - 1) / per;
-  } else {
-    *bn = (N % 64 == 0) ? 64 : 128;
+  } else if (!geglu && N % 64 == 0) {
+    *bn = 64;
   }
-  if (geglu && M <= 512 && num_k >= 16 && tiles128 < c->num_sms) {
-    int s = (int)std::min<long long>(num_k / 4, (2LL * c->num_sms + tiles128 - 1) / tiles128);
-    s = std::max(1, s);
-    const int per = (num_k + s - 1) / s;
-    *splits = (num_k + per - 1) / per;
-  }
+}
+
+int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
+  int bn, s;
+  choose_tiling(c, M, N, K / 64, geglu, &bn, &s);
+  return s > 1 ? 2 : 1;
 }
 
 // Chooses the N tile: 128 by default; 64 when the grid would leave most SMs idle.

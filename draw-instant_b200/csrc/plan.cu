@@ -41,6 +41,7 @@ int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1,
                     int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
                     void* partial_ws);
 size_t gn_nhwc_ws_bytes(int N, int HW, int G);
+int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu);
 int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* g, const float* b, void* y, int rows,
                int D, float eps);
 int attention(Ctx* c, int dtype, const void* Q, const void* K, const void* V, void* O, int B, int H, int Sq, int Skv,
@@ -483,7 +484,7 @@ struct Plan {
     const int C2 = x2 ? x2->C : 0;
     record([=] { return gemm_conv3x3(cc, DI_F16, xx.p, xx.C, p2, C2, xx.N, xx.H, xx.W, stride, w, Co, b, nullptr,
                                      nullptr, 0, y.p, 0, Co, splitk); },
-           0, 2.0 * y.N * y.H * y.W * Co * 9 * Ci, (double)x.bytes() + 18.0 * Co * Ci + (double)y.bytes());
+           0, 2.0 * y.N * y.H * y.W * Co * 9 * Ci, (double)x.bytes() + 18.0 * Co * Ci + (double)y.bytes(), gemm_kernel_count(c, y.N * y.H * y.W, Co, 9 * Ci, 0));
     return y;
   }
 
@@ -525,7 +526,7 @@ struct Plan {
               const void* X2 = nullptr, int K1 = 0) {
     Ctx* cc = c;
     record([=] { return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1, splitk); },
-           0, 2.0 * M * N * K, 2.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1)));
+           0, 2.0 * M * N * K, 2.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1)), gemm_kernel_count(c, M, N, K, 0));
   }
 
   // ResnetBlock2D on concat(x1, x2): gn1+silu -> conv1 (+b1 +time proj) -> gn2+silu -> conv2 (+b2 + shortcut).
@@ -560,7 +561,7 @@ struct Plan {
     Plan* self = this;
     record([=] { return gemm_conv3x3(cc, DI_F16, a, Ci, nullptr, 0, N, H, W, 1, w1, Co, b1,
                                      self->temb_all + toff, nullptr, 0, h.p, 0, self->tproj_ld, splitk); },
-           0, 2.0 * N * H * W * Co * 9 * Ci, 2.0 * ((double)N * H * W * (Ci + Co) + 9.0 * Co * Ci));
+           0, 2.0 * N * H * W * Co * 9 * Ci, 2.0 * ((double)N * H * W * (Ci + Co) + 9.0 * Co * Ci), gemm_kernel_count(c, N * H * W, Co, 9 * Ci, 0));
     void* a2 = gn(pre + ".norm2", h, nullptr, 1e-5f, 1);
     const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
     const float* b2 = bias_padded(pre + ".conv2.bias", Co, Co, Co * 9);
@@ -575,7 +576,7 @@ struct Plan {
     Act y = new_act(N, H, W, Co);
     record([=] { return gemm_conv3x3(cc, DI_F16, a2, Co, nullptr, 0, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0,
                                      Co, splitk); },
-           0, 2.0 * N * H * W * Co * 9 * Co, 2.0 * ((double)N * H * W * 3 * Co + 9.0 * Co * Co));
+           0, 2.0 * N * H * W * Co * 9 * Co, 2.0 * ((double)N * H * W * 3 * Co + 9.0 * Co * Co), gemm_kernel_count(c, N * H * W, Co, 9 * Co, 0));
     return y;
   }
 
@@ -661,7 +662,7 @@ struct Plan {
     void* g = tmp((size_t)M * F * 2);
     record([=] { return gemm_linear(cc, DI_F16, n3, C, nullptr, M, C, Wff, 2 * F, Bff, nullptr, 0, g, 0, 1, nullptr,
                                     1, splitk); },
-           0, 2.0 * M * 2 * F * C, 2.0 * ((double)M * C + 2.0 * F * C + (double)M * F));
+           0, 2.0 * M * 2 * F * C, 2.0 * ((double)M * C + 2.0 * F * C + (double)M * F), gemm_kernel_count(c, M, 2 * F, C, 1));
     const void* wf2 = lin_weight(tb + ".ff.net.2.weight", C, F);
     const float* bf2 = vec(tb + ".ff.net.2.bias", C, 0, F);
     void* h3 = tmp((size_t)M * C * 2);
@@ -785,7 +786,7 @@ static int build_unet(UNetPlan* u) {
     const Act y = h;
     P.record([=] { return gemm_conv3x3(cc, DI_F16, x.p, 64, nullptr, 0, B, H, W, 1, w, 320, b, nullptr, nullptr, 0,
                                        y.p, 0, 320, sk); },
-             0, 2.0 * B * H * W * 320 * 9 * 4, (double)B * H * W * (128 + 640));
+             0, 2.0 * B * H * W * 320 * 9 * 4, (double)B * H * W * (128 + 640), gemm_kernel_count(cc, B * H * W, 320, 9 * 64, 0));
   }
   const int ch[4] = {320, 640, 1280, 1280};
   std::vector<Act> skips{h};
@@ -828,7 +829,7 @@ static int build_unet(UNetPlan* u) {
     void* y16 = P.act_alloc((size_t)B * H * W * 16 * 2);
     P.record([=] { return gemm_conv3x3(cc, DI_F16, a, 320, nullptr, 0, B, H, W, 1, w, 16, b, nullptr, nullptr, 0, y16,
                                        0, 16, sk); },
-             0, 2.0 * B * H * W * 4 * 9 * 320, (double)B * H * W * (640 + 32));
+             0, 2.0 * B * H * W * 4 * 9 * 320, (double)B * H * W * (640 + 32), gemm_kernel_count(cc, B * H * W, 16, 9 * 320, 0));
     float* out = u->out;
     P.record([=] {
       const size_t n = (size_t)B * 4 * H * W;
@@ -889,11 +890,11 @@ static int build_resnet(ResPlan* r, float eps, int temb_silu) {
            2, 0, 10.0 * act, 2);
   P.record([=] { return gemv(cc, te, N, T, Wt, 0, Bt, C, temb_silu, tp, C); }, 3, 2.0 * N * C * T, 4.0 * C * T);
   P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W1, C, B1, tp, nullptr, 0, hbuf, 0, C, sk); },
-           0, conv_flops, 4.0 * act + 18.0 * C * C);
+           0, conv_flops, 4.0 * act + 18.0 * C * C, gemm_kernel_count(cc, N * HW, C, 9 * C, 0));
   P.record([=] { return group_norm_nhwc(cc, DI_F16, DI_F16, hbuf, C, nullptr, 0, N, HW, 32, eps, G2, Be2, 1, a, part); },
            2, 0, 6.0 * act, 2);
   P.record([=] { return gemm_conv3x3(cc, DI_F16, a, C, nullptr, 0, N, H, W, 1, W2, C, B2, nullptr, xh, 1, yh, 1, C, sk); },
-           0, conv_flops, 10.0 * act + 18.0 * C * C);
+           0, conv_flops, 10.0 * act + 18.0 * C * C, gemm_kernel_count(cc, N * HW, C, 9 * C, 0));
   P.record([=] { return nhwc_to_nchw(cc, DI_F32, DI_F32, yh, y, N, C, HW); }, 3, 0, 8.0 * act);
   cudaDeviceSynchronize();
   return P.err;
