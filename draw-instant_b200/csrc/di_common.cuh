@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string>
+#include <utility>
 
 #include "../../include/di.h"
 
@@ -34,6 +35,9 @@ struct Ctx {
   int sticky = 0;                // sticky fault (device lost / kernel error), like unet-wgsl.js _gpuError
   int num_sms = 148;
   struct Scratch { void* ptr = nullptr; size_t bytes = 0; } ws[6];  // library-owned workspace slots
+  // Set while a plan enqueues its ops: GEMM weight operands are not written by any kernel still in
+  // flight, so they may be read before the programmatic-dependency wait.
+  bool weights_const = false;
 };
 
 Ctx* ctx_of(di_ctx_t h);
@@ -48,6 +52,23 @@ bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* b
                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz, std::string* err);
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
+
+// Kernel launch with programmatic stream serialisation (see pdl_wait in the device helpers).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // device error codes (OR-ed into Ctx::d_err)
 enum : int {
@@ -74,6 +95,19 @@ __device__ __forceinline__ bool elect_one() {
       "{\n\t.reg .pred P;\n\telect.sync _|P, %1;\n\tselp.b32 %0, 1, 0, P;\n\t}\n"
       : "=r"(pred) : "r"(0xffffffffu));
   return pred != 0;
+}
+
+// ---- programmatic dependent launch ----
+// Every libdi kernel is launched with programmatic stream serialisation (launch_k below): the next
+// kernel's CTAs may start while this one drains, run their memory-free set-up (barrier init, TMEM
+// allocation, descriptor prefetch), then block in pdl_wait() until the previous grid has completed and
+// its writes are visible.  Kernels touch no global memory before pdl_wait().  pdl_trigger() lets the
+// next kernel be scheduled as soon as every CTA of this one has started.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_begin() {
+  pdl_wait();
+  pdl_trigger();
 }
 
 // ---- mbarrier ----

@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_begin();  // set-up above touches no global memory
   const uint32_t tS0 = tmem, tO = tmem + 128;
 
   if (warp == 0) {
@@ -315,7 +316,7 @@ int attention(Ctx* c, int dtype, const void* Q, const void* K, const void* V, vo
     attr_done[di] |= 1u << (c->device & 31);
   }
   dim3 grid((Sq + QT - 1) / QT, H, B);
-  kern<<<grid, 192, SMEM_ATTN, c->stream>>>(p);
+  launch_k(kern, grid, 192, SMEM_ATTN, c->stream, p);
   return check_launch(c, "attention");
 }
 

@@ -49,10 +49,12 @@ __device__ __forceinline__ float binary_op(int op, float a, float b) {
 }
 
 __global__ void unary_kernel(int op, const float* __restrict__ x, float* __restrict__ y, uint32_t n) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = unary_op(op, x[i]);
 }
 __global__ void binary_kernel(int op, const float* __restrict__ a, uint32_t na, const float* __restrict__ b,
                               uint32_t nb, float* __restrict__ y, uint32_t n) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     y[i] = binary_op(op, a[i % na], b[i % nb]);
 }
@@ -70,6 +72,7 @@ __device__ __forceinline__ void decompose(const Cfg20& c, uint32_t i, uint32_t i
 
 __global__ void binary_bcast_kernel(int op, const float* __restrict__ a, const float* __restrict__ b,
                                     float* __restrict__ y, Cfg20 c) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < c.v[16]; i += gridDim.x * blockDim.x) {
     uint32_t idx[4];
     decompose(c, i, idx);
@@ -81,6 +84,7 @@ __global__ void binary_bcast_kernel(int op, const float* __restrict__ a, const f
 }
 __global__ void affine_bcast_kernel(const float* __restrict__ a, const float* __restrict__ g,
                                     const float* __restrict__ bt, float* __restrict__ y, Cfg20 c) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < c.v[16]; i += gridDim.x * blockDim.x) {
     uint32_t idx[4];
     decompose(c, i, idx);
@@ -91,6 +95,7 @@ __global__ void affine_bcast_kernel(const float* __restrict__ a, const float* __
   }
 }
 __global__ void transpose_kernel(const float* __restrict__ x, float* __restrict__ y, Cfg20 c) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < c.v[16]; i += gridDim.x * blockDim.x) {
     uint32_t o[4];
     decompose(c, i, o);
@@ -103,6 +108,7 @@ __global__ void transpose_kernel(const float* __restrict__ x, float* __restrict_
   }
 }
 __global__ void slice_kernel(const float* __restrict__ x, float* __restrict__ y, Cfg20 c) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < c.v[16]; i += gridDim.x * blockDim.x) {
     uint32_t o[4];
     decompose(c, i, o);
@@ -115,6 +121,7 @@ __global__ void slice_kernel(const float* __restrict__ x, float* __restrict__ y,
 
 // Softmax / ReduceMean over the last dim: one warp per row.
 __global__ void softmax_rows(const float* __restrict__ x, float* __restrict__ y, uint32_t inner, uint32_t rows) {
+  pdl_begin();
   const uint32_t row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= rows) return;
   const float* xr = x + (size_t)row * inner;
@@ -128,6 +135,7 @@ __global__ void softmax_rows(const float* __restrict__ x, float* __restrict__ y,
   for (uint32_t j = lane; j < inner; j += 32) y[(size_t)row * inner + j] = expf(xr[j] - m) * inv;
 }
 __global__ void reduce_mean_rows(const float* __restrict__ x, float* __restrict__ y, uint32_t inner, uint32_t rows) {
+  pdl_begin();
   const uint32_t row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= rows) return;
   float s = 0.f;
@@ -138,12 +146,14 @@ __global__ void reduce_mean_rows(const float* __restrict__ x, float* __restrict_
 
 __global__ void resize_nearest_kernel(const float* __restrict__ x, float* __restrict__ y, uint32_t Hi, uint32_t Wi,
                                       uint32_t Ho, uint32_t Wo, uint32_t n) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const uint32_t ox = i % Wo, t = i / Wo, oy = t % Ho, oc = t / Ho;
     y[i] = x[(oc * Hi + (oy * Hi) / Ho) * Wi + (ox * Wi) / Wo];
   }
 }
 __global__ void pow_scalar_kernel(const float* __restrict__ x, float* __restrict__ y, float e, uint32_t n) {
+  pdl_begin();
   const float ei = floorf(e);
   const bool is_int = fabsf(e - ei) < 1e-6f;
   const bool odd = ((int)ei & 1) == 1;
@@ -156,6 +166,7 @@ __global__ void pow_scalar_kernel(const float* __restrict__ x, float* __restrict
 }
 __global__ void concat_copy_kernel(const float* __restrict__ x, float* __restrict__ y, uint32_t stripe_in,
                                    uint32_t stripe_out, uint32_t off, uint32_t n) {
+  pdl_begin();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     y[(i / stripe_in) * stripe_out + off + i % stripe_in] = x[i];
 }
@@ -163,6 +174,7 @@ __global__ void concat_copy_kernel(const float* __restrict__ x, float* __restric
 // Timestep embedding stage 1: h[b][o] = silu(W1[o] . [cos||sin](t_b f) + b1[o]); one warp per output o.
 __global__ void tembed_stage1(const float* __restrict__ t, int B, const float* __restrict__ W1,
                               const float* __restrict__ b1, int Din, int Dh, float* __restrict__ h) {
+  pdl_begin();
   extern __shared__ float emb[];  // [B][Din]
   const int half = Din / 2;
   const float LOG = 9.210340371976184f;  // ln(10000)
@@ -190,6 +202,7 @@ __global__ void tembed_stage1(const float* __restrict__ t, int B, const float* _
 template <typename TW>
 __global__ void gemv_rows(const float* __restrict__ x, int B, int K, const TW* __restrict__ W,
                           const float* __restrict__ bias, int N, int silu_in, float* __restrict__ y, int ldy) {
+  pdl_begin();
   extern __shared__ float xs[];  // [B][K]
   for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
     const float v = x[i];
@@ -216,9 +229,9 @@ int gemv(Ctx* c, const float* x, int B, int K, const void* W, int w_f16, const f
   }
   const int blocks = (N + 7) / 8;
   if (w_f16)
-    gemv_rows<__half><<<blocks, 256, shm, c->stream>>>(x, B, K, static_cast<const __half*>(W), bias, N, silu_in, y, ldy);
+    launch_k(gemv_rows<__half>, blocks, 256, shm, c->stream, x, B, K, static_cast<const __half*>(W), bias, N, silu_in, y, ldy);
   else
-    gemv_rows<float><<<blocks, 256, shm, c->stream>>>(x, B, K, static_cast<const float*>(W), bias, N, silu_in, y, ldy);
+    launch_k(gemv_rows<float>, blocks, 256, shm, c->stream, x, B, K, static_cast<const float*>(W), bias, N, silu_in, y, ldy);
   return check_launch(c, "gemv");
 }
 
@@ -226,7 +239,7 @@ int tembed(Ctx* c, const float* t, int B, const float* W1, const float* b1, cons
            int Dh, float* hidden, float* y) {
   const size_t shm = sizeof(float) * (size_t)B * Din;
   if (shm > 48 * 1024 || Din % 2) return set_error(c, DI_EUNSUPPORTED, "tembed: sizes");
-  tembed_stage1<<<(Dh + 7) / 8, 256, shm, c->stream>>>(t, B, W1, b1, Din, Dh, hidden);
+  launch_k(tembed_stage1, (Dh + 7) / 8, 256, shm, c->stream, t, B, W1, b1, Din, Dh, hidden);
   int r = check_launch(c, "tembed_stage1");
   if (r) return r;
   return gemv(c, hidden, B, Dh, W2, 0, b2, Dh, 0, y, Dh);
@@ -235,6 +248,7 @@ int tembed(Ctx* c, const float* t, int B, const float* W1, const float* b1, cons
 // Layout converters for the NCHW fp32 drop-ins: [N][C][HW] <-> [N][HW][C] through a 32x32 smem tile.
 template <typename Tin, typename Tout>
 __global__ void nchw_to_nhwc_kernel(const Tin* __restrict__ x, Tout* __restrict__ y, int C, int HW) {
+  pdl_begin();
   __shared__ float tile[32][33];
   const int n = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -249,6 +263,7 @@ __global__ void nchw_to_nhwc_kernel(const Tin* __restrict__ x, Tout* __restrict_
 }
 template <typename Tin, typename Tout>
 __global__ void nhwc_to_nchw_kernel(const Tin* __restrict__ x, Tout* __restrict__ y, int C, int HW) {
+  pdl_begin();
   __shared__ float tile[32][33];
   const int n = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -265,7 +280,7 @@ __global__ void nhwc_to_nchw_kernel(const Tin* __restrict__ x, Tout* __restrict_
 int nchw_to_nhwc(Ctx* c, int in_dt, int out_dt, const void* x, void* y, int N, int C, int HW) {
   dim3 grid((HW + 31) / 32, (C + 31) / 32, N), block(32, 8);
 #define NC_CASE(TI, TO) \
-  nchw_to_nhwc_kernel<TI, TO><<<grid, block, 0, c->stream>>>(static_cast<const TI*>(x), static_cast<TO*>(y), C, HW)
+  launch_k(nchw_to_nhwc_kernel<TI, TO>, grid, block, 0, c->stream, static_cast<const TI*>(x), static_cast<TO*>(y), C, HW)
   if (in_dt == DI_F32 && out_dt == DI_F32) NC_CASE(float, float);
   else if (in_dt == DI_F32 && out_dt == DI_F16) NC_CASE(float, __half);
   else if (in_dt == DI_F32 && out_dt == DI_BF16) NC_CASE(float, __nv_bfloat16);
@@ -277,7 +292,7 @@ int nchw_to_nhwc(Ctx* c, int in_dt, int out_dt, const void* x, void* y, int N, i
 int nhwc_to_nchw(Ctx* c, int in_dt, int out_dt, const void* x, void* y, int N, int C, int HW) {
   dim3 grid((HW + 31) / 32, (C + 31) / 32, N), block(32, 8);
 #define CN_CASE(TI, TO) \
-  nhwc_to_nchw_kernel<TI, TO><<<grid, block, 0, c->stream>>>(static_cast<const TI*>(x), static_cast<TO*>(y), C, HW)
+  launch_k(nhwc_to_nchw_kernel<TI, TO>, grid, block, 0, c->stream, static_cast<const TI*>(x), static_cast<TO*>(y), C, HW)
   if (in_dt == DI_F32 && out_dt == DI_F32) CN_CASE(float, float);
   else if (in_dt == DI_F16 && out_dt == DI_F32) CN_CASE(__half, float);
   else if (in_dt == DI_BF16 && out_dt == DI_F32) CN_CASE(__nv_bfloat16, float);
@@ -291,6 +306,7 @@ int nhwc_to_nchw(Ctx* c, int in_dt, int out_dt, const void* x, void* y, int N, i
 template <typename TO>
 __global__ void cast_rows_kernel(const float* __restrict__ x, int rows, int cols, int ld_in, TO* __restrict__ y,
                                  int ld_out, int transpose) {
+  pdl_begin();
   const size_t total = (size_t)rows * ld_out;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int r = i / ld_out, k = i % ld_out;
@@ -303,7 +319,7 @@ __global__ void cast_rows_kernel(const float* __restrict__ x, int rows, int cols
 // or column-major x[cols][rows] (transpose=1, i.e. x[k][r] with row stride ld_in).
 int cast_rows_f16(Ctx* c, const float* x, int rows, int cols, int ld_in, void* y, int ld_out, int transpose) {
   const size_t total = (size_t)rows * ld_out;
-  cast_rows_kernel<__half><<<grid_for(c, total), 256, 0, c->stream>>>(x, rows, cols, ld_in, static_cast<__half*>(y),
+  launch_k(cast_rows_kernel<__half>, grid_for(c, total), 256, 0, c->stream, x, rows, cols, ld_in, static_cast<__half*>(y),
                                                                        ld_out, transpose);
   return check_launch(c, "cast_rows");
 }
@@ -318,14 +334,14 @@ int di_unary(di_ctx_t h, int op, const float* X, float* Y, uint32_t n) {
   Ctx* c = ctx_of(h);
   if (!c || op < 0 || op > DI_ERF) return DI_EINVAL;
   if (!n) return DI_OK;
-  unary_kernel<<<grid_for(c, n), 256, 0, c->stream>>>(op, X, Y, n);
+  launch_k(unary_kernel, grid_for(c, n), 256, 0, c->stream, op, X, Y, n);
   return check_launch(c, "unary");
 }
 int di_binary(di_ctx_t h, int op, const float* A, uint32_t nA, const float* B, uint32_t nB, float* Y, uint32_t n) {
   Ctx* c = ctx_of(h);
   if (!c || op < 0 || op > DI_MIN || !nA || !nB) return DI_EINVAL;
   if (!n) return DI_OK;
-  binary_kernel<<<grid_for(c, n), 256, 0, c->stream>>>(op, A, nA, B, nB, Y, n);
+  launch_k(binary_kernel, grid_for(c, n), 256, 0, c->stream, op, A, nA, B, nB, Y, n);
   return check_launch(c, "binary");
 }
 int di_binary_bcast(di_ctx_t h, int op, const float* A, const float* B, float* Y, const uint32_t cfg[20]) {
@@ -334,7 +350,7 @@ int di_binary_bcast(di_ctx_t h, int op, const float* A, const float* B, float* Y
   Cfg20 k;
   memcpy(k.v, cfg, sizeof k.v);
   if (!k.v[16]) return DI_OK;
-  binary_bcast_kernel<<<grid_for(c, k.v[16]), 256, 0, c->stream>>>(op, A, B, Y, k);
+  launch_k(binary_bcast_kernel, grid_for(c, k.v[16]), 256, 0, c->stream, op, A, B, Y, k);
   return check_launch(c, "binary_bcast");
 }
 int di_affine_bcast(di_ctx_t h, const float* A, const float* G, const float* Bt, float* Y, const uint32_t cfg[20]) {
@@ -343,28 +359,28 @@ int di_affine_bcast(di_ctx_t h, const float* A, const float* G, const float* Bt,
   Cfg20 k;
   memcpy(k.v, cfg, sizeof k.v);
   if (!k.v[16]) return DI_OK;
-  affine_bcast_kernel<<<grid_for(c, k.v[16]), 256, 0, c->stream>>>(A, G, Bt, Y, k);
+  launch_k(affine_bcast_kernel, grid_for(c, k.v[16]), 256, 0, c->stream, A, G, Bt, Y, k);
   return check_launch(c, "affine_bcast");
 }
 int di_softmax(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[2]) {
   Ctx* c = ctx_of(h);
   if (!c || !cfg || !cfg[0]) return DI_EINVAL;
   if (!cfg[1]) return DI_OK;
-  softmax_rows<<<(cfg[1] + 7) / 8, 256, 0, c->stream>>>(X, Y, cfg[0], cfg[1]);
+  launch_k(softmax_rows, (cfg[1] + 7) / 8, 256, 0, c->stream, X, Y, cfg[0], cfg[1]);
   return check_launch(c, "softmax");
 }
 int di_reduce_mean(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[2]) {
   Ctx* c = ctx_of(h);
   if (!c || !cfg || !cfg[0]) return DI_EINVAL;
   if (!cfg[1]) return DI_OK;
-  reduce_mean_rows<<<(cfg[1] + 7) / 8, 256, 0, c->stream>>>(X, Y, cfg[0], cfg[1]);
+  launch_k(reduce_mean_rows, (cfg[1] + 7) / 8, 256, 0, c->stream, X, Y, cfg[0], cfg[1]);
   return check_launch(c, "reduce_mean");
 }
 int di_resize_nearest(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[8]) {
   Ctx* c = ctx_of(h);
   if (!c || !cfg || !cfg[3] || !cfg[4]) return DI_EINVAL;
   if (!cfg[5]) return DI_OK;
-  resize_nearest_kernel<<<grid_for(c, cfg[5]), 256, 0, c->stream>>>(X, Y, cfg[1], cfg[2], cfg[3], cfg[4], cfg[5]);
+  launch_k(resize_nearest_kernel, grid_for(c, cfg[5]), 256, 0, c->stream, X, Y, cfg[1], cfg[2], cfg[3], cfg[4], cfg[5]);
   return check_launch(c, "resize_nearest");
 }
 int di_transpose(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[20]) {
@@ -373,14 +389,14 @@ int di_transpose(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[20]) {
   Cfg20 k;
   memcpy(k.v, cfg, sizeof k.v);
   if (!k.v[16]) return DI_OK;
-  transpose_kernel<<<grid_for(c, k.v[16]), 256, 0, c->stream>>>(X, Y, k);
+  launch_k(transpose_kernel, grid_for(c, k.v[16]), 256, 0, c->stream, X, Y, k);
   return check_launch(c, "transpose");
 }
 int di_pow_scalar(di_ctx_t h, const float* X, float* Y, float e, uint32_t n) {
   Ctx* c = ctx_of(h);
   if (!c) return DI_EINVAL;
   if (!n) return DI_OK;
-  pow_scalar_kernel<<<grid_for(c, n), 256, 0, c->stream>>>(X, Y, e, n);
+  launch_k(pow_scalar_kernel, grid_for(c, n), 256, 0, c->stream, X, Y, e, n);
   return check_launch(c, "pow_scalar");
 }
 int di_slice(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[20]) {
@@ -389,14 +405,14 @@ int di_slice(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[20]) {
   Cfg20 k;
   memcpy(k.v, cfg, sizeof k.v);
   if (!k.v[16]) return DI_OK;
-  slice_kernel<<<grid_for(c, k.v[16]), 256, 0, c->stream>>>(X, Y, k);
+  launch_k(slice_kernel, grid_for(c, k.v[16]), 256, 0, c->stream, X, Y, k);
   return check_launch(c, "slice");
 }
 int di_concat_copy(di_ctx_t h, const float* X, float* Y, const uint32_t cfg[4]) {
   Ctx* c = ctx_of(h);
   if (!c || !cfg || !cfg[0]) return DI_EINVAL;
   if (!cfg[3]) return DI_OK;
-  concat_copy_kernel<<<grid_for(c, cfg[3]), 256, 0, c->stream>>>(X, Y, cfg[0], cfg[1], cfg[2], cfg[3]);
+  launch_k(concat_copy_kernel, grid_for(c, cfg[3]), 256, 0, c->stream, X, Y, cfg[0], cfg[1], cfg[2], cfg[3]);
   return check_launch(c, "concat_copy");
 }
 int di_tembed(di_ctx_t h, const float* t, int B, const float* W1, const float* b1, const float* W2, const float* b2,

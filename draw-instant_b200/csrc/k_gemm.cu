@@ -49,7 +49,9 @@ struct GemmParams {
   int ldo, out_f32;
   int geglu;
   int vec_ok;  // 16-byte aligned rows for out / residual: vectorised epilogue
-  int splits;      // K splits (grid.z); > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
+  int b_early;     // weights are constant data: fetch the first B stages before the dependency wait
+  int splits;      // K splits; > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
+  int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
   int* err;
 };
@@ -62,7 +64,7 @@ template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
-  static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;
+  static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;  // ring + align + barriers
 };
 
 __device__ __forceinline__ void store_row32(void* out, size_t off, const float* v, int out_f32, bool bf16) {
@@ -124,29 +126,34 @@ __device__ __forceinline__ void store_one(void* dst, size_t off, float v, int is
   else static_cast<__half*>(dst)[off] = __float2half_rn(v);
 }
 
+// Persistent tile-scheduled kernel: grid = min(units, SMs), one CTA per SM.  A unit is one
+// (K split, 128-row M tile, BN-column N tile); CTA b processes units b, b + grid, ...  The smem ring
+// runs continuously across units, and the accumulator is double-buffered in TMEM (2 x BN columns)
+// so the epilogue of one unit overlaps the main loop of the next.
 template <int BN, int STAGES, bool BF16>
-__global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmSmem<BN, STAGES>;
   constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
-  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  constexpr uint32_t TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::B_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = empty + STAGES;  // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;      // [2] accumulator drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int nt = p.n_tiles, per_split = p.m_tiles * p.n_tiles;
+  const int units = per_split * p.splits;
   const int kper = (p.num_k + p.splits - 1) / p.splits;
-  const int kb0 = blockIdx.z * kper, kb1 = min(p.num_k, kb0 + kper);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    mbar_init(accum, 1);
+    for (int s = 0; s < 2; ++s) { mbar_init(&tfull[s], 1); mbar_init(&tempty[s], 128); }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -155,143 +162,205 @@ __global__ void __launch_bounds__(192, 2) gemm_tc_kernel(const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: let the next kernel be scheduled right away.  Everything before
+  // pdl_wait() below reads only constant data (tensor maps, weights), so it overlaps the previous
+  // kernel's tail; activations are read only after the wait.
+  pdl_trigger();
+
+  auto decode = [&](int u, int& m0, int& n0, int& sp, int& kb0, int& kb1) {
+    sp = u / per_split;
+    const int r = u - sp * per_split;
+    m0 = (r / nt) * BM;
+    n0 = (r % nt) * BN;
+    kb0 = sp * kper;
+    kb1 = min(p.num_k, kb0 + kper);
+  };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (elect_one()) {
       for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.tmA[i]);
       tma_prefetch_desc(&p.tmB);
-      int img = 0, y0 = 0;
-      if (p.mode != 0) { img = m0 / p.HWo; y0 = (m0 % p.HWo) / p.Wo; }
-      for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1, p.err, DEVERR_WAIT_TMA)) { *abort_flag = 1; break; }
-        mbar_arrive_expect_tx(&full[s], STAGE_TX);
-        uint8_t* dA = sA + s * S::A_BYTES;
-        if (p.mode == 0) {
-          if (kb < p.k_split) tma_load_2d(dA, &p.tmA[0], &full[s], kb * BK, m0);
-          else tma_load_2d(dA, &p.tmA[1], &full[s], (kb - p.k_split) * BK, m0);
-        } else {
-          const int tap = kb / p.cin_blocks, cb = kb % p.cin_blocks;
-          const int ky = tap / 3, kx = tap % 3;
-          if (p.mode == 1) {
-            const bool first = cb < p.k_split;
-            tma_load_4d(dA, &p.tmA[first ? 0 : 1], &full[s], (first ? cb : cb - p.k_split) * BK, kx - 1,
-                        y0 + ky - 1, img);
-          } else {
-            const int py = ky == 1 ? 0 : 1, px = kx == 1 ? 0 : 1;
-            tma_load_4d(dA, &p.tmA[py * 2 + px], &full[s], cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0), img);
-          }
+      // Weight tiles of the first ring stages are requested before the dependency wait (constant data).
+      int npre = 0;
+      {
+        int m0, n0, sp, kb0, kb1;
+        decode(blockIdx.x, m0, n0, sp, kb0, kb1);
+        npre = p.b_early ? min(STAGES, kb1 - kb0) : 0;
+        for (int i = 0; i < npre; ++i) {
+          mbar_arrive_expect_tx(&full[i], STAGE_TX);
+          tma_load_2d(sB + i * S::B_BYTES, &p.tmB, &full[i], (kb0 + i) * BK, n0);
         }
-        tma_load_2d(sB + s * S::B_BYTES, &p.tmB, &full[s], kb * BK, n0);
+      }
+      pdl_wait();
+      int it = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        int m0, n0, sp, kb0, kb1;
+        decode(u, m0, n0, sp, kb0, kb1);
+        int img = 0, y0 = 0;
+        if (p.mode != 0) { img = m0 / p.HWo; y0 = (m0 % p.HWo) / p.Wo; }
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          const bool pre = it < npre;  // B already requested, barrier already armed
+          if (!pre) {
+            if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1, p.err, DEVERR_WAIT_TMA)) { *abort_flag = 1; break; }
+            mbar_arrive_expect_tx(&full[s], STAGE_TX);
+          }
+          uint8_t* dA = sA + s * S::A_BYTES;
+          if (p.mode == 0) {
+            if (kb < p.k_split) tma_load_2d(dA, &p.tmA[0], &full[s], kb * BK, m0);
+            else tma_load_2d(dA, &p.tmA[1], &full[s], (kb - p.k_split) * BK, m0);
+          } else {
+            const int tap = kb / p.cin_blocks, cb = kb % p.cin_blocks;
+            const int ky = tap / 3, kx = tap % 3;
+            if (p.mode == 1) {
+              const bool first = cb < p.k_split;
+              tma_load_4d(dA, &p.tmA[first ? 0 : 1], &full[s], (first ? cb : cb - p.k_split) * BK, kx - 1,
+                          y0 + ky - 1, img);
+            } else {
+              const int py = ky == 1 ? 0 : 1, px = kx == 1 ? 0 : 1;
+              tma_load_4d(dA, &p.tmA[py * 2 + px], &full[s], cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0),
+                          img);
+            }
+          }
+          if (!pre) tma_load_2d(sB + s * S::B_BYTES, &p.tmB, &full[s], kb * BK, n0);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_f16(BM, BN, BF16);
-      for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (*abort_flag || !mbar_wait(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; break; }
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * S::A_BYTES), b0 = smem_u32(sB + s * S::B_BYTES);
-#pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(b0 + k * 32, 16, 1024);
-          umma_f16(tmem, ad, bd, idesc, (it | k) != 0 ? 1u : 0u);
+      int it = 0, lt = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
+        int m0, n0, sp, kb0, kb1;
+        decode(u, m0, n0, sp, kb0, kb1);
+        const int ab = lt & 1;
+        if (*abort_flag || !mbar_wait(&tempty[ab], ((lt >> 1) & 1) ^ 1, p.err, DEVERR_WAIT_MMA)) {
+          *abort_flag = 1;
+          umma_commit(&tfull[ab]);
+          break;
         }
-        umma_commit(&empty[s]);
+        tc_fence_after();
+        const uint32_t dt = tmem + ab * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (*abort_flag || !mbar_wait(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * S::A_BYTES), b0 = smem_u32(sB + s * S::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b0 + k * 32, 16, 1024);
+            umma_f16(dt, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&tfull[ab]);
+        if (!ok) break;
       }
-      umma_commit(accum);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();  // residual reads / output writes follow the previous kernel
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
-    const int m = m0 + row;
-    const bool ok = mbar_wait(accum, 0, p.err, DEVERR_WAIT_EPI);
-    tc_fence_after();
-    const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    if (p.splits > 1) {
-      // split-K: raw fp32 partial sums; splitk_reduce adds the splits and applies the epilogue
+    int lt = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
+      int m0, n0, sp, kb0, kb1;
+      decode(u, m0, n0, sp, kb0, kb1);
+      const int ab = lt & 1;
+      const int m = m0 + row;
+      const bool ok = mbar_wait(&tfull[ab], (lt >> 1) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
+      tc_fence_after();
+      const uint32_t trow = tmem + ab * BN + (static_cast<uint32_t>(q * 32) << 16);
+      if (p.splits > 1) {
+        // split-K: raw fp32 partial sums; splitk_reduce adds the splits and applies the epilogue
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(trow + c * 32, r);
-        tmem_wait_ld();
-        const int nb = n0 + c * 32;
-        if (!ok || m >= p.M || nb >= p.N) continue;
-        float* dst = p.partial + ((size_t)blockIdx.z * p.M + m) * p.N + nb;
-        if (nb + 32 <= p.N && (p.N & 3) == 0) {
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + c * 32, r);
+          tmem_wait_ld();
+          const int nb = n0 + c * 32;
+          if (!ok || m >= p.M || nb >= p.N) continue;
+          float* dst = p.partial + ((size_t)sp * p.M + m) * p.N + nb;
+          if (nb + 32 <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            reinterpret_cast<float4*>(dst)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-        } else {
-          for (int j = 0; j < 32 && nb + j < p.N; ++j) dst[j] = __uint_as_float(r[j]);
-        }
-      }
-    } else if (!p.geglu) {
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(trow + c * 32, r);
-        tmem_wait_ld();
-        const int nb = n0 + c * 32;
-        if (!ok || m >= p.M || nb >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const bool full_chunk = p.vec_ok && nb + 32 <= p.N;
-        if (full_chunk) {
-          if (p.bias) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
-          }
-          if (p.rowvec) {
-            const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.rowvec_ld + nb;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
-          }
-          if (p.residual) {
-            float rr[32];
-            load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += rr[j];
-          }
-          store_row32(p.out, (size_t)m * p.ldo + nb, v, p.out_f32, BF16);
-        } else {
-          for (int j = 0; j < 32 && nb + j < p.N; ++j) {
-            float x = v[j];
-            if (p.bias) x += p.bias[nb + j];
-            if (p.rowvec) x += p.rowvec[(size_t)(m / p.rowvec_div) * p.rowvec_ld + nb + j];
-            if (p.residual) x += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
-            store_one(p.out, (size_t)m * p.ldo + nb + j, x, p.out_f32, BF16);
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<float4*>(dst)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                              __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          } else {
+            for (int j = 0; j < 32 && nb + j < p.N; ++j) dst[j] = __uint_as_float(r[j]);
           }
         }
-      }
-    } else {
-      // GEGLU: accumulator columns [0,64) are value rows, [64,128) the matching gate rows of this tile.
+      } else if (!p.geglu) {
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t rv[32], rg[32];
-        tmem_ld32(trow + c * 32, rv);
-        tmem_ld32(trow + 64 + c * 32, rg);
-        tmem_wait_ld();
-        const int ob = blockIdx.x * 64 + c * 32;  // output column
-        if (!ok || m >= p.M || ob >= p.N / 2) continue;
-        float v[32];
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + c * 32, r);
+          tmem_wait_ld();
+          const int nb = n0 + c * 32;
+          if (!ok || m >= p.M || nb >= p.N) continue;
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float a = __uint_as_float(rv[j]), g = __uint_as_float(rg[j]);
-          if (p.bias) { a += __ldg(p.bias + n0 + c * 32 + j); g += __ldg(p.bias + n0 + 64 + c * 32 + j); }
-          v[j] = a * gelu_erf(g);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (p.vec_ok && nb + 32 <= p.N) {
+            if (p.bias) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
+            }
+            if (p.rowvec) {
+              const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.rowvec_ld + nb;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
+            }
+            if (p.residual) {
+              float rr[32];
+              load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += rr[j];
+            }
+            store_row32(p.out, (size_t)m * p.ldo + nb, v, p.out_f32, BF16);
+          } else {
+            for (int j = 0; j < 32 && nb + j < p.N; ++j) {
+              float x = v[j];
+              if (p.bias) x += p.bias[nb + j];
+              if (p.rowvec) x += p.rowvec[(size_t)(m / p.rowvec_div) * p.rowvec_ld + nb + j];
+              if (p.residual) x += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
+              store_one(p.out, (size_t)m * p.ldo + nb + j, x, p.out_f32, BF16);
+            }
+          }
         }
-        store_row32(p.out, (size_t)m * p.ldo + ob, v, p.out_f32, BF16);
+      } else {
+        // GEGLU: each 128 accumulator columns hold 64 value rows then the matching 64 gate rows.
+#pragma unroll 1
+        for (int g = 0; g < BN / 128; ++g) {
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t rv[32], rg[32];
+            tmem_ld32(trow + g * 128 + c * 32, rv);
+            tmem_ld32(trow + g * 128 + 64 + c * 32, rg);
+            tmem_wait_ld();
+            const int nv = n0 + g * 128 + c * 32;  // packed value column
+            const int ob = (n0 + g * 128) / 2 + c * 32;
+            if (!ok || m >= p.M || ob >= p.N / 2) continue;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float a = __uint_as_float(rv[j]), gt = __uint_as_float(rg[j]);
+              if (p.bias) { a += __ldg(p.bias + nv + j); gt += __ldg(p.bias + nv + 64 + j); }
+              v[j] = a * gelu_erf(gt);
+            }
+            store_row32(p.out, (size_t)m * p.ldo + ob, v, p.out_f32, BF16);
+          }
+        }
       }
+      tc_fence_before();
+      mbar_arrive(&tempty[ab]);
+      if (!ok) break;
     }
   }
 
@@ -313,16 +382,15 @@ int launch_variant(Ctx* c, const GemmParams& p) {
       return set_error(c, DI_ECUDA, "gemm: cudaFuncSetAttribute failed");
     attr_done |= 1u << (c->device & 31);
   }
-  const int n_tiles = p.geglu ? (p.N / BN) : (p.N + BN - 1) / BN;
-  dim3 grid(n_tiles, (p.M + BM - 1) / BM, p.splits);
-  kern<<<grid, 192, S::TOTAL, c->stream>>>(p);
+  const int units = p.m_tiles * p.n_tiles * p.splits;
+  launch_k(kern, std::min(units, c->num_sms), 192, S::TOTAL, c->stream, p);
   return check_launch(c, "gemm_tc_kernel");
 }
-
 // Sums the split-K partials and applies the epilogue (bias, per-image row vector, residual or GEGLU).
 __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
                               const float* __restrict__ rowvec, int rowvec_div, int rowvec_ld, const void* residual,
                               int ldr, int res_f32, void* out, int ldo, int out_f32, int geglu, int bf16) {
+  pdl_begin();
   const size_t slice = (size_t)M * N;
   const int NO = geglu ? N / 2 : N;
   if (!geglu && (N & 3) == 0 && (ldo & 3) == 0 && (!residual || (ldr & 3) == 0)) {
@@ -371,22 +439,52 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
 
 }  // namespace
 
-// Tiling: N tile (64 / 128) and K splits.  Large grids: 128-wide tiles.  Few tiles with a long K on a
-// small M (the low-resolution levels at batch 1, where the weights stream from HBM once per step):
-// 128-wide tiles split along K so that about two CTAs per SM stream disjoint weight slices.  Few tiles
-// with a short K: 64-wide tiles for more CTAs.
+// Tiling: N tile width (128 / 160 / 192 / 256) and K splits from a cost model in units of one 128-wide
+// K block of MMA work per SM: units = M tiles x N tiles x splits run on min(units, SMs) persistent CTAs;
+// cost = rounds x (K blocks per unit x BN/128 + per-unit overhead) + split-K reduce (partial-sum traffic
+// and one launch).  GEGLU needs BN in {128, 256} (value/gate rows packed per 128 columns).
 void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits) {
-  const int tiles128 = ((N + 127) / 128) * ((M + 127) / 128);
-  *splits = 1;
-  *bn = 128;
-  if (tiles128 >= c->num_sms) return;
-  // at most two resident CTAs per SM: keep tiles x splits within one wave of 2 * SMs
-  int s = std::min(num_k / 4, (2 * c->num_sms) / tiles128);
-  if (num_k >= 16 && s >= 2) {
-    const int per = (num_k + s - 1) / s;
+  static const int cands[4] = {128, 160, 192, 256};
+  const int mt = (M + BM - 1) / BM;
+  // Tuning / diagnostics override: DI_GEMM_TILING="bn,splits" forces the tiling of every GEMM.
+  static int forced_bn = -1, forced_s = 1;
+  if (forced_bn < 0) {
+    forced_bn = 0;
+    if (const char* e = getenv("DI_GEMM_TILING")) {
+      int b = 0, s = 1;
+      if (sscanf(e, "%d,%d", &b, &s) >= 1 && (b == 128 || b == 160 || b == 192 || b == 256)) {
+        forced_bn = b;
+        forced_s = std::max(1, s);
+      }
+    }
+  }
+  if (forced_bn && (!geglu || forced_bn % 128 == 0)) {
+    *bn = forced_bn;
+    const int per = (num_k + forced_s - 1) / forced_s;
     *splits = (num_k + per - 1) / per;
-  } else if (!geglu && N % 64 == 0) {
-    *bn = 64;
+    return;
+  }
+  double best = 1e30;
+  *bn = 128;
+  *splits = 1;
+  for (int bc : cands) {
+    if (geglu && (bc % 128 || N % bc)) continue;
+    const int nt = geglu ? N / bc : (N + bc - 1) / bc;
+    const int smax = std::max(1, std::min(16, num_k / 4));
+    for (int s = 1; s <= smax; ++s) {
+      const int per = (num_k + s - 1) / s;
+      const int seff = (num_k + per - 1) / per;
+      if (seff != s) continue;
+      const long long units = (long long)mt * nt * s;
+      const long long rounds = (units + c->num_sms - 1) / c->num_sms;
+      double cost = (double)rounds * (per * (bc / 128.0) + 3.0) + 4.0;
+      if (s > 1) cost += 15.0 + (double)M * N * s * 8.0 / 6.4e12 / 130e-9;
+      if (cost < best - 1e-9 || (cost < best + 1e-9 && bc > *bn)) {
+        best = cost;
+        *bn = bc;
+        *splits = s;
+      }
+    }
   }
 }
 
@@ -396,36 +494,34 @@ int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
   return s > 1 ? 2 : 1;
 }
 
-// Chooses the N tile: 128 by default; 64 when the grid would leave most SMs idle.
-int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int force_bn, int splits, void* splitk_ws) {
+static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16) {
+  switch (bn) {
+    case 256: return bf16 ? launch_variant<256, 4, true>(c, p) : launch_variant<256, 4, false>(c, p);
+    case 192: return bf16 ? launch_variant<192, 5, true>(c, p) : launch_variant<192, 5, false>(c, p);
+    case 160: return bf16 ? launch_variant<160, 5, true>(c, p) : launch_variant<160, 5, false>(c, p);
+    default: return bf16 ? launch_variant<128, 6, true>(c, p) : launch_variant<128, 6, false>(c, p);
+  }
+}
+
+int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, void* splitk_ws) {
   p.err = c->d_err;
+  p.b_early = c->weights_const ? 1 : 0;
   p.splits = std::max(1, splits);
+  p.m_tiles = (p.M + BM - 1) / BM;
+  p.n_tiles = p.geglu ? p.N / bn : (p.N + bn - 1) / bn;
   if (p.splits > 1) {
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
     p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
     if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
-    const int bnv = force_bn;
-    int r = bnv == 64 ? (bf16 ? launch_variant<64, 4, true>(c, p) : launch_variant<64, 4, false>(c, p))
-                      : (bf16 ? launch_variant<128, 3, true>(c, p) : launch_variant<128, 3, false>(c, p));
+    int r = dispatch_variant(c, p, bn, bf16);
     if (r) return r;
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
-    splitk_reduce<<<blocks, 256, 0, c->stream>>>(p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,
-                                                 p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32,
-                                                 p.geglu, bf16);
+    launch_k(splitk_reduce, blocks, 256, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,
+             p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32, p.geglu, bf16);
     return check_launch(c, "splitk_reduce");
   }
-  int bn = force_bn;
-  if (!bn) {
-    if (p.geglu) bn = 128;
-    else {
-      const long long tiles128 = (long long)((p.N + 127) / 128) * ((p.M + 127) / 128);
-      bn = (tiles128 < c->num_sms && p.N % 64 == 0) ? 64 : 128;
-    }
-  }
-  // ~97 KB of stages per CTA so two CTAs share an SM: one's epilogue overlaps the other's main loop.
-  if (bn == 64) return bf16 ? launch_variant<64, 4, true>(c, p) : launch_variant<64, 4, false>(c, p);
-  return bf16 ? launch_variant<128, 3, true>(c, p) : launch_variant<128, 3, false>(c, p);
+  return dispatch_variant(c, p, bn, bf16);
 }
 
 static CUtensorMapDataType tdt(int dtype) {
@@ -578,6 +674,7 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
 
 // Weight repack: [Co][Ci][3][3] fp32 -> [Co][3][3][Ci] fp16/bf16.
 __global__ void pack_conv3x3_kernel(const float* __restrict__ w, int Co, int Ci, void* out, int bf16) {
+  pdl_begin();
   const size_t n = (size_t)Co * Ci * 9;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const int ci = i % Ci;
@@ -590,7 +687,7 @@ __global__ void pack_conv3x3_kernel(const float* __restrict__ w, int Co, int Ci,
 }
 
 int pack_conv3x3(Ctx* c, int dtype, const float* w, int Co, int Ci, void* out) {
-  pack_conv3x3_kernel<<<std::min<size_t>(((size_t)Co * Ci * 9 + 255) / 256, 4096), 256, 0, c->stream>>>(
+  launch_k(pack_conv3x3_kernel, std::min<size_t>(((size_t)Co * Ci * 9 + 255) / 256, 4096), 256, 0, c->stream, 
       w, Co, Ci, out, dtype == DI_BF16);
   return check_launch(c, "pack_conv3x3");
 }

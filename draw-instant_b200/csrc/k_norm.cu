@@ -62,6 +62,7 @@ __device__ __forceinline__ void store8(T* p, const float* f) {
 template <typename T>
 __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2, int HW,
                                 int chunk_pixels, int G, float2* __restrict__ partial) {
+  pdl_begin();
   extern __shared__ float sh[];
   const int C = C1 + C2, V = C / 8, R = blockDim.x / V;
   const int n = blockIdx.y, chunk = blockIdx.x, nchunks = gridDim.x;
@@ -115,6 +116,7 @@ template <typename Tin, typename Tout>
 __global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __restrict__ x2, int C2, int HW, int G,
                               const float2* __restrict__ partial, int nchunks, const float* __restrict__ gamma,
                               const float* __restrict__ beta, float eps, int silu, Tout* __restrict__ y) {
+  pdl_begin();
   __shared__ float s_mean[128], s_rstd[128];
   __shared__ float2 s_part[256];
   const int C = C1 + C2, V = C / 8, cpg = C / G;
@@ -165,6 +167,7 @@ __global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __r
 // ---------------------------------------------------------------------------------------------
 __global__ void gn_nchw_partial(const float* __restrict__ x, int G, size_t gsize, int nchunks,
                                 float2* __restrict__ partial) {
+  pdl_begin();
   const int chunk = blockIdx.x, g = blockIdx.y, n = blockIdx.z;
   const size_t base = ((size_t)n * G + g) * gsize;
   const size_t per = (gsize + nchunks - 1) / nchunks;
@@ -189,6 +192,7 @@ __global__ void gn_nchw_apply(const float* __restrict__ x, int C, int G, int HW,
                               const float2* __restrict__ partial, const float* __restrict__ gamma,
                               const float* __restrict__ beta, float eps, int silu, int clamp, size_t total,
                               float* __restrict__ y) {
+  pdl_begin();
   const int cpg = C / G;
   const float cnt = (float)cpg * (float)HW;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -213,6 +217,7 @@ __global__ void gn_nchw_apply(const float* __restrict__ x, int C, int G, int HW,
 template <typename Tin, typename Tout>
 __global__ void layer_norm_rows(const Tin* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
                                 Tout* __restrict__ y, int rows, int D, float eps) {
+  pdl_begin();
   const int warps = blockDim.x / 32;
   const int row = blockIdx.x * warps + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -249,10 +254,10 @@ static int gn_nhwc_impl(Ctx* c, const Tin* x1, int C1, const Tin* x2, int C2, in
     if (!partial) return set_error(c, DI_ENOMEM, "group_norm_nhwc: workspace");
   }
   const size_t shm = sizeof(float) * 2 * R * C;
-  gn_nhwc_partial<Tin><<<dim3(chunks, N), threads, shm, c->stream>>>(x1, C1, x2, C2, HW, chunk_pixels, G, partial);
+  launch_k(gn_nhwc_partial<Tin>, dim3(chunks, N), threads, shm, c->stream, x1, C1, x2, C2, HW, chunk_pixels, G, partial);
   const size_t work = (size_t)HW * V;
   const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)std::max(1, 4 * c->num_sms / std::max(1, N)));
-  gn_nhwc_apply<Tin, Tout><<<dim3(blocks, N), 256, 0, c->stream>>>(x1, C1, x2, C2, HW, G, partial, chunks, gamma,
+  launch_k(gn_nhwc_apply<Tin, Tout>, dim3(blocks, N), 256, 0, c->stream, x1, C1, x2, C2, HW, G, partial, chunks, gamma,
                                                                     beta, eps, silu, y);
   return check_launch(c, "group_norm_nhwc");
 }
@@ -283,10 +288,10 @@ int group_norm_nchw(Ctx* c, const float* x, const float* g, const float* b, floa
   int chunks = (int)std::max<size_t>(1, std::min<size_t>((gsize + 2047) / 2048, (size_t)std::max(1, target / (N * G))));
   float2* partial = static_cast<float2*>(workspace(c, sizeof(float2) * (size_t)N * G * chunks, 0));
   if (!partial) return set_error(c, DI_ENOMEM, "group_norm: workspace");
-  gn_nchw_partial<<<dim3(chunks, G, N), 256, 0, c->stream>>>(x, G, gsize, chunks, partial);
+  launch_k(gn_nchw_partial, dim3(chunks, G, N), 256, 0, c->stream, x, G, gsize, chunks, partial);
   const size_t total = (size_t)N * C * HW;
   const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
-  gn_nchw_apply<<<blocks, 256, 0, c->stream>>>(x, C, G, HW, chunks, partial, g, b, eps, silu, clamp, total, y);
+  launch_k(gn_nchw_apply, blocks, 256, 0, c->stream, x, C, G, HW, chunks, partial, g, b, eps, silu, clamp, total, y);
   return check_launch(c, "group_norm_nchw");
 }
 
@@ -294,7 +299,7 @@ int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* 
                int D, float eps) {
   const int blocks = (rows + 7) / 8;
 #define LN_CASE(TI, TO)                                                                                         \
-  layer_norm_rows<TI, TO><<<blocks, 256, 0, c->stream>>>(static_cast<const TI*>(x), g, b, static_cast<TO*>(y), \
+  launch_k(layer_norm_rows<TI, TO>, blocks, 256, 0, c->stream, static_cast<const TI*>(x), g, b, static_cast<TO*>(y), \
                                                          rows, D, eps);                                         \
   return check_launch(c, "layer_norm")
   if (in_dtype == DI_F32 && out_dtype == DI_F32) { LN_CASE(float, float); }

@@ -21,6 +21,7 @@ inline int pad64(int k) { return (k + 63) / 64 * 64; }
 // im2col for one image: col[p][kd] (fp16, row = output pixel, K = ci*K*K + ky*K + kx padded to ldk).
 __global__ void im2col_kernel(const float* __restrict__ x, int Ci, int H, int W, int K, int S, int PAD, int Ho,
                               int Wo, int ldk, __half* __restrict__ col) {
+  pdl_begin();
   const int KD = Ci * K * K;
   const size_t total = (size_t)Ho * Wo * ldk;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -39,6 +40,7 @@ __global__ void im2col_kernel(const float* __restrict__ x, int Ci, int H, int W,
 
 // y[co][p] = t[p][co] (pixel-major GEMM output -> NCHW)
 __global__ void pm_to_cm_kernel(const float* __restrict__ t, int P, int Co, float* __restrict__ y) {
+  pdl_begin();
   const size_t total = (size_t)P * Co;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int p = i % P, co = i / P;
@@ -113,12 +115,12 @@ int di_conv(di_ctx_t h, const float* X, const float* W, const float* bias, float
   if (r) return r;
   const int blocks = 8 * c->num_sms;
   for (uint32_t n = 0; n < n_batch; ++n) {
-    im2col_kernel<<<blocks, 256, 0, c->stream>>>(X + (size_t)n * Ci * H * Wd, Ci, H, Wd, K, S, PAD, Ho, Wo, Kp, col);
+    launch_k(im2col_kernel, blocks, 256, 0, c->stream, X + (size_t)n * Ci * H * Wd, Ci, H, Wd, K, S, PAD, Ho, Wo, Kp, col);
     r = check_launch(c, "im2col");
     if (r) return r;
     r = gemm_linear(c, DI_F16, col, Kp, nullptr, P, Kp, w, Co, bias, nullptr, 0, t, 1, 0, nullptr, 1);
     if (r) return r;
-    pm_to_cm_kernel<<<blocks, 256, 0, c->stream>>>(t, P, Co, Y + (size_t)n * Co * P);
+    launch_k(pm_to_cm_kernel, blocks, 256, 0, c->stream, t, P, Co, Y + (size_t)n * Co * P);
     r = check_launch(c, "conv_out_layout");
     if (r) return r;
   }

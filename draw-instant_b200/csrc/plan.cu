@@ -106,6 +106,7 @@ void synth_normal(uint64_t seed, const char* name, size_t n, float mean, float s
 namespace {
 
 __global__ void latent_in_kernel(const float* __restrict__ x, __half* __restrict__ y, int N, int C, int HW, int Cp) {
+  pdl_begin();
   const size_t total = (size_t)N * HW * Cp;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int c = i % Cp;
@@ -116,6 +117,7 @@ __global__ void latent_in_kernel(const float* __restrict__ x, __half* __restrict
   }
 }
 __global__ void latent_out_kernel(const __half* __restrict__ x, int Cp, float* __restrict__ y, int N, int C, int HW) {
+  pdl_begin();
   const size_t total = (size_t)N * C * HW;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int p = i % HW;
@@ -127,6 +129,7 @@ __global__ void latent_out_kernel(const __half* __restrict__ x, int Cp, float* _
 }
 // Nearest 2x upsample, NHWC, 16-byte vectors (index math of wgsl-ops.js:921-943 with W_out = 2 W_in).
 __global__ void upsample2_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, int N, int H, int W, int Cv) {
+  pdl_begin();
   const size_t total = (size_t)N * 4 * H * W * Cv;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int v = i % Cv;
@@ -139,6 +142,7 @@ __global__ void upsample2_kernel(const uint4* __restrict__ x, uint4* __restrict_
   }
 }
 __global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+  pdl_begin();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     y[i] = __float2half_rn(x[i]);
 }
@@ -275,7 +279,15 @@ struct Plan {
   std::vector<OpInfo> info;
 
   void record(std::function<int()> f, int kind = 3, double flops = 0, double bytes = 0, int kernels = 1) {
-    ops.push_back(std::move(f));
+    // A plan's weights are written once at build time (and synchronised), so its GEMMs may fetch
+    // weight tiles before the programmatic-dependency wait.
+    Ctx* cc = c;
+    ops.push_back([cc, f = std::move(f)] {
+      cc->weights_const = true;
+      const int r = f();
+      cc->weights_const = false;
+      return r;
+    });
     info.push_back({kind, flops, bytes, kernels});
     launches += kernels;
   }
@@ -494,7 +506,7 @@ struct Plan {
     const Act xx = x;
     record([=] {
       const size_t total = (size_t)xx.N * 4 * xx.H * xx.W * (xx.C / 8);
-      upsample2_kernel<<<(int)std::min<size_t>((total + 255) / 256, 16 * cc->num_sms), 256, 0, cc->stream>>>(
+      launch_k(upsample2_kernel, (int)std::min<size_t>((total + 255) / 256, 16 * cc->num_sms), 256, 0, cc->stream,
           static_cast<const uint4*>(xx.p), static_cast<uint4*>(y.p), xx.N, xx.H, xx.W, xx.C / 8);
       return check_launch(cc, "upsample2");
     }, 3, 0, 5.0 * x.bytes());
@@ -735,7 +747,7 @@ static int build_unet(UNetPlan* u) {
     const float* src = u->ctx32;
     const size_t n = (size_t)B * Sk * 1024;
     P.record([=] {
-      f32_to_f16_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream>>>(src, ctx16, n);
+      launch_k(f32_to_f16_kernel, (int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream, src, ctx16, n);
       return check_launch(cc, "ctx_to_f16");
     }, 3, 0, 6.0 * n);
   }
@@ -747,7 +759,7 @@ static int build_unet(UNetPlan* u) {
     void* dst = lat.p;
     P.record([=] {
       const size_t n = (size_t)B * H * W * 64;
-      latent_in_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, cc->stream>>>(
+      launch_k(latent_in_kernel, (int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, cc->stream, 
           src, static_cast<__half*>(dst), B, 4, H * W, 64);
       return check_launch(cc, "latent_in");
     }, 3, 0, (double)B * H * W * (16 + 128));
@@ -833,7 +845,7 @@ static int build_unet(UNetPlan* u) {
     float* out = u->out;
     P.record([=] {
       const size_t n = (size_t)B * 4 * H * W;
-      latent_out_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream>>>(
+      launch_k(latent_out_kernel, (int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream, 
           static_cast<const __half*>(y16), 16, out, B, 4, H * W);
       return check_launch(cc, "latent_out");
     }, 3, 0, (double)B * H * W * (32 + 16));
