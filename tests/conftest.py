@@ -66,3 +66,17 @@ def cosine(got, ref):
     a = np.asarray(got, np.float64).ravel()
     b = np.asarray(ref, np.float64).ravel()
     return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
+
+
+GOLDEN = ROOT / "tests" / "golden"
+
+
+def golden_cases():
+    """The 27 wgsl-ops-test.js known-answer cases: [(name, tol, {array name: array})]."""
+    z = np.load(GOLDEN / "wgsl_ops_cases.npz")
+    out = []
+    for name in z["names"]:
+        name = str(name)
+        arrays = {k.split("|", 1)[1]: z[k] for k in z.files if k.startswith(name + "|")}
+        out.append((name, float(arrays.pop("tol")[0]), arrays))
+    return out
