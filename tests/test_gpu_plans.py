@@ -64,7 +64,7 @@ def test_transformer_block_config2(ctx, dib, oracle):
     assert cosine(got, ref) > 0.9999
 
 
-@pytest.mark.parametrize("B,H,W", [(1, 8, 8), (2, 16, 16)])
+@pytest.mark.parametrize("B,H,W", [(1, 8, 8), (2, 16, 16), (1, 64, 64)])
 def test_unet_config4_small(ctx, dib, oracle, B, H, W):
     """Config 4 architecture at small latents (the reference's own U-Net check runs an 8x8 latent,
     unet-wgsl-test.html:84-208): cosine >= 0.999 and max-rel-err <= 1e-2 on the noise prediction."""
