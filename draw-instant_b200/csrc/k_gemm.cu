@@ -34,6 +34,7 @@ Ctx* ctx_of(di_ctx_t h);
 struct GemmParams {
   CUtensorMap tmA[4];
   CUtensorMap tmB;
+  int staged;       // epilogue stores through the shared-memory staging slab (16-byte aligned rows)
   int mode;        // 0 linear, 1 conv s1, 2 conv s2
   int M, N;        // output rows, accumulator columns (geglu: 2F packed columns)
   int num_k;       // K blocks of 64
@@ -54,17 +55,28 @@ struct GemmParams {
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
   int* err;
+  unsigned long long* trace;  // diagnostics: kTracePoints %globaltimer stamps per CTA, or null
 };
+
+// Diagnostics: per-CTA timeline points of the first work unit (di_debug_gemm_trace).
+constexpr int kTracePoints = 16;
+static unsigned long long* g_trace = nullptr;
+static int g_trace_ctas = 0;
 
 namespace {
 
 constexpr int BM = 128, BK = 64;
+// Warps: 0 = TMA producer, 1 = MMA issuer, 2 .. 2 + kEpiWarps - 1 = epilogue.  Two epilogue warps share
+// each TMEM lane quarter (a warp may only read lanes 32 * (warp % 4) ..), splitting the column chunks.
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
-  static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + 256;  // ring + align + barriers
+  static constexpr uint32_t EPI_BYTES = kEpiWarps * 4096;  // one 32 x 128 B staging slab per epilogue warp
+  static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + 256;  // + align + barriers
 };
 
 __device__ __forceinline__ void store_row32(void* out, size_t off, const float* v, int out_f32, bool bf16) {
@@ -131,7 +143,7 @@ __device__ __forceinline__ void store_one(void* dst, size_t off, float v, int is
 // runs continuously across units, and the accumulator is double-buffered in TMEM (2 x BN columns)
 // so the epilogue of one unit overlaps the main loop of the next.
 template <int BN, int STAGES, bool BF16>
-__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmSmem<BN, STAGES>;
   constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
   constexpr uint32_t TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
@@ -139,7 +151,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::B_BYTES);
+  uint8_t* sEpi = sB + STAGES * S::B_BYTES;  // 1024-aligned: A and B stage sizes are multiples of 1 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + S::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;  // [2] accumulator ready
   uint64_t* tempty = tfull + 2;      // [2] accumulator drained by the epilogue
@@ -147,13 +160,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  unsigned long long* tr = p.trace ? p.trace + (size_t)blockIdx.x * kTracePoints : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer();
   const int nt = p.n_tiles, per_split = p.m_tiles * p.n_tiles;
   const int units = per_split * p.splits;
   const int kper = (p.num_k + p.splits - 1) / p.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&tfull[s], 1); mbar_init(&tempty[s], 128); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&tfull[s], 1); mbar_init(&tempty[s], 32 * kEpiWarps); }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -162,6 +177,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tr && threadIdx.x == 0) tr[1] = globaltimer();
   // Programmatic dependent launch: let the next kernel be scheduled right away.  Everything before
   // pdl_wait() below reads only constant data (tensor maps, weights), so it overlaps the previous
   // kernel's tail; activations are read only after the wait.
@@ -193,6 +209,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         }
       }
       pdl_wait();
+      if (tr) tr[2] = globaltimer();
       int it = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int m0, n0, sp, kb0, kb1;
@@ -249,6 +266,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (*abort_flag || !mbar_wait(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; ok = false; break; }
+          if (tr && lt == 0 && kb == kb0) tr[3] = globaltimer();
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * S::A_BYTES), b0 = smem_u32(sB + s * S::B_BYTES);
 #pragma unroll
@@ -260,116 +278,202 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           umma_commit(&empty[s]);
         }
         umma_commit(&tfull[ab]);
+        if (tr && lt == 0) tr[4] = globaltimer();
         if (!ok) break;
       }
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    // Per 32-column chunk: tcgen05.ld of this warp's 32 accumulator rows, bias / row vector / residual /
+    // GEGLU in registers, then (staged) the 32x32 tile goes through a swizzled shared-memory slab and is
+    // written back with whole-row-segment (coalesced) stores, or else it is stored row by row.
     pdl_wait();  // residual reads / output writes follow the previous kernel
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
+    const int half = (warp - 2) / 4;  // which alternate column chunks this warp handles
+    uint8_t* stg = sEpi + (warp - 2) * 4096;
     int lt = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
       int m0, n0, sp, kb0, kb1;
       decode(u, m0, n0, sp, kb0, kb1);
       const int ab = lt & 1;
       const int m = m0 + row;
-      const bool ok = mbar_wait(&tfull[ab], (lt >> 1) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
+      const bool okw = mbar_wait(&tfull[ab], (lt >> 1) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
+      const bool ok = __all_sync(0xffffffffu, okw);
+      if (tr && lt == 0 && threadIdx.x == 64) tr[5] = globaltimer();
       tc_fence_after();
       const uint32_t trow = tmem + ab * BN + (static_cast<uint32_t>(q * 32) << 16);
-      if (p.splits > 1) {
-        // split-K: raw fp32 partial sums; splitk_reduce adds the splits and applies the epilogue
+      const bool split = p.splits > 1;
+      const bool gg = p.geglu && !split;  // split-K stores raw packed partials; the reduce applies GEGLU
+      const int nchunks = gg ? BN / 64 : BN / 32;
+      const int n_out = gg ? p.N / 2 : p.N;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < nchunks; c += kEpiWarps / 4) {
+        float v[32];
+        int nb;  // first output column of the chunk
+        {
           uint32_t r[32];
-          tmem_ld32(trow + c * 32, r);
-          tmem_wait_ld();
-          const int nb = n0 + c * 32;
-          if (!ok || m >= p.M || nb >= p.N) continue;
-          float* dst = p.partial + ((size_t)sp * p.M + m) * p.N + nb;
-          if (nb + 32 <= p.N && (p.N & 3) == 0) {
+          if (gg) {
+            // each 128 accumulator columns hold 64 value rows then the matching 64 gate rows
+            const int g = c >> 1, h = c & 1;
+            uint32_t rg[32];
+            tmem_ld32(trow + g * 128 + h * 32, r);
+            tmem_ld32(trow + g * 128 + 64 + h * 32, rg);
+            tmem_wait_ld();
+            const int nv = n0 + g * 128 + h * 32;  // packed value column
+            nb = (n0 + g * 128) / 2 + h * 32;
+            if (nb < n_out) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float a = __uint_as_float(r[j]), gt = __uint_as_float(rg[j]);
+                if (p.bias) { a += __ldg(p.bias + nv + j); gt += __ldg(p.bias + nv + 64 + j); }
+                v[j] = a * gelu_erf(gt);
+              }
+            }
+          } else {
+            if (tr && lt == 0 && threadIdx.x == 64 && c < 2) tr[8 + 2 * c] = globaltimer();
+            tmem_ld32(trow + c * 32, r);
+            tmem_wait_ld();
+            if (tr && lt == 0 && threadIdx.x == 64 && c < 2) tr[9 + 2 * c] = globaltimer();
+            nb = n0 + c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (!split && nb < n_out && m < p.M) {
+              const bool full = nb + 32 <= n_out;
+              if (p.bias) {
+                if (full) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (nb + j < n_out) v[j] += p.bias[nb + j];
+                }
+              }
+              if (p.rowvec) {
+                const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.rowvec_ld + nb;
+                if (full) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (nb + j < n_out) v[j] += rv[j];
+                }
+              }
+              if (p.residual) {
+                if (full && p.vec_ok) {
+                  float rr[32];
+                  load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += rr[j];
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (nb + j < n_out) v[j] += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
+                }
+              }
+            }
+          }
+        }
+        if (!ok || nb >= n_out) continue;  // warp-uniform
+        if (p.staged) {
+          // The warp's 32 x 32 tile goes through a swizzled staging slab (conflict-free writes of one row
+          // per lane), then is read back so that each store instruction writes whole 64/128-byte row
+          // segments of 8 or 4 rows (coalesced), instead of 32 rows 16 bytes at a time.
+          __syncwarp();  // the previous chunk's read-back is done
+          if (split || p.out_f32) {
+            // 32 fp32 per row = 128 B; 16-byte chunk j of row r at j ^ (r & 7)
+            float4* rp = reinterpret_cast<float4*>(stg + lane * 128);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              reinterpret_cast<float4*>(dst)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                              __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+              rp[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           } else {
-            for (int j = 0; j < 32 && nb + j < p.N; ++j) dst[j] = __uint_as_float(r[j]);
+            // 32 x 16-bit per row = 64 B; 16-byte chunk j of row r at j ^ ((r >> 1) & 3)
+            uint4* rp = reinterpret_cast<uint4*>(stg + lane * 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t w[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float x0 = v[8 * j + 2 * k], x1 = v[8 * j + 2 * k + 1];
+                if (BF16) {
+                  __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+                  w[k] = *reinterpret_cast<uint32_t*>(&h2);
+                } else {
+                  __half2 h2 = __floats2half2_rn(x0, x1);
+                  w[k] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+              }
+              rp[j ^ ((lane >> 1) & 3)] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
           }
-        }
-      } else if (!p.geglu) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(trow + c * 32, r);
-          tmem_wait_ld();
-          const int nb = n0 + c * 32;
-          if (!ok || m >= p.M || nb >= p.N) continue;
-          float v[32];
+          __syncwarp();
+          const int mrow0 = m0 + q * 32;
+          if (split || p.out_f32) {
+            float* base = split ? p.partial + (size_t)sp * p.M * p.N : static_cast<float*>(p.out);
+            const int ld = split ? p.N : p.ldo;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (p.vec_ok && nb + 32 <= p.N) {
-            if (p.bias) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
+            for (int i = 0; i < 8; ++i) {
+              const int r = i * 4 + (lane >> 3), ch = lane & 7;
+              const float4 val = reinterpret_cast<const float4*>(stg + r * 128)[ch ^ (r & 7)];
+              const int mm = mrow0 + r, col = nb + ch * 4;
+              if (mm < p.M && col < n_out) {
+                float* d = base + (size_t)mm * ld + col;
+                if (col + 4 <= n_out) {
+                  *reinterpret_cast<float4*>(d) = val;
+                } else {
+                  const float t[4] = {val.x, val.y, val.z, val.w};
+                  for (int k = 0; k < 4 && col + k < n_out; ++k) d[k] = t[k];
+                }
+              }
             }
-            if (p.rowvec) {
-              const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.rowvec_ld + nb;
+          } else {
+            uint16_t* base = static_cast<uint16_t*>(p.out);
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
+            for (int i = 0; i < 4; ++i) {
+              const int r = i * 8 + (lane >> 2), ch = lane & 3;
+              const uint4 val = reinterpret_cast<const uint4*>(stg + r * 64)[ch ^ ((r >> 1) & 3)];
+              const int mm = mrow0 + r, col = nb + ch * 8;
+              if (mm < p.M && col < n_out) {
+                uint16_t* d = base + (size_t)mm * p.ldo + col;
+                if (col + 8 <= n_out) {
+                  *reinterpret_cast<uint4*>(d) = val;
+                } else {
+                  const uint32_t t[4] = {val.x, val.y, val.z, val.w};
+                  for (int k = 0; k < 8 && col + k < n_out; ++k) d[k] = static_cast<uint16_t>(t[k >> 1] >> (16 * (k & 1)));
+                }
+              }
             }
-            if (p.residual) {
-              float rr[32];
-              load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
+          }
+        } else if (m < p.M) {
+          if (split) {
+            float* dst = p.partial + ((size_t)sp * p.M + m) * p.N + nb;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += rr[j];
-            }
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < p.N) dst[j] = v[j];
+          } else if (p.vec_ok && nb + 32 <= n_out) {
             store_row32(p.out, (size_t)m * p.ldo + nb, v, p.out_f32, BF16);
           } else {
-            for (int j = 0; j < 32 && nb + j < p.N; ++j) {
-              float x = v[j];
-              if (p.bias) x += p.bias[nb + j];
-              if (p.rowvec) x += p.rowvec[(size_t)(m / p.rowvec_div) * p.rowvec_ld + nb + j];
-              if (p.residual) x += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
-              store_one(p.out, (size_t)m * p.ldo + nb + j, x, p.out_f32, BF16);
-            }
-          }
-        }
-      } else {
-        // GEGLU: each 128 accumulator columns hold 64 value rows then the matching 64 gate rows.
-#pragma unroll 1
-        for (int g = 0; g < BN / 128; ++g) {
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t rv[32], rg[32];
-            tmem_ld32(trow + g * 128 + c * 32, rv);
-            tmem_ld32(trow + g * 128 + 64 + c * 32, rg);
-            tmem_wait_ld();
-            const int nv = n0 + g * 128 + c * 32;  // packed value column
-            const int ob = (n0 + g * 128) / 2 + c * 32;
-            if (!ok || m >= p.M || ob >= p.N / 2) continue;
-            float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float a = __uint_as_float(rv[j]), gt = __uint_as_float(rg[j]);
-              if (p.bias) { a += __ldg(p.bias + nv + j); gt += __ldg(p.bias + nv + 64 + j); }
-              v[j] = a * gelu_erf(gt);
-            }
-            store_row32(p.out, (size_t)m * p.ldo + ob, v, p.out_f32, BF16);
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < n_out) store_one(p.out, (size_t)m * p.ldo + nb + j, v[j], p.out_f32, BF16);
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&tempty[ab]);
+      if (tr && lt == 0 && threadIdx.x == 64) tr[6] = globaltimer();
       if (!ok) break;
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+  if (tr && threadIdx.x == 0) tr[7] = globaltimer();
 }
 
 template <int BN, int STAGES, bool BF16>
@@ -383,7 +487,10 @@ int launch_variant(Ctx* c, const GemmParams& p) {
     attr_done |= 1u << (c->device & 31);
   }
   const int units = p.m_tiles * p.n_tiles * p.splits;
-  launch_k(kern, std::min(units, c->num_sms), 192, S::TOTAL, c->stream, p);
+  const int grid = std::min(units, c->num_sms);
+  GemmParams q = p;
+  q.trace = (g_trace && grid <= g_trace_ctas) ? g_trace : nullptr;
+  launch_k(kern, grid, kGemmThreads, S::TOTAL, c->stream, q);
   return check_launch(c, "gemm_tc_kernel");
 }
 // Sums the split-K partials and applies the epilogue (bias, per-image row vector, residual or GEGLU).
@@ -441,8 +548,8 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
 
 // Tiling: N tile width (128 / 160 / 192 / 256) and K splits from a cost model in units of one 128-wide
 // K block of MMA work per SM: units = M tiles x N tiles x splits run on min(units, SMs) persistent CTAs;
-// cost = rounds x (K blocks per unit x BN/128 + per-unit overhead) + split-K reduce (partial-sum traffic
-// and one launch).  GEGLU needs BN in {128, 256} (value/gate rows packed per 128 columns).
+// cost = rounds x (K blocks per unit x (128 + BN)/256 + per-unit overhead) + split-K reduce (partial-sum
+// traffic and one launch).  GEGLU needs BN in {128, 256} (value/gate rows packed per 128 columns).
 void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits) {
   static const int cands[4] = {128, 160, 192, 256};
   const int mt = (M + BM - 1) / BM;
@@ -477,8 +584,12 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
       if (seff != s) continue;
       const long long units = (long long)mt * nt * s;
       const long long rounds = (units + c->num_sms - 1) / c->num_sms;
-      double cost = (double)rounds * (per * (bc / 128.0) + 3.0) + 4.0;
-      if (s > 1) cost += 15.0 + (double)M * N * s * 8.0 / 6.4e12 / 130e-9;
+      // Units of one BN=128 K block (~0.29 us).  The main loop is bound by the SM's L2->smem rate
+      // (~64 B/clk), so a K block costs in proportion to its A + B rows (128 + BN), not to BN; a tile
+      // adds ~8 for the first load and the epilogue; split-K adds the reduce launch and the fp32
+      // partial traffic.
+      double cost = (double)rounds * (per * ((128.0 + bc) / 256.0) + 8.0) + 4.0;
+      if (s > 1) cost += 9.0 + (double)M * N * s * 8.0 / 6.4e12 / 290e-9;
       if (cost < best - 1e-9 || (cost < best + 1e-9 && bc > *bn)) {
         best = cost;
         *bn = bc;
@@ -497,7 +608,7 @@ int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
 static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16) {
   switch (bn) {
     case 256: return bf16 ? launch_variant<256, 4, true>(c, p) : launch_variant<256, 4, false>(c, p);
-    case 192: return bf16 ? launch_variant<192, 5, true>(c, p) : launch_variant<192, 5, false>(c, p);
+    case 192: return bf16 ? launch_variant<192, 4, true>(c, p) : launch_variant<192, 4, false>(c, p);
     case 160: return bf16 ? launch_variant<160, 5, true>(c, p) : launch_variant<160, 5, false>(c, p);
     default: return bf16 ? launch_variant<128, 6, true>(c, p) : launch_variant<128, 6, false>(c, p);
   }
@@ -505,6 +616,7 @@ static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16) {
 
 int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, void* splitk_ws) {
   p.err = c->d_err;
+  p.staged = (p.vec_ok && splits <= 1) ? 1 : 0;
   p.b_early = c->weights_const ? 1 : 0;
   p.splits = std::max(1, splits);
   p.m_tiles = (p.M + BM - 1) / BM;
@@ -513,6 +625,7 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, void* spli
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
     p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
     if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
+    p.staged = (p.N % 4 == 0 && reinterpret_cast<uintptr_t>(p.partial) % 16 == 0) ? 1 : 0;
     int r = dispatch_variant(c, p, bn, bf16);
     if (r) return r;
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
@@ -697,6 +810,13 @@ int pack_conv3x3(Ctx* c, int dtype, const float* w, int Co, int Ci, void* out) {
 using namespace di;
 
 extern "C" {
+
+int di_debug_gemm_trace(unsigned long long* buf, int ctas) {
+  if (ctas < 0 || (ctas > 0 && !buf)) return DI_EINVAL;
+  g_trace = ctas ? buf : nullptr;
+  g_trace_ctas = ctas;
+  return DI_OK;
+}
 
 int di_linear(di_ctx_t h, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
               const float* bias, const void* R, void* Y) {

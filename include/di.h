@@ -58,6 +58,12 @@ DI_API const char* di_last_error(di_ctx_t ctx);
 DI_API int di_device_fault(di_ctx_t ctx);
 DI_API int di_clear_fault(di_ctx_t ctx);
 
+/* Diagnostics (no counterpart in the reference): while set, every tensor-core GEMM launch with at most
+ * `ctas` CTAs writes 16 %globaltimer stamps per CTA to buf[cta * 16 + i] (device memory): entry, set-up
+ * done, dependency wait passed, first stage landed, last MMA issued, accumulator ready, epilogue done,
+ * exit, then epilogue detail (TMEM load issue / done for chunks 0 and 1, store issued for chunks 0, 1).  ctas = 0 switches it off.  Launches in flight keep the pointer they were given. */
+DI_API int di_debug_gemm_trace(unsigned long long* buf, int ctas);
+
 /* ---------------------------------------------------------------------------------------------
  * wgsl-ops.js op families: fp32 tensors in the reference's layouts, cfg blocks exactly as the
  * executor packs them (wgsl-executor.js OPS.* bodies).  Pointers are device pointers.
