@@ -71,10 +71,10 @@ constexpr int BM = 128, BK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 struct GemmSmem {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
-  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // a pair splits B's rows
   static constexpr uint32_t EPI_BYTES = kEpiWarps * 4096;  // one 32 x 128 B staging slab per epilogue warp
   static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + 256;  // + align + barriers
 };
@@ -142,9 +142,16 @@ __device__ __forceinline__ void store_one(void* dst, size_t off, float v, int is
 // (K split, 128-row M tile, BN-column N tile); CTA b processes units b, b + grid, ...  The smem ring
 // runs continuously across units, and the accumulator is double-buffered in TMEM (2 x BN columns)
 // so the epilogue of one unit overlaps the main loop of the next.
-template <int BN, int STAGES, bool BF16>
+//
+// PAIR: clusters of two CTAs on two SMs run one 256-row tile with cta_group::2 MMAs.  Each CTA loads its
+// own 128 A rows and half of B's BN rows, so a K block moves (128 + BN/2) rows per SM instead of
+// (128 + BN): the main loop is bound by each SM's L2 -> shared-memory rate, so this halves the B
+// traffic per FLOP.  The leader (rank 0) issues the MMAs; the peer's TMA loads count their bytes on the
+// leader's `full` barrier; MMA commits arrive on `empty` / `tfull` in both CTAs; both CTAs' epilogue
+// warps release the accumulator on the leader's `tempty`.  Units then index 256-row M tiles.
+template <int BN, int STAGES, bool BF16, bool PAIR = false>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
-  using S = GemmSmem<BN, STAGES>;
+  using S = GemmSmem<BN, STAGES, PAIR>;
   constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
   constexpr uint32_t TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   extern __shared__ uint8_t smem_raw[];
@@ -160,6 +167,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0 = leader
+  const int cta0 = PAIR ? blockIdx.x >> 1 : blockIdx.x;  // first unit of this CTA (pair)
+  const int cstride = PAIR ? gridDim.x >> 1 : gridDim.x;
   unsigned long long* tr = p.trace ? p.trace + (size_t)blockIdx.x * kTracePoints : nullptr;
   if (tr && threadIdx.x == 0) tr[0] = globaltimer();
   const int nt = p.n_tiles, per_split = p.m_tiles * p.n_tiles;
@@ -168,14 +178,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&tfull[s], 1); mbar_init(&tempty[s], 32 * kEpiWarps); }
+    // tempty: one arrival per epilogue warp (of both CTAs of a pair, on the leader's barrier)
+    for (int s = 0; s < 2; ++s) { mbar_init(&tfull[s], 1); mbar_init(&tempty[s], (PAIR ? 2 : 1) * kEpiWarps); }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+  if (warp == 1) {
+    if (PAIR) { tmem_alloc_pair(tmem_slot, TMEM_COLS); tmem_relinquish_pair(); }
+    else { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+  }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
+  else __syncthreads();
   tc_fence_after();
+  const uint32_t full0_leader = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
+  const uint32_t tempty_leader = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
   const uint32_t tmem = *tmem_slot;
   if (tr && threadIdx.x == 0) tr[1] = globaltimer();
   // Programmatic dependent launch: let the next kernel be scheduled right away.  Everything before
@@ -183,10 +200,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   // kernel's tail; activations are read only after the wait.
   pdl_trigger();
 
+  // m0: this CTA's first output row (a pair's tile is 256 rows, the peer takes the second 128)
   auto decode = [&](int u, int& m0, int& n0, int& sp, int& kb0, int& kb1) {
     sp = u / per_split;
     const int r = u - sp * per_split;
-    m0 = (r / nt) * BM;
+    m0 = (r / nt) * (PAIR ? 2 * BM : BM) + (int)rank * BM;
     n0 = (r % nt) * BN;
     kb0 = sp * kper;
     kb1 = min(p.num_k, kb0 + kper);
@@ -198,20 +216,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.tmA[i]);
       tma_prefetch_desc(&p.tmB);
       // Weight tiles of the first ring stages are requested before the dependency wait (constant data).
+      // In a pair, rank r loads B rows n0 + r * BN/2 .. and only the leader arms `full` (both CTAs' bytes).
+      const int brow = PAIR ? (int)rank * (BN / 2) : 0;
+      auto arm = [&](int s) {
+        if (!PAIR) mbar_arrive_expect_tx(&full[s], STAGE_TX);
+        else if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_TX);
+      };
+      auto load2 = [&](void* dst, const CUtensorMap* m, int s, int c0, int c1) {
+        if (PAIR) tma_load_2d_pair(dst, m, full0_leader + s * 8, c0, c1);
+        else tma_load_2d(dst, m, &full[s], c0, c1);
+      };
+      auto load4 = [&](void* dst, const CUtensorMap* m, int s, int c0, int c1, int c2, int c3) {
+        if (PAIR) tma_load_4d_pair(dst, m, full0_leader + s * 8, c0, c1, c2, c3);
+        else tma_load_4d(dst, m, &full[s], c0, c1, c2, c3);
+      };
       int npre = 0;
       {
         int m0, n0, sp, kb0, kb1;
-        decode(blockIdx.x, m0, n0, sp, kb0, kb1);
+        decode(cta0, m0, n0, sp, kb0, kb1);
         npre = p.b_early ? min(STAGES, kb1 - kb0) : 0;
         for (int i = 0; i < npre; ++i) {
-          mbar_arrive_expect_tx(&full[i], STAGE_TX);
-          tma_load_2d(sB + i * S::B_BYTES, &p.tmB, &full[i], (kb0 + i) * BK, n0);
+          arm(i);
+          load2(sB + i * S::B_BYTES, &p.tmB, i, (kb0 + i) * BK, n0 + brow);
         }
       }
       pdl_wait();
       if (tr) tr[2] = globaltimer();
       int it = 0;
-      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+      for (int u = cta0; u < units && !*abort_flag; u += cstride) {
         int m0, n0, sp, kb0, kb1;
         decode(u, m0, n0, sp, kb0, kb1);
         int img = 0, y0 = 0;
@@ -221,42 +253,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           const uint32_t ph = (it / STAGES) & 1;
           const bool pre = it < npre;  // B already requested, barrier already armed
           if (!pre) {
-            if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1, p.err, DEVERR_WAIT_TMA)) { *abort_flag = 1; break; }
-            mbar_arrive_expect_tx(&full[s], STAGE_TX);
+            if (*abort_flag || !mbar_wait<PAIR>(&empty[s], ph ^ 1, p.err, DEVERR_WAIT_TMA)) { *abort_flag = 1; break; }
+            arm(s);
           }
           uint8_t* dA = sA + s * S::A_BYTES;
           if (p.mode == 0) {
-            if (kb < p.k_split) tma_load_2d(dA, &p.tmA[0], &full[s], kb * BK, m0);
-            else tma_load_2d(dA, &p.tmA[1], &full[s], (kb - p.k_split) * BK, m0);
+            if (kb < p.k_split) load2(dA, &p.tmA[0], s, kb * BK, m0);
+            else load2(dA, &p.tmA[1], s, (kb - p.k_split) * BK, m0);
           } else {
             const int tap = kb / p.cin_blocks, cb = kb % p.cin_blocks;
             const int ky = tap / 3, kx = tap % 3;
             if (p.mode == 1) {
               const bool first = cb < p.k_split;
-              tma_load_4d(dA, &p.tmA[first ? 0 : 1], &full[s], (first ? cb : cb - p.k_split) * BK, kx - 1,
-                          y0 + ky - 1, img);
+              load4(dA, &p.tmA[first ? 0 : 1], s, (first ? cb : cb - p.k_split) * BK, kx - 1, y0 + ky - 1, img);
             } else {
               const int py = ky == 1 ? 0 : 1, px = kx == 1 ? 0 : 1;
-              tma_load_4d(dA, &p.tmA[py * 2 + px], &full[s], cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0),
-                          img);
+              load4(dA, &p.tmA[py * 2 + px], s, cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0), img);
             }
           }
-          if (!pre) tma_load_2d(sB + s * S::B_BYTES, &p.tmB, &full[s], kb * BK, n0);
+          if (!pre) load2(sB + s * S::B_BYTES, &p.tmB, s, kb * BK, n0 + brow);
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (elect_one()) {
-      constexpr uint32_t idesc = idesc_f16(BM, BN, BF16);
+    // ---------------- MMA issuer (the pair leader only) ----------------
+    if (rank == 0 && elect_one()) {
+      constexpr uint32_t idesc = idesc_f16(PAIR ? 2 * BM : BM, BN, BF16);
+      auto commit = [&](uint64_t* bar) {
+        if (PAIR) umma_commit_pair(bar, 0x3);
+        else umma_commit(bar);
+      };
       int it = 0, lt = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
+      for (int u = cta0; u < units; u += cstride, ++lt) {
         int m0, n0, sp, kb0, kb1;
         decode(u, m0, n0, sp, kb0, kb1);
         const int ab = lt & 1;
-        if (*abort_flag || !mbar_wait(&tempty[ab], ((lt >> 1) & 1) ^ 1, p.err, DEVERR_WAIT_MMA)) {
+        if (*abort_flag || !mbar_wait<PAIR>(&tempty[ab], ((lt >> 1) & 1) ^ 1, p.err, DEVERR_WAIT_MMA)) {
           *abort_flag = 1;
-          umma_commit(&tfull[ab]);
+          commit(&tfull[ab]);
           break;
         }
         tc_fence_after();
@@ -265,7 +299,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (*abort_flag || !mbar_wait(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; ok = false; break; }
+          if (*abort_flag || !mbar_wait<PAIR>(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; ok = false; break; }
           if (tr && lt == 0 && kb == kb0) tr[3] = globaltimer();
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * S::A_BYTES), b0 = smem_u32(sB + s * S::B_BYTES);
@@ -273,11 +307,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
             const uint64_t bd = sdesc_sw128(b0 + k * 32, 16, 1024);
-            umma_f16(dt, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            if (PAIR) umma_f16_pair(dt, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            else umma_f16(dt, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          commit(&empty[s]);
         }
-        umma_commit(&tfull[ab]);
+        commit(&tfull[ab]);
         if (tr && lt == 0) tr[4] = globaltimer();
         if (!ok) break;
       }
@@ -293,12 +328,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     const int half = (warp - 2) / 4;  // which alternate column chunks this warp handles
     uint8_t* stg = sEpi + (warp - 2) * 4096;
     int lt = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
+    for (int u = cta0; u < units; u += cstride, ++lt) {
       int m0, n0, sp, kb0, kb1;
       decode(u, m0, n0, sp, kb0, kb1);
       const int ab = lt & 1;
       const int m = m0 + row;
-      const bool okw = mbar_wait(&tfull[ab], (lt >> 1) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
+      const bool okw = mbar_wait<PAIR>(&tfull[ab], (lt >> 1) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
       const bool ok = __all_sync(0xffffffffu, okw);
       if (tr && lt == 0 && threadIdx.x == 64) tr[5] = globaltimer();
       tc_fence_after();
@@ -462,24 +497,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[ab]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + ab * 8);
       if (tr && lt == 0 && threadIdx.x == 64) tr[6] = globaltimer();
       if (!ok) break;
     }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync();  // no CTA leaves while its pair partner may still signal its barriers
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem, TMEM_COLS);
+    else tmem_dealloc(tmem, TMEM_COLS);
   }
   if (tr && threadIdx.x == 0) tr[7] = globaltimer();
 }
 
-template <int BN, int STAGES, bool BF16>
+// Pairs of CTAs that can be resident at once (clusters of 2 need both SMs in one GPC), per device.
+static int g_max_pairs[32] = {0};
+
+template <int BN, int STAGES, bool BF16, bool PAIR>
 int launch_variant(Ctx* c, const GemmParams& p) {
-  using S = GemmSmem<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES, BF16>;
+  using S = GemmSmem<BN, STAGES, PAIR>;
+  auto kern = gemm_tc_kernel<BN, STAGES, BF16, PAIR>;
   static unsigned attr_done = 0;  // per-device bit: dynamic smem opt-in is a per-device attribute
   if (!(attr_done & (1u << (c->device & 31)))) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
@@ -487,12 +528,46 @@ int launch_variant(Ctx* c, const GemmParams& p) {
     attr_done |= 1u << (c->device & 31);
   }
   const int units = p.m_tiles * p.n_tiles * p.splits;
-  const int grid = std::min(units, c->num_sms);
+  int grid;
+  if (PAIR) {
+    const int pairs = g_max_pairs[c->device & 31] > 0 ? g_max_pairs[c->device & 31] : c->num_sms / 2;
+    grid = 2 * std::min(units, pairs);
+  } else {
+    grid = std::min(units, c->num_sms);
+  }
   GemmParams q = p;
   q.trace = (g_trace && grid <= g_trace_ctas) ? g_trace : nullptr;
-  launch_k(kern, grid, kGemmThreads, S::TOTAL, c->stream, q);
+  if (PAIR) launch_k_cluster(kern, grid, kGemmThreads, S::TOTAL, c->stream, 2, q);
+  else launch_k(kern, grid, kGemmThreads, S::TOTAL, c->stream, q);
   return check_launch(c, "gemm_tc_kernel");
 }
+
+// Queries (once per device) how many 2-CTA clusters of the paired kernel fit on the GPU at once.
+static int max_pairs(Ctx* c) {
+  int& mp = g_max_pairs[c->device & 31];
+  if (mp) return mp;
+  using S = GemmSmem<256, 6, true>;
+  auto kern = gemm_tc_kernel<256, 6, false, true>;
+  mp = c->num_sms / 2;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * mp);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = S::TOTAL;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) mp = std::min(mp, n);
+  }
+  cudaGetLastError();
+  return mp;
+}
+
 // Sums the split-K partials and applies the epilogue (bias, per-image row vector, residual or GEGLU).
 __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
                               const float* __restrict__ rowvec, int rowvec_div, int rowvec_ld, const void* residual,
@@ -550,18 +625,20 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
 // K block of MMA work per SM: units = M tiles x N tiles x splits run on min(units, SMs) persistent CTAs;
 // cost = rounds x (K blocks per unit x (128 + BN)/256 + per-unit overhead) + split-K reduce (partial-sum
 // traffic and one launch).  GEGLU needs BN in {128, 256} (value/gate rows packed per 128 columns).
-void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits) {
+void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits, int* pair) {
   static const int cands[4] = {128, 160, 192, 256};
   const int mt = (M + BM - 1) / BM;
-  // Tuning / diagnostics override: DI_GEMM_TILING="bn,splits" forces the tiling of every GEMM.
-  static int forced_bn = -1, forced_s = 1;
+  *pair = 0;
+  // Tuning / diagnostics override: DI_GEMM_TILING="bn,splits[,pair]" forces the tiling of every GEMM.
+  static int forced_bn = -1, forced_s = 1, forced_pair = 0;
   if (forced_bn < 0) {
     forced_bn = 0;
     if (const char* e = getenv("DI_GEMM_TILING")) {
-      int b = 0, s = 1;
-      if (sscanf(e, "%d,%d", &b, &s) >= 1 && (b == 128 || b == 160 || b == 192 || b == 256)) {
+      int b = 0, s = 1, pr = 0;
+      if (sscanf(e, "%d,%d,%d", &b, &s, &pr) >= 1 && (b == 128 || b == 160 || b == 192 || b == 256)) {
         forced_bn = b;
         forced_s = std::max(1, s);
+        forced_pair = pr ? 1 : 0;
       }
     }
   }
@@ -569,64 +646,87 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
     *bn = forced_bn;
     const int per = (num_k + forced_s - 1) / forced_s;
     *splits = (num_k + per - 1) / per;
+    *pair = forced_pair && M > BM;
     return;
   }
+  // Model in units of one BN=128 K block on one CTA (~0.3 us, measured with the per-CTA trace).  A K
+  // block of the main loop costs nearly the same for any tile width: 1.0 at BN=128, +20% at BN=256 for
+  // one CTA and +5% for a pair, whose tile has twice the rows; so wide and paired tiles do more work
+  // per unit of time, narrow and split tiles fill more SMs.  A tile adds ~8 for its first load and the
+  // epilogue; split-K adds the reduce launch and the fp32 partial traffic; a wave holds min(SMs,
+  // resident pairs) units.
+  const int pairs = max_pairs(c);
+  static const int pair_ok = [] {  // diagnostics: DI_GEMM_PAIR=0 disables paired-CTA tiles
+    const char* e = getenv("DI_GEMM_PAIR");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
   double best = 1e30;
   *bn = 128;
   *splits = 1;
-  for (int bc : cands) {
-    if (geglu && (bc % 128 || N % bc)) continue;
-    const int nt = geglu ? N / bc : (N + bc - 1) / bc;
-    const int smax = std::max(1, std::min(16, num_k / 4));
-    for (int s = 1; s <= smax; ++s) {
-      const int per = (num_k + s - 1) / s;
-      const int seff = (num_k + per - 1) / per;
-      if (seff != s) continue;
-      const long long units = (long long)mt * nt * s;
-      const long long rounds = (units + c->num_sms - 1) / c->num_sms;
-      // Units of one BN=128 K block (~0.29 us).  The main loop is bound by the SM's L2->smem rate
-      // (~64 B/clk), so a K block costs in proportion to its A + B rows (128 + BN), not to BN; a tile
-      // adds ~8 for the first load and the epilogue; split-K adds the reduce launch and the fp32
-      // partial traffic.
-      double cost = (double)rounds * (per * ((128.0 + bc) / 256.0) + 8.0) + 4.0;
-      if (s > 1) cost += 9.0 + (double)M * N * s * 8.0 / 6.4e12 / 290e-9;
-      if (cost < best - 1e-9 || (cost < best + 1e-9 && bc > *bn)) {
-        best = cost;
-        *bn = bc;
-        *splits = s;
+  for (int pr = 0; pr < 2; ++pr) {
+    if (pr && (M <= BM || !pair_ok)) continue;
+    const int mtiles = pr ? (M + 2 * BM - 1) / (2 * BM) : mt;
+    const int slots = pr ? pairs : c->num_sms;  // concurrently running units
+    for (int bc : cands) {
+      if (geglu && (bc % 128 || N % bc)) continue;
+      const int nt = geglu ? N / bc : (N + bc - 1) / bc;
+      const int smax = std::max(1, std::min(16, num_k / 4));
+      const double kb_cost = 1.0 + (pr ? 0.05 : 0.2) * (bc - 128) / 128.0;
+      for (int s = 1; s <= smax; ++s) {
+        const int per = (num_k + s - 1) / s;
+        const int seff = (num_k + per - 1) / per;
+        if (seff != s) continue;
+        const long long units = (long long)mtiles * nt * s;
+        const long long rounds = (units + slots - 1) / slots;
+        double cost = (double)rounds * (per * kb_cost + 8.0) + 4.0;
+        if (s > 1) cost += 9.0 + (double)M * N * s * 8.0 / 6.4e12 / 290e-9;
+        if (cost < best - 1e-9 || (cost < best + 1e-9 && bc > *bn)) {
+          best = cost;
+          *bn = bc;
+          *splits = s;
+          *pair = pr;
+        }
       }
     }
   }
 }
 
 int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
-  int bn, s;
-  choose_tiling(c, M, N, K / 64, geglu, &bn, &s);
+  int bn, s, pr;
+  choose_tiling(c, M, N, K / 64, geglu, &bn, &s, &pr);
   return s > 1 ? 2 : 1;
 }
 
-static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16) {
+static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
+  if (pair) {
+    switch (bn) {
+      case 256: return bf16 ? launch_variant<256, 6, true, true>(c, p) : launch_variant<256, 6, false, true>(c, p);
+      case 192: return bf16 ? launch_variant<192, 6, true, true>(c, p) : launch_variant<192, 6, false, true>(c, p);
+      case 160: return bf16 ? launch_variant<160, 7, true, true>(c, p) : launch_variant<160, 7, false, true>(c, p);
+      default: return bf16 ? launch_variant<128, 8, true, true>(c, p) : launch_variant<128, 8, false, true>(c, p);
+    }
+  }
   switch (bn) {
-    case 256: return bf16 ? launch_variant<256, 4, true>(c, p) : launch_variant<256, 4, false>(c, p);
-    case 192: return bf16 ? launch_variant<192, 4, true>(c, p) : launch_variant<192, 4, false>(c, p);
-    case 160: return bf16 ? launch_variant<160, 5, true>(c, p) : launch_variant<160, 5, false>(c, p);
-    default: return bf16 ? launch_variant<128, 6, true>(c, p) : launch_variant<128, 6, false>(c, p);
+    case 256: return bf16 ? launch_variant<256, 4, true, false>(c, p) : launch_variant<256, 4, false, false>(c, p);
+    case 192: return bf16 ? launch_variant<192, 4, true, false>(c, p) : launch_variant<192, 4, false, false>(c, p);
+    case 160: return bf16 ? launch_variant<160, 5, true, false>(c, p) : launch_variant<160, 5, false, false>(c, p);
+    default: return bf16 ? launch_variant<128, 6, true, false>(c, p) : launch_variant<128, 6, false, false>(c, p);
   }
 }
 
-int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, void* splitk_ws) {
+int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, void* splitk_ws) {
   p.err = c->d_err;
   p.staged = (p.vec_ok && splits <= 1) ? 1 : 0;
   p.b_early = c->weights_const ? 1 : 0;
   p.splits = std::max(1, splits);
-  p.m_tiles = (p.M + BM - 1) / BM;
+  p.m_tiles = pair ? (p.M + 2 * BM - 1) / (2 * BM) : (p.M + BM - 1) / BM;
   p.n_tiles = p.geglu ? p.N / bn : (p.N + bn - 1) / bn;
   if (p.splits > 1) {
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
     p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
     if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
     p.staged = (p.N % 4 == 0 && reinterpret_cast<uintptr_t>(p.partial) % 16 == 0) ? 1 : 0;
-    int r = dispatch_variant(c, p, bn, bf16);
+    int r = dispatch_variant(c, p, bn, bf16, pair);
     if (r) return r;
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
@@ -634,7 +734,7 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, void* spli
              p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32, p.geglu, bf16);
     return check_launch(c, "splitk_reduce");
   }
-  return dispatch_variant(c, p, bn, bf16);
+  return dispatch_variant(c, p, bn, bf16, pair);
 }
 
 static CUtensorMapDataType tdt(int dtype) {
@@ -728,9 +828,10 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
   p.vec_ok = vec_rows_ok(Y, p.ldo, out_f32 ? 4 : 2) && (!R || vec_rows_ok(R, N, res_f32 ? 4 : 2));
   (void)bn;
   int chosen, splits;
-  choose_tiling(c, M, N, p.num_k, geglu, &chosen, &splits);
-  if (!tmap_kmajor(&p.tmB, dtype, W, N, K, K, chosen, &err)) return set_error(c, DI_EINVAL, err);
-  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, splitk_ws);
+  int pair;
+  choose_tiling(c, M, N, p.num_k, geglu, &chosen, &splits, &pair);
+  if (!tmap_kmajor(&p.tmB, dtype, W, N, K, K, pair ? chosen / 2 : chosen, &err)) return set_error(c, DI_EINVAL, err);
+  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, pair, splitk_ws);
 }
 
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
@@ -780,9 +881,11 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
   p.out_f32 = out_f32;
   p.vec_ok = vec_rows_ok(y, Co, out_f32 ? 4 : 2) && (!residual || vec_rows_ok(residual, Co, res_f32 ? 4 : 2));
   int chosen, splits;
-  choose_tiling(c, p.M, Co, p.num_k, 0, &chosen, &splits);
-  if (!tmap_kmajor(&p.tmB, dtype, Wt, Co, 9 * Cin, 9 * Cin, chosen, &err)) return set_error(c, DI_EINVAL, err);
-  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, splitk_ws);
+  int pair;
+  choose_tiling(c, p.M, Co, p.num_k, 0, &chosen, &splits, &pair);
+  if (!tmap_kmajor(&p.tmB, dtype, Wt, Co, 9 * Cin, 9 * Cin, pair ? chosen / 2 : chosen, &err))
+    return set_error(c, DI_EINVAL, err);
+  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, pair, splitk_ws);
 }
 
 // Weight repack: [Co][Ci][3][3] fp32 -> [Co][3][3][Ci] fp16/bf16.
