@@ -20,7 +20,7 @@ import os
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
-LIB_PATH = PKG_DIR / "libdi.so"
+LIB_PATH = Path(os.environ["DI_LIB"]) if os.environ.get("DI_LIB") else PKG_DIR / "libdi.so"  # DI_LIB: diagnostics
 
 DI_OK, DI_EINVAL, DI_ECUDA, DI_ENOMEM, DI_EUNSUPPORTED, DI_EFAULT = 0, -1, -2, -3, -4, -5
 DI_F32, DI_F16, DI_BF16 = 0, 1, 2

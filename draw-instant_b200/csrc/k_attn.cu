@@ -10,10 +10,18 @@
 //               for tile j+1 runs while the softmax warps work on tile j; then O += P_j V_j
 //               (M=128, N=64, K=64) with O resident in TMEM for the whole row block
 //   warps 2..5  softmax, one query row per thread (= one TMEM lane): running max / sum in the exp2
-//               domain, rescale of O in TMEM when the max moves, P written to shared memory as fp16/bf16
-//               in the 128B-swizzled K-major layout the MMA reads; finally O / l is stored.
+//               domain, P written to shared memory as fp16/bf16 in the 128B-swizzled K-major layout the
+//               MMA reads (two P buffers, so P_{j+1} is written while P_j.V_j runs); finally O / l.
 //
-// Footprint: ~81 KB shared memory and 256 TMEM columns (S0 [0,64), S1 [64,128), O [128,192)), so two
+// Softmax cost, which bounds this kernel rather than the tensor pipe:
+//   * lazy rescaling: the running max used for the exponentials only moves when a row's true max
+//     exceeds it by more than 8 (log2 units), so O in TMEM is rescaled rarely; P then stays <= 2^8,
+//     well inside fp16 / bf16 range, and l uses the same stale max, so O / l is exact;
+//   * the softmax warps' instruction issue, not the MUFU unit, is the limit: the max runs on raw
+//     scores with 3-input max, the scale and max subtraction are one packed f32x2 FMA per two scores,
+//     the row sum is packed f32x2 adds, and key masking runs only on the last, partial tile.
+//
+// Footprint: ~97 KB shared memory and 256 TMEM columns (S0 [0,64), S1 [64,128), O [128,192)), so two
 // CTAs share an SM: one CTA's softmax overlaps the other's tensor-core work, and the U-Net's
 // 160-CTA attention grids are resident in a single wave.
 // Scores are scaled by 1/sqrt(64) as in the reference.  Keys past Skv (the zero-filled tail of the last
@@ -40,7 +48,35 @@ constexpr int QT = 128, KT = 64, HD = 64, KV_STAGES = 3;
 constexpr uint32_t Q_BYTES = QT * HD * 2;   // 16 KB
 constexpr uint32_t KV_BYTES = KT * HD * 2;  // 8 KB per K or V tile
 constexpr uint32_t P_BYTES = QT * KT * 2;   // 16 KB
-constexpr uint32_t SMEM_ATTN = 1024 + Q_BYTES + 2 * KV_STAGES * KV_BYTES + P_BYTES + 512;
+constexpr uint32_t SMEM_ATTN = 1024 + Q_BYTES + 2 * KV_STAGES * KV_BYTES + 2 * P_BYTES + 512;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+// Packed two-lane fp32 arithmetic (sm_100): halves the FMA / FADD instruction count of the softmax.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float ex2_approx(float x) {  // MUFU 2^x; -inf -> +0
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <bool BF16>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ AttnParams p) {
@@ -49,15 +85,15 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + Q_BYTES;               // KV_STAGES tiles
   uint8_t* sV = sK + KV_STAGES * KV_BYTES;  // KV_STAGES tiles
-  uint8_t* sP = sV + KV_STAGES * KV_BYTES;  // 128 x 64, one 128B-swizzled K-major block
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint8_t* sP = sV + KV_STAGES * KV_BYTES;  // [2] x (128 x 64), 128B-swizzled K-major blocks
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;                // [KV_STAGES]
   uint64_t* kv_empty = kv_full + KV_STAGES;    // [KV_STAGES]
   uint64_t* s_full = kv_empty + KV_STAGES;     // [2]
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  uint64_t* p_full = s_full + 2;               // [2] P_j written (buffer j & 1)
+  uint64_t* pv_done = p_full + 2;              // [2] P_j.V_j complete (buffer j & 1)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -67,9 +103,11 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < KV_STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
-    for (int i = 0; i < 2; ++i) mbar_init(&s_full[i], 1);
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -106,18 +144,19 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     if (elect_one()) {
       constexpr uint32_t idS = idesc_f16(128, KT, BF16);
       constexpr uint32_t idO = idesc_f16(128, HD, BF16, false, true);  // B = V is MN-major (d contiguous)
-      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      const uint32_t aQ = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, p.err, DEVERR_WAIT_MMA);
       auto issue_pv = [&](int jj) {
         const int st = jj % KV_STAGES;
         const uint32_t aV = smem_u32(sV + st * KV_BYTES);
+        const uint32_t aP = smem_u32(sP + (jj & 1) * P_BYTES);
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
           const uint64_t ad = sdesc_sw128(aP + kk * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(aV + kk * 2048, 8192, 1024);
           umma_f16(tO, ad, bd, idO, (jj | kk) != 0 ? 1u : 0u);
         }
-        umma_commit(o_done);
+        umma_commit(&pv_done[jj & 1]);
         umma_commit(&kv_empty[st]);
       };
       for (int j = 0; ok && j < nt; ++j) {
@@ -136,17 +175,18 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         }
         umma_commit(&s_full[j & 1]);
         if (j > 0) {
-          if (!mbar_wait(p_full, (j - 1) & 1, p.err, DEVERR_WAIT_MMA)) { ok = false; break; }
+          if (!mbar_wait(&p_full[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, DEVERR_WAIT_MMA)) { ok = false; break; }
           tc_fence_after();
           issue_pv(j - 1);
         }
       }
-      if (ok && mbar_wait(p_full, (nt - 1) & 1, p.err, DEVERR_WAIT_MMA)) {
+      if (ok && mbar_wait(&p_full[(nt - 1) & 1], ((nt - 1) >> 1) & 1, p.err, DEVERR_WAIT_MMA)) {
         tc_fence_after();
         issue_pv(nt - 1);
       } else {
         *abort_flag = 1;
-        umma_commit(o_done);  // release the softmax warps promptly
+        umma_commit(&pv_done[0]);  // release the softmax warps promptly
+        umma_commit(&pv_done[1]);
       }
     }
   } else {
@@ -156,7 +196,6 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    uint8_t* prow = sP + row * 128;
     for (int j = 0; j < nt; ++j) {
       const int sb = j & 1;
       ok = ok && mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
@@ -173,40 +212,52 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         }
       }
       const int kvalid = p.Skv - j * KT;
+      if (kvalid < KT) {
+#pragma unroll
+        for (int i = 0; i < KT; ++i)
+          if (i >= kvalid) s[i] = -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < KT; ++i) {
-        s[i] = i < kvalid ? s[i] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[i]);
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = exp2f(m_run - m_new);
-      float sum = 0.f;
+      for (int i = 0; i < KT; i += 2) mx = max3f(mx, s[i], s[i + 1]);
+      mx *= p.scale_log2;  // the scale is positive: max of the scaled scores
+      // lazy rescale: move the reference max only when the row max exceeds it by the threshold
+      const bool move = mx > m_run + kRescaleThreshold;
+      const float m_new = move ? mx : m_run;
+      const float alpha = move ? ex2_approx(m_run - m_new) : 1.0f;
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(-m_new, -m_new);
+      uint64_t acc2 = 0;
 #pragma unroll
-      for (int i = 0; i < KT; ++i) {
-        s[i] = exp2f(s[i] - m_new);
-        sum += s[i];
+      for (int i = 0; i < KT; i += 2) {
+        const uint64_t x = fma2(f2_pack(s[i], s[i + 1]), sc2, nm2);
+        s[i] = ex2_approx(lo_f(x));
+        s[i + 1] = ex2_approx(hi_f(x));
+        acc2 = add2(acc2, f2_pack(s[i], s[i + 1]));
       }
+      const float sum = lo_f(acc2) + hi_f(acc2);
       l_run = l_run * alpha + sum;
       m_run = m_new;
-      if (j > 0) {
-        // P buffer and O are busy until the previous P.V product completes.
-        ok = ok && mbar_wait(o_done, (j - 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        // O is rescaled only after P_{j-1}.V_{j-1} has landed in it
+        ok = ok && mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-          uint32_t r[32];
+        uint32_t r[32];
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            tmem_ld32(tO + lane_off + c * 32, r);
-            tmem_wait_ld();
+        for (int c = 0; c < HD / 32; ++c) {
+          tmem_ld32(tO + lane_off + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, r);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO + lane_off + c * 32, r);
         }
+        tmem_wait_st();
+      }
+      if (j > 1) {
+        // P buffer j & 1 is free once P_{j-2}.V_{j-2} has completed
+        ok = ok && mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
       }
       // P row -> shared memory, 128B swizzle: 16-byte chunk c of row r lands at chunk c ^ (r % 8).
+      uint8_t* prow = sP + sb * P_BYTES + row * 128;
 #pragma unroll
       for (int c = 0; c < KT / 8; ++c) {
         uint32_t w[4];
@@ -225,9 +276,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[sb]);
     }
-    ok = ok && mbar_wait(o_done, (nt - 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
+    ok = ok && mbar_wait(&pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, p.err, DEVERR_WAIT_SOFTMAX);
     tc_fence_after();
     uint32_t r0[32], r1[32];
     tmem_ld32(tO + lane_off, r0);
