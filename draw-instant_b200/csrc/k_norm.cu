@@ -59,6 +59,8 @@ __device__ __forceinline__ void store8(T* p, const float* f) {
 // NHWC GroupNorm.  x = concat(x1[P, C1], x2[P, C2]) per pixel; partial[n][chunk][g] = (sum, sumsq).
 // Block = R rows x V vectors (8 channels each); thread (r, v) walks pixels r, r+R, ... of its chunk.
 // ---------------------------------------------------------------------------------------------
+constexpr int kGnRows = 8;  // pixels per thread per chunk in the statistics pass
+
 template <typename T>
 __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2, int HW,
                                 int chunk_pixels, int G, float2* __restrict__ partial) {
@@ -77,21 +79,27 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
     const int p0 = chunk * chunk_pixels, p1 = min(HW, p0 + chunk_pixels);
     const T* base = c < C1 ? x1 + (size_t)n * HW * C1 + c : x2 + (size_t)n * HW * C2 + (c - C1);
     const size_t ld = c < C1 ? C1 : C2;
-    int p = p0 + r;
-    for (; p + 3 * R < p1; p += 4 * R) {  // four independent loads in flight per thread
-      float f[4][8];
+    // Rounds of kGnRows pixels per thread, all loads of a round issued before any use, so a whole
+    // round of the chunk is in flight at once.
+    for (int pr = p0 + r; pr < p1; pr += kGnRows * R) {
+      uint4 raw[kGnRows];  // 16-bit inputs: eight channels per 16-byte load
 #pragma unroll
-      for (int u = 0; u < 4; ++u) load8<T>(base + (size_t)(p + u * R) * ld, f[u]);
+      for (int u = 0; u < kGnRows; ++u) {
+        const int p = pr + u * R;
+        if constexpr (sizeof(T) == 2)
+          if (p < p1) raw[u] = __ldg(reinterpret_cast<const uint4*>(base + (size_t)p * ld));
+      }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < kGnRows; ++u) {
+        const int p = pr + u * R;
+        if (p < p1) {
+          float f[8];
+          if constexpr (sizeof(T) == 4) load8<T>(base + (size_t)p * ld, f);  // fp32: loaded at use
+          else load8<T>(reinterpret_cast<const T*>(&raw[u]), f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { s[j] += f[u][j]; q[j] += f[u][j] * f[u][j]; }
-    }
-    for (; p < p1; p += R) {
-      float f[8];
-      load8<T>(base + (size_t)p * ld, f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) { s[j] += f[j]; q[j] += f[j] * f[j]; }
+          for (int j = 0; j < 8; ++j) { s[j] += f[j]; q[j] += f[j] * f[j]; }
+        }
+      }
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) { ssum[r * C + c + j] = s[j]; ssq[r * C + c + j] = q[j]; }
@@ -112,31 +120,33 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
   }
 }
 
+// Normalise pass.  Block = V threads (one 8-channel vector each) x R pixel rows, so every thread keeps
+// the same 8 channels for the whole grid-stride loop and applies them as one FMA per element with
+// per-thread scale / shift (gamma * rstd, beta - mean * gamma * rstd).  The group statistics are first
+// folded from the partials: all threads stage the (chunk, group) partials of image n in shared memory
+// with independent loads, then each group is summed over the chunks in a fixed order (deterministic).
 template <typename Tin, typename Tout>
 __global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __restrict__ x2, int C2, int HW, int G,
                               const float2* __restrict__ partial, int nchunks, const float* __restrict__ gamma,
                               const float* __restrict__ beta, float eps, int silu, Tout* __restrict__ y) {
   pdl_begin();
+  extern __shared__ float2 s_part[];  // [nchunks][G]
   __shared__ float s_mean[128], s_rstd[128];
-  __shared__ float2 s_part[256];
   const int C = C1 + C2, V = C / 8, cpg = C / G;
   const int n = blockIdx.y;
-  // Group statistics from the partials: blockDim/G threads per group each fold a strided subset of the
-  // chunks, then one thread per group folds those in a fixed order (deterministic).
-  const int tpg = blockDim.x / G;  // blockDim (256) >= G
-  if ((int)threadIdx.x < tpg * G) {
-    const int g = threadIdx.x / tpg, sub = threadIdx.x % tpg;
-    float s = 0.f, q = 0.f;
-    for (int k = sub; k < nchunks; k += tpg) {
-      const float2 pq = partial[((size_t)n * nchunks + k) * G + g];
-      s += pq.x; q += pq.y;
-    }
-    s_part[threadIdx.x] = make_float2(s, q);
-  }
+  const int nthr = blockDim.x * blockDim.y, tid = threadIdx.y * blockDim.x + threadIdx.x;
+  const float2* src = partial + (size_t)n * nchunks * G;
+  const int total = nchunks * G;
+#pragma unroll 4
+  for (int k = tid; k < total; k += nthr) s_part[k] = src[k];
   __syncthreads();
-  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+  for (int g = tid; g < G; g += nthr) {
     float s = 0.f, q = 0.f;
-    for (int u = 0; u < tpg; ++u) { s += s_part[g * tpg + u].x; q += s_part[g * tpg + u].y; }
+    for (int k = 0; k < nchunks; ++k) {
+      const float2 pq = s_part[k * G + g];
+      s += pq.x;
+      q += pq.y;
+    }
     const float cnt = (float)cpg * (float)HW;
     const float mean = s / cnt;
     const float var = fmaxf(q / cnt - mean * mean, 0.0f);
@@ -144,21 +154,39 @@ __global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __r
     s_rstd[g] = 1.0f / sqrtf(var + eps);
   }
   __syncthreads();
-  const size_t total = (size_t)HW * V;
-  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    const int v = e % V;
-    const size_t p = (size_t)n * HW + e / V;
-    const int c = v * 8;
-    float f[8];
-    if (c < C1) load8<Tin>(x1 + p * C1 + c, f);
-    else load8<Tin>(x2 + p * C2 + (c - C1), f);
+  const int v = threadIdx.x, c = v * 8;
+  if (v >= V) return;
+  float sc[8], sh[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int cc = c + j, g = cc / cpg;
-      float o = (f[j] - s_mean[g]) * s_rstd[g] * __ldg(gamma + cc) + __ldg(beta + cc);
-      f[j] = silu ? silu_f(o) : o;
+  for (int j = 0; j < 8; ++j) {
+    const int g = (c + j) / cpg;
+    sc[j] = s_rstd[g] * __ldg(gamma + c + j);
+    sh[j] = __ldg(beta + c + j) - s_mean[g] * sc[j];
+  }
+  const Tin* base = c < C1 ? x1 + (size_t)n * HW * C1 + c : x2 + (size_t)n * HW * C2 + (c - C1);
+  const size_t ld = c < C1 ? C1 : C2;
+  Tout* out = y + (size_t)n * HW * C + c;
+  const int R = blockDim.y, stride = gridDim.x * R;
+  // four pixels per thread per round, loads issued before any use
+  for (int p0 = blockIdx.x * R + threadIdx.y; p0 < HW; p0 += 4 * stride) {
+    float f[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int p = p0 + u * stride;
+      if (p < HW) load8<Tin>(base + (size_t)p * ld, f[u]);
     }
-    store8<Tout>(y + p * C + c, f);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int p = p0 + u * stride;
+      if (p < HW) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float o = fmaf(f[u][j], sc[j], sh[j]);
+          f[u][j] = silu ? silu_f(o) : o;
+        }
+        store8<Tout>(out + (size_t)p * C, f[u]);
+      }
+    }
   }
 }
 
@@ -255,10 +283,11 @@ static int gn_nhwc_impl(Ctx* c, const Tin* x1, int C1, const Tin* x2, int C2, in
   }
   const size_t shm = sizeof(float) * 2 * R * C;
   launch_k(gn_nhwc_partial<Tin>, dim3(chunks, N), threads, shm, c->stream, x1, C1, x2, C2, HW, chunk_pixels, G, partial);
-  const size_t work = (size_t)HW * V;
-  const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)std::max(1, 4 * c->num_sms / std::max(1, N)));
-  launch_k(gn_nhwc_apply<Tin, Tout>, dim3(blocks, N), 256, 0, c->stream, x1, C1, x2, C2, HW, G, partial, chunks, gamma,
-                                                                    beta, eps, silu, y);
+  // normalise: V x Ra threads per block, about two blocks per SM over the whole batch
+  const int Ra = std::max(1, 256 / V);
+  const int ablocks = std::max(1, std::min((HW + 4 * Ra - 1) / (4 * Ra), std::max(1, 2 * c->num_sms / std::max(1, N))));
+  launch_k(gn_nhwc_apply<Tin, Tout>, dim3(ablocks, N), dim3(V, Ra), sizeof(float2) * chunks * G, c->stream, x1, C1, x2,
+           C2, HW, G, partial, chunks, gamma, beta, eps, silu, y);
   return check_launch(c, "group_norm_nhwc");
 }
 
