@@ -23,7 +23,7 @@ size_t gn_nhwc_ws_bytes(int N, int HW, int G);
 
 namespace {
 
-// 1 MiB of (sum, sum-of-squares) partials: N * min(64, max(1, HW/16)) * G entries of 8 bytes.
+// 1 MiB of (sum, sum-of-squares) partials: N * max(1, min(16, HW/256)) * G entries of 8 bytes.
 constexpr size_t kNoAllocScratchBytes = 1u << 20;
 static __device__ __align__(256) float2 g_gn_scratch[kNoAllocScratchBytes / sizeof(float2)];
 
@@ -64,7 +64,7 @@ extern "C" int di_group_norm_nhwc_noalloc(di_ctx_t h, int dtype, const void* x1,
   if (need > kNoAllocScratchBytes)
     return set_error(c, DI_EINVAL,
                      "group_norm_nhwc_noalloc: needs " + std::to_string(need) + " bytes of scratch, the fixed maximum is " +
-                         std::to_string(kNoAllocScratchBytes) + " (N * min(64, max(1, HW/16)) * G * 8 bytes)");
+                         std::to_string(kNoAllocScratchBytes) + " (N * max(1, min(16, HW/256)) * G * 8 bytes)");
   void* scratch = nullptr;
   const int r = scratch_address(c, &scratch);
   if (r) return r;

@@ -56,22 +56,35 @@ __device__ __forceinline__ void store8(T* p, const float* f) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// NHWC GroupNorm.  x = concat(x1[P, C1], x2[P, C2]) per pixel; partial[n][chunk][g] = (sum, sumsq).
-// Block = R rows x V vectors (8 channels each); thread (r, v) walks pixels r, r+R, ... of its chunk.
+// NHWC GroupNorm.  x = concat(x1[P, C1], x2[P, C2]) per pixel.
+//
+// Statistics pass: the pixels of image n are cut into `chunks` chunks of ~32 pixels; CTA (chunk, n) is a
+// (V vectors of 8 channels) x (R pixel rows) block that sums its chunk per channel, then per group.
+// CTAs form clusters of `cl` consecutive chunks: after a cluster barrier the rank-0 CTA adds the
+// cluster's group sums from the other CTAs' shared memory (distributed shared memory, fixed rank
+// order) and writes one (sum, sum-of-squares) per group: partial[n][cluster][g].  So the normalise
+// pass folds only chunks / cl partials per group, and everything is run-to-run deterministic.
 // ---------------------------------------------------------------------------------------------
-constexpr int kGnRows = 8;  // pixels per thread per chunk in the statistics pass
+constexpr int kGnRows = 8;  // pixels per thread per round in the statistics pass
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
 
 template <typename T>
 __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2, int HW,
                                 int chunk_pixels, int G, float2* __restrict__ partial) {
   pdl_begin();
   extern __shared__ float sh[];
-  const int C = C1 + C2, V = C / 8, R = blockDim.x / V;
-  const int n = blockIdx.y, chunk = blockIdx.x, nchunks = gridDim.x;
-  const int t = threadIdx.x, r = t / V, v = t % V;
+  __shared__ float s_grp[2 * 128];  // this CTA's (sum, sumsq) per group
+  const int C = C1 + C2, V = blockDim.x, R = blockDim.y;
+  const int n = blockIdx.y, chunk = blockIdx.x;
+  const int v = threadIdx.x, r = threadIdx.y, tid = r * V + v, nthr = V * R;
   float* ssum = sh;            // [R][C]
   float* ssq = sh + R * C;     // [R][C]
-  if (r < R) {
+  {
     float s[8], q[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) { s[j] = 0.f; q[j] = 0.f; }
@@ -79,8 +92,7 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
     const int p0 = chunk * chunk_pixels, p1 = min(HW, p0 + chunk_pixels);
     const T* base = c < C1 ? x1 + (size_t)n * HW * C1 + c : x2 + (size_t)n * HW * C2 + (c - C1);
     const size_t ld = c < C1 ? C1 : C2;
-    // Rounds of kGnRows pixels per thread, all loads of a round issued before any use, so a whole
-    // round of the chunk is in flight at once.
+    // rounds of kGnRows pixels per thread, every load of a round issued before any use
     for (int pr = p0 + r; pr < p1; pr += kGnRows * R) {
       uint4 raw[kGnRows];  // 16-bit inputs: eight channels per 16-byte load
 #pragma unroll
@@ -105,7 +117,7 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
     for (int j = 0; j < 8; ++j) { ssum[r * C + c + j] = s[j]; ssq[r * C + c + j] = q[j]; }
   }
   __syncthreads();
-  for (int cc = t; cc < C; cc += blockDim.x) {  // fold the R rows per channel (fixed order)
+  for (int cc = tid; cc < C; cc += nthr) {  // fold the R rows per channel (fixed order)
     float s = 0.f, q = 0.f;
     for (int rr = 0; rr < R; ++rr) { s += ssum[rr * C + cc]; q += ssq[rr * C + cc]; }
     ssum[cc] = s;
@@ -113,36 +125,51 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
   }
   __syncthreads();
   const int cpg = C / G;
-  for (int g = t; g < G; g += blockDim.x) {
+  for (int g = tid; g < G; g += nthr) {
     float s = 0.f, q = 0.f;
     for (int cc = g * cpg; cc < (g + 1) * cpg; ++cc) { s += ssum[cc]; q += ssq[cc]; }
-    partial[((size_t)n * nchunks + chunk) * G + g] = make_float2(s, q);
+    s_grp[2 * g] = s;
+    s_grp[2 * g + 1] = q;
   }
+  cluster_sync();  // every CTA of the cluster has its group sums in shared memory
+  const uint32_t rank = cluster_ctarank();
+  uint32_t csize;
+  asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
+  if (rank == 0) {
+    const uint32_t base_addr = smem_u32(s_grp);
+    for (int g = tid; g < G; g += nthr) {
+      float s = 0.f, q = 0.f;
+      for (uint32_t k = 0; k < csize; ++k) {
+        const uint32_t a = mapa_shared(base_addr, k) + 8u * g;
+        s += ld_dsmem_f32(a);
+        q += ld_dsmem_f32(a + 4);
+      }
+      const int cluster = chunk / (int)csize, ncl = gridDim.x / (int)csize;
+      partial[((size_t)n * ncl + cluster) * G + g] = make_float2(s, q);
+    }
+  }
+  cluster_sync();  // the other CTAs' shared memory stays alive until rank 0 has read it
 }
 
 // Normalise pass.  Block = V threads (one 8-channel vector each) x R pixel rows, so every thread keeps
-// the same 8 channels for the whole grid-stride loop and applies them as one FMA per element with
-// per-thread scale / shift (gamma * rstd, beta - mean * gamma * rstd).  The group statistics are first
-// folded from the partials: all threads stage the (chunk, group) partials of image n in shared memory
-// with independent loads, then each group is summed over the chunks in a fixed order (deterministic).
+// the same 8 channels for the whole grid and applies them as one FMA per element with per-thread
+// scale / shift (gamma * rstd, beta - mean * gamma * rstd); two pixels per thread per round.
 template <typename Tin, typename Tout>
 __global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __restrict__ x2, int C2, int HW, int G,
-                              const float2* __restrict__ partial, int nchunks, const float* __restrict__ gamma,
+                              const float2* __restrict__ partial, int ncl, const float* __restrict__ gamma,
                               const float* __restrict__ beta, float eps, int silu, Tout* __restrict__ y) {
   pdl_begin();
-  extern __shared__ float2 s_part[];  // [nchunks][G]
+  extern __shared__ float2 s_part[];  // [ncl][G]
   __shared__ float s_mean[128], s_rstd[128];
   const int C = C1 + C2, V = C / 8, cpg = C / G;
   const int n = blockIdx.y;
   const int nthr = blockDim.x * blockDim.y, tid = threadIdx.y * blockDim.x + threadIdx.x;
-  const float2* src = partial + (size_t)n * nchunks * G;
-  const int total = nchunks * G;
-#pragma unroll 4
-  for (int k = tid; k < total; k += nthr) s_part[k] = src[k];
+  const float2* src = partial + (size_t)n * ncl * G;
+  for (int k = tid; k < ncl * G; k += nthr) s_part[k] = src[k];
   __syncthreads();
   for (int g = tid; g < G; g += nthr) {
     float s = 0.f, q = 0.f;
-    for (int k = 0; k < nchunks; ++k) {
+    for (int k = 0; k < ncl; ++k) {
       const float2 pq = s_part[k * G + g];
       s += pq.x;
       q += pq.y;
@@ -156,33 +183,32 @@ __global__ void gn_nhwc_apply(const Tin* __restrict__ x1, int C1, const Tin* __r
   __syncthreads();
   const int v = threadIdx.x, c = v * 8;
   if (v >= V) return;
-  float sc[8], sh[8];
+  float sc[8], sf[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int g = (c + j) / cpg;
     sc[j] = s_rstd[g] * __ldg(gamma + c + j);
-    sh[j] = __ldg(beta + c + j) - s_mean[g] * sc[j];
+    sf[j] = __ldg(beta + c + j) - s_mean[g] * sc[j];
   }
   const Tin* base = c < C1 ? x1 + (size_t)n * HW * C1 + c : x2 + (size_t)n * HW * C2 + (c - C1);
   const size_t ld = c < C1 ? C1 : C2;
   Tout* out = y + (size_t)n * HW * C + c;
   const int R = blockDim.y, stride = gridDim.x * R;
-  // four pixels per thread per round, loads issued before any use
-  for (int p0 = blockIdx.x * R + threadIdx.y; p0 < HW; p0 += 4 * stride) {
-    float f[4][8];
+  for (int p0 = blockIdx.x * R + threadIdx.y; p0 < HW; p0 += 2 * stride) {
+    float f[2][8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 2; ++u) {
       const int p = p0 + u * stride;
       if (p < HW) load8<Tin>(base + (size_t)p * ld, f[u]);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < 2; ++u) {
       const int p = p0 + u * stride;
       if (p < HW) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float o = fmaf(f[u][j], sc[j], sh[j]);
-          f[u][j] = silu ? silu_f(o) : o;
+          const float o = fmaf(f[u][j], sc[j], sf[j]);
+          f[u][j] = silu ? __fdividef(o, 1.0f + __expf(-o)) : o;
         }
         store8<Tout>(out + (size_t)p * C, f[u]);
       }
@@ -264,7 +290,15 @@ __global__ void layer_norm_rows(const Tin* __restrict__ x, const float* __restri
 // ---------------------------------------------------------------------------------------------
 // Host entry points (also used by the fused blocks / U-Net plan).
 // ---------------------------------------------------------------------------------------------
-int gn_nhwc_chunks(int HW) { return std::max(1, std::min(64, HW / 16)); }
+// Statistics-pass geometry: chunks of ~32 pixels (at most 128 per image), in clusters of up to 8 CTAs
+// (cl divides chunks); the partial buffer holds chunks / cl = max(1, min(16, HW / 256)) entries per
+// (image, group).
+static void gn_geometry(int HW, int* chunks, int* cl) {
+  int ch = std::max(1, std::min(128, HW / 32));
+  const int k = std::min(8, ch);
+  *chunks = (ch / k) * k;
+  *cl = k;
+}
 
 template <typename Tin, typename Tout>
 static int gn_nhwc_impl(Ctx* c, const Tin* x1, int C1, const Tin* x2, int C2, int N, int HW, int G, float eps,
@@ -272,22 +306,24 @@ static int gn_nhwc_impl(Ctx* c, const Tin* x1, int C1, const Tin* x2, int C2, in
   const int C = C1 + C2;
   if (C % 8 || C1 % 8 || G <= 0 || G > 128 || C % G) return set_error(c, DI_EINVAL, "group_norm_nhwc: bad channels");
   const int V = C / 8;
-  const int R = std::max(1, 6144 / C);  // 2*R*C floats of shared memory <= 48 KB
-  const int threads = R * V;
-  if (threads > 1024) return set_error(c, DI_EUNSUPPORTED, "group_norm_nhwc: too many channels");
-  const int chunks = gn_nhwc_chunks(HW);
+  if (V > 1024) return set_error(c, DI_EUNSUPPORTED, "group_norm_nhwc: too many channels");
+  int chunks, cl;
+  gn_geometry(HW, &chunks, &cl);
+  const int ncl = chunks / cl;
   const int chunk_pixels = (HW + chunks - 1) / chunks;
   if (!partial) {
-    partial = static_cast<float2*>(workspace(c, sizeof(float2) * (size_t)N * chunks * G, 0));
+    partial = static_cast<float2*>(workspace(c, sizeof(float2) * (size_t)N * ncl * G, 0));
     if (!partial) return set_error(c, DI_ENOMEM, "group_norm_nhwc: workspace");
   }
+  const int R = std::max(1, 256 / V);
   const size_t shm = sizeof(float) * 2 * R * C;
-  launch_k(gn_nhwc_partial<Tin>, dim3(chunks, N), threads, shm, c->stream, x1, C1, x2, C2, HW, chunk_pixels, G, partial);
-  // normalise: V x Ra threads per block, about two blocks per SM over the whole batch
+  launch_k_cluster(gn_nhwc_partial<Tin>, dim3(chunks, N), dim3(V, R), shm, c->stream, cl, x1, C1, x2, C2, HW,
+                   chunk_pixels, G, partial);
+  // normalise: V x Ra threads per block, two pixels per thread
   const int Ra = std::max(1, 256 / V);
-  const int ablocks = std::max(1, std::min((HW + 4 * Ra - 1) / (4 * Ra), std::max(1, 2 * c->num_sms / std::max(1, N))));
-  launch_k(gn_nhwc_apply<Tin, Tout>, dim3(ablocks, N), dim3(V, Ra), sizeof(float2) * chunks * G, c->stream, x1, C1, x2,
-           C2, HW, G, partial, chunks, gamma, beta, eps, silu, y);
+  const int ablocks = std::max(1, (HW + 2 * Ra - 1) / (2 * Ra));
+  launch_k(gn_nhwc_apply<Tin, Tout>, dim3(ablocks, N), dim3(V, Ra), sizeof(float2) * ncl * G, c->stream, x1, C1, x2,
+           C2, HW, G, partial, ncl, gamma, beta, eps, silu, y);
   return check_launch(c, "group_norm_nhwc");
 }
 
@@ -307,7 +343,11 @@ int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1,
   return set_error(c, DI_EINVAL, "group_norm_nhwc: dtype combination");
 }
 
-size_t gn_nhwc_ws_bytes(int N, int HW, int G) { return sizeof(float2) * (size_t)N * gn_nhwc_chunks(HW) * G; }
+size_t gn_nhwc_ws_bytes(int N, int HW, int G) {
+  int chunks, cl;
+  gn_geometry(HW, &chunks, &cl);
+  return sizeof(float2) * (size_t)N * (chunks / cl) * G;
+}
 
 int group_norm_nchw(Ctx* c, const float* x, const float* g, const float* b, float* y, int N, int C, int HW, int G,
                     float eps, int silu, int clamp) {

@@ -136,7 +136,7 @@ DI_API int di_group_norm_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, c
  * call cudaMalloc (a fixed, pre-reserved memory budget, an external allocator that owns the device
  * memory, or latency-critical code that must not take allocation locks).  No counterpart in the
  * reference.  Its scratch is a fixed 1 MiB array inside the library (kept on every GPU that loads the
- * library until the process exits): sizes needing more than N * min(64, max(1, HW/16)) * G * 8 =
+ * library until the process exits): sizes needing more than N * max(1, min(16, HW/256)) * G * 8 =
  * 1 MiB are rejected with DI_EINVAL.  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress), so make that first call before any stream capture.  All calls share the one
  * array: calls that may overlap on the GPU (different streams or contexts on the same device) race and

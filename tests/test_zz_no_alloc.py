@@ -45,12 +45,12 @@ def test_noalloc_matches_group_norm_on_two_calls(ctx, dib):
 
 def test_noalloc_rejects_oversize(ctx, dib):
     import torch
-    # N=64 images x 64 chunks x 32 groups x 8 B = 1 MiB + 0 -> fits; N=65 needs more than the fixed 1 MiB
-    x = torch.zeros((65, 4096, 64), dtype=torch.float16, device="cuda")
+    # N=256 images x 16 cluster partials x 32 groups x 8 B = 1 MiB -> fits; N=257 needs more than the fixed 1 MiB
+    x = torch.zeros((257, 4096, 64), dtype=torch.float16, device="cuda")
     g = torch.ones(64, device="cuda")
     b = torch.zeros(64, device="cuda")
     y = torch.empty_like(x)
-    rc = dib.lib().di_group_norm_nhwc_noalloc(ctx.h, 1, x.data_ptr(), 64, None, 0, 65, 4096, 32, 1e-5, g.data_ptr(),
+    rc = dib.lib().di_group_norm_nhwc_noalloc(ctx.h, 1, x.data_ptr(), 64, None, 0, 257, 4096, 32, 1e-5, g.data_ptr(),
                                               b.data_ptr(), 0, y.data_ptr())
     assert rc == dib.DI_EINVAL
     assert b"fixed maximum" in dib.lib().di_last_error(ctx.h)
