@@ -26,6 +26,13 @@ namespace di {
 // ---------------------------------------------------------------------------------------------
 // Host-side context
 // ---------------------------------------------------------------------------------------------
+// GroupNorm(+SiLU) applied to a GEMM's A operand as it is loaded: tab[n][c] = (scale, shift) per image
+// and input channel (from gn_table_nhwc); rows of image n get x * scale + shift, then SiLU if `silu`.
+struct GnFuse {
+  const float2* tab;
+  int silu;
+};
+
 struct Ctx {
   int device = 0;
   cudaStream_t stream = nullptr;

@@ -56,6 +56,11 @@ struct GemmParams {
   float* partial;  // [splits][M][N] fp32 when splits > 1
   int* err;
   unsigned long long* trace;  // diagnostics: kTracePoints %globaltimer stamps per CTA, or null
+  // GroupNorm(+SiLU) of the A operand (GnFuse): applied in shared memory by the epilogue warps between
+  // the TMA load and the MMA; gn_C = input channels, gn_HW = pixels per image, conv_bh = image rows
+  // per 128-row conv tile.
+  const float2* gn_tab;
+  int gn_silu, gn_C, gn_HW, conv_bh;
 };
 
 // Diagnostics: per-CTA timeline points of the first work unit (di_debug_gemm_trace).
@@ -76,7 +81,7 @@ struct GemmSmem {
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // a pair splits B's rows
   static constexpr uint32_t EPI_BYTES = kEpiWarps * 4096;  // one 32 x 128 B staging slab per epilogue warp
-  static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + 256;  // + align + barriers
+  static constexpr uint32_t TOTAL = 1024 + STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + 512;  // + align + barriers
 };
 
 __device__ __forceinline__ void store_row32(void* out, size_t off, const float* v, int out_f32, bool bf16) {
@@ -149,7 +154,7 @@ __device__ __forceinline__ void store_one(void* dst, size_t off, float v, int is
 // traffic per FLOP.  The leader (rank 0) issues the MMAs; the peer's TMA loads count their bytes on the
 // leader's `full` barrier; MMA commits arrive on `empty` / `tfull` in both CTAs; both CTAs' epilogue
 // warps release the accumulator on the leader's `tempty`.  Units then index 256-row M tiles.
-template <int BN, int STAGES, bool BF16, bool PAIR = false>
+template <int BN, int STAGES, bool BF16, bool PAIR = false, bool XF = false>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmSmem<BN, STAGES, PAIR>;
   constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
@@ -163,7 +168,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;  // [2] accumulator ready
   uint64_t* tempty = tfull + 2;      // [2] accumulator drained by the epilogue
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* afull = tempty + 2;       // [STAGES] this CTA's A tile landed (operand-fused GroupNorm only)
+  uint64_t* aready = afull + STAGES;  // [STAGES] A tiles transformed (on the pair leader: both CTAs')
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aready + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -177,7 +184,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   const int kper = (p.num_k + p.splits - 1) / p.splits;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&afull[s], 1);
+      mbar_init(&aready[s], (PAIR ? 2 : 1) * kEpiWarps);  // one arrival per transforming warp
+    }
     // tempty: one arrival per epilogue warp (of both CTAs of a pair, on the leader's barrier)
     for (int s = 0; s < 2; ++s) { mbar_init(&tfull[s], 1); mbar_init(&tempty[s], (PAIR ? 2 : 1) * kEpiWarps); }
     *abort_flag = 0;
@@ -193,6 +205,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   tc_fence_after();
   const uint32_t full0_leader = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
   const uint32_t tempty_leader = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
+  const uint32_t aready_leader = PAIR ? mapa_shared(smem_u32(aready), 0) : smem_u32(aready);
+  constexpr bool xform = XF;  // operand-fused GroupNorm (p.gn_tab): a separate instantiation
   const uint32_t tmem = *tmem_slot;
   if (tr && threadIdx.x == 0) tr[1] = globaltimer();
   // Programmatic dependent launch: let the next kernel be scheduled right away.  Everything before
@@ -218,16 +232,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       // Weight tiles of the first ring stages are requested before the dependency wait (constant data).
       // In a pair, rank r loads B rows n0 + r * BN/2 .. and only the leader arms `full` (both CTAs' bytes).
       const int brow = PAIR ? (int)rank * (BN / 2) : 0;
-      auto arm = [&](int s) {
-        if (!PAIR) mbar_arrive_expect_tx(&full[s], STAGE_TX);
-        else if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_TX);
+      // `full` counts the bytes the MMA needs; with the fused GroupNorm the A tile instead lands on this
+      // CTA's own `afull` (for the transforming warps) and `full` only counts B.
+      auto armB = [&](int s) {
+        const uint32_t tx = xform ? S::B_BYTES : STAGE_TX;
+        if (!PAIR) mbar_arrive_expect_tx(&full[s], tx);
+        else if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * tx);
+      };
+      auto armA = [&](int s) {
+        if (xform) mbar_arrive_expect_tx(&afull[s], S::A_BYTES);
       };
       auto load2 = [&](void* dst, const CUtensorMap* m, int s, int c0, int c1) {
         if (PAIR) tma_load_2d_pair(dst, m, full0_leader + s * 8, c0, c1);
         else tma_load_2d(dst, m, &full[s], c0, c1);
       };
-      auto load4 = [&](void* dst, const CUtensorMap* m, int s, int c0, int c1, int c2, int c3) {
-        if (PAIR) tma_load_4d_pair(dst, m, full0_leader + s * 8, c0, c1, c2, c3);
+      auto loadA2 = [&](void* dst, const CUtensorMap* m, int s, int c0, int c1) {
+        if (xform) tma_load_2d(dst, m, &afull[s], c0, c1);
+        else load2(dst, m, s, c0, c1);
+      };
+      auto loadA4 = [&](void* dst, const CUtensorMap* m, int s, int c0, int c1, int c2, int c3) {
+        if (xform) tma_load_4d(dst, m, &afull[s], c0, c1, c2, c3);
+        else if (PAIR) tma_load_4d_pair(dst, m, full0_leader + s * 8, c0, c1, c2, c3);
         else tma_load_4d(dst, m, &full[s], c0, c1, c2, c3);
       };
       int npre = 0;
@@ -236,7 +261,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         decode(cta0, m0, n0, sp, kb0, kb1);
         npre = p.b_early ? min(STAGES, kb1 - kb0) : 0;
         for (int i = 0; i < npre; ++i) {
-          arm(i);
+          armB(i);
           load2(sB + i * S::B_BYTES, &p.tmB, i, (kb0 + i) * BK, n0 + brow);
         }
       }
@@ -254,21 +279,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           const bool pre = it < npre;  // B already requested, barrier already armed
           if (!pre) {
             if (*abort_flag || !mbar_wait<PAIR>(&empty[s], ph ^ 1, p.err, DEVERR_WAIT_TMA)) { *abort_flag = 1; break; }
-            arm(s);
+            armB(s);
           }
+          armA(s);
           uint8_t* dA = sA + s * S::A_BYTES;
           if (p.mode == 0) {
-            if (kb < p.k_split) load2(dA, &p.tmA[0], s, kb * BK, m0);
-            else load2(dA, &p.tmA[1], s, (kb - p.k_split) * BK, m0);
+            if (kb < p.k_split) loadA2(dA, &p.tmA[0], s, kb * BK, m0);
+            else loadA2(dA, &p.tmA[1], s, (kb - p.k_split) * BK, m0);
           } else {
             const int tap = kb / p.cin_blocks, cb = kb % p.cin_blocks;
             const int ky = tap / 3, kx = tap % 3;
             if (p.mode == 1) {
               const bool first = cb < p.k_split;
-              load4(dA, &p.tmA[first ? 0 : 1], s, (first ? cb : cb - p.k_split) * BK, kx - 1, y0 + ky - 1, img);
+              loadA4(dA, &p.tmA[first ? 0 : 1], s, (first ? cb : cb - p.k_split) * BK, kx - 1, y0 + ky - 1, img);
             } else {
               const int py = ky == 1 ? 0 : 1, px = kx == 1 ? 0 : 1;
-              load4(dA, &p.tmA[py * 2 + px], s, cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0), img);
+              loadA4(dA, &p.tmA[py * 2 + px], s, cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0), img);
             }
           }
           if (!pre) load2(sB + s * S::B_BYTES, &p.tmB, s, kb * BK, n0 + brow);
@@ -299,7 +325,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (*abort_flag || !mbar_wait<PAIR>(&full[s], ph, p.err, DEVERR_WAIT_MMA)) { *abort_flag = 1; ok = false; break; }
+          if (*abort_flag || !mbar_wait<PAIR>(&full[s], ph, p.err, DEVERR_WAIT_MMA) ||
+              (xform && !mbar_wait<PAIR>(&aready[s], ph, p.err, DEVERR_WAIT_MMA))) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
           if (tr && lt == 0 && kb == kb0) tr[3] = globaltimer();
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * S::A_BYTES), b0 = smem_u32(sB + s * S::B_BYTES);
@@ -327,12 +358,133 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     const int row = q * 32 + lane;
     const int half = (warp - 2) / 4;  // which alternate column chunks this warp handles
     uint8_t* stg = sEpi + (warp - 2) * 4096;
-    int lt = 0;
+    int lt = 0, xit = 0;
     for (int u = cta0; u < units; u += cstride, ++lt) {
       int m0, n0, sp, kb0, kb1;
       decode(u, m0, n0, sp, kb0, kb1);
       const int ab = lt & 1;
       const int m = m0 + row;
+      if (xform) {
+        // ---- operand-fused GroupNorm: normalise (+SiLU) this unit's A tiles in shared memory ----
+        // Thread tt handles the 16-byte chunks tt + 256 i (i < 4) of the 128 x 8-chunk tile: a warp
+        // instruction covers four whole 128-byte rows (bank-conflict free).  Rows outside the image
+        // (conv padding, zero-filled by TMA) and rows past M are left as loaded (zero).
+        const int tt = (warp - 2) * 32 + lane, pc = tt & 7;
+        int r_img[4], r_y[4], r_x[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rw = (tt >> 3) + 32 * i, mr = m0 + rw;
+          r_y[i] = 0;
+          r_x[i] = 0;
+          if (p.mode == 0) {
+            r_img[i] = mr < p.M ? mr / p.gn_HW : -1;
+          } else {
+            const int rr = rw / p.Wo;
+            r_x[i] = rw % p.Wo;
+            r_img[i] = mr < p.M ? m0 / p.HWo + rr / p.conv_bh : -1;
+            r_y[i] = (m0 % p.HWo) / p.Wo + rr % p.conv_bh;
+          }
+        }
+        const int Ho = p.mode == 0 ? 0 : p.HWo / p.Wo;
+        // The unit's (scale, shift) rows are staged in the epilogue slabs (free until this unit's
+        // epilogue; the barrier keeps the previous unit's epilogue stores out of the way) when they fit,
+        // so the per-K-block lookups are shared-memory reads instead of global-memory round trips.
+        const int img_lo = m0 / p.gn_HW, img_hi = (min(m0 + BM, p.M) - 1) / p.gn_HW;
+        const int tab_n = (img_hi - img_lo + 1) * p.gn_C;  // (scale, shift) pairs
+        const bool tab_smem = tab_n * 8 <= (int)S::EPI_BYTES;
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
+        if (tab_smem) {
+          const float4* src = reinterpret_cast<const float4*>(p.gn_tab + (size_t)img_lo * p.gn_C);
+          float4* dst = reinterpret_cast<float4*>(sEpi);
+          for (int i = tt; i < tab_n / 2; i += 32 * kEpiWarps) dst[i] = __ldg(src + i);
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
+        const float4* tab_base = tab_smem ? reinterpret_cast<const float4*>(sEpi) - (size_t)img_lo * p.gn_C / 2
+                                          : reinterpret_cast<const float4*>(p.gn_tab);
+        for (int kb = kb0; kb < kb1; ++kb, ++xit) {
+          const int s = xit % STAGES;
+          const uint32_t ph = (xit / STAGES) & 1;
+          if (tr && lt == 0 && threadIdx.x == 64 && kb == kb0) tr[8] = globaltimer();
+          const bool okx = mbar_wait(&afull[s], ph, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
+          if (tr && lt == 0 && threadIdx.x == 64 && kb == kb0) tr[9] = globaltimer();
+          if (tr && lt == 0 && threadIdx.x == 64 && kb == kb0 + 1) tr[12] = globaltimer();
+          int gch, dy = 0, dx = 0;
+          if (p.mode == 0) {
+            gch = kb * BK;
+          } else {
+            const int tap = kb / p.cin_blocks;
+            gch = (kb % p.cin_blocks) * BK;
+            dy = tap / 3 - 1;
+            dx = tap % 3 - 1;
+          }
+          uint8_t* tile = sA + s * S::A_BYTES;
+          // all loads of the four chunks first (independent), then the arithmetic, then the stores
+          uint4 raw[4];
+          float4 tv[4][4];
+          bool vld[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rw = (tt >> 3) + 32 * i;
+            bool valid = okx && r_img[i] >= 0;
+            if (p.mode != 0)
+              valid = valid && (unsigned)(r_y[i] + dy) < (unsigned)Ho && (unsigned)(r_x[i] + dx) < (unsigned)p.Wo;
+            vld[i] = valid;
+            const int lc = pc ^ (rw & 7);  // 128B swizzle: physical chunk pc of row rw holds logical chunk lc
+            const float4* tb = tab_base + ((size_t)(valid ? r_img[i] : img_lo) * p.gn_C + gch + lc * 8) / 2;
+            raw[i] = *reinterpret_cast<const uint4*>(tile + rw * 128 + pc * 16);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) tv[i][e] = tb[e];  // (scale, shift) of channels 2e, 2e + 1
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float4 t = tv[i][e];
+              float2 f;
+              if (BF16) f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
+              else f = __half22float2(*reinterpret_cast<__half2*>(&w[e]));
+              const float y0 = fmaf(f.x, t.x, t.y), y1 = fmaf(f.y, t.z, t.w);
+              if (BF16) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(y0, y1);
+                if (p.gn_silu) {  // silu(y) = y * (0.5 + 0.5 tanh(y / 2))
+                  __nv_bfloat162 hh = __hmul2(h, __floats2bfloat162_rn(0.5f, 0.5f));
+                  uint32_t th, hv = *reinterpret_cast<uint32_t*>(&hh);
+                  asm("tanh.approx.bf16x2 %0, %1;" : "=r"(th) : "r"(hv));
+                  const __nv_bfloat162 sg = __hfma2(*reinterpret_cast<__nv_bfloat162*>(&th),
+                                                    __floats2bfloat162_rn(0.5f, 0.5f), __floats2bfloat162_rn(0.5f, 0.5f));
+                  h = __hmul2(h, sg);
+                }
+                w[e] = *reinterpret_cast<uint32_t*>(&h);
+              } else {
+                __half2 h = __floats2half2_rn(y0, y1);
+                if (p.gn_silu) {
+                  __half2 hh = __hmul2(h, __float2half2_rn(0.5f));
+                  uint32_t th, hv = *reinterpret_cast<uint32_t*>(&hh);
+                  asm("tanh.approx.f16x2 %0, %1;" : "=r"(th) : "r"(hv));
+                  const __half2 sg = __hfma2(*reinterpret_cast<__half2*>(&th), __float2half2_rn(0.5f), __float2half2_rn(0.5f));
+                  h = __hmul2(h, sg);
+                }
+                w[e] = *reinterpret_cast<uint32_t*>(&h);
+              }
+            }
+            // padding rows (TMA zero fill) and rows past M keep their loaded zeros
+            if (vld[i])
+              *reinterpret_cast<uint4*>(tile + ((tt >> 3) + 32 * i) * 128 + pc * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+#ifndef DI_XF_NOFENCE
+          fence_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+#endif
+          __syncwarp();
+#ifdef DI_XF_CTA_ARRIVE
+          if (lane == 0) mbar_arrive(&aready[s]);
+#else
+          if (lane == 0) mbar_arrive_cluster(aready_leader + s * 8);
+#endif
+          if (tr && lt == 0 && threadIdx.x == 64 && kb == kb0) tr[10] = globaltimer();
+          if (tr && lt == 0 && threadIdx.x == 64 && kb == kb1 - 1) tr[11] = globaltimer();
+        }
+      }
       const bool okw = mbar_wait<PAIR>(&tfull[ab], (lt >> 1) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
       const bool ok = __all_sync(0xffffffffu, okw);
       if (tr && lt == 0 && threadIdx.x == 64) tr[5] = globaltimer();
@@ -517,10 +669,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
 // Pairs of CTAs that can be resident at once (clusters of 2 need both SMs in one GPC), per device.
 static int g_max_pairs[32] = {0};
 
-template <int BN, int STAGES, bool BF16, bool PAIR>
+template <int BN, int STAGES, bool BF16, bool PAIR, bool XF>
 int launch_variant(Ctx* c, const GemmParams& p) {
   using S = GemmSmem<BN, STAGES, PAIR>;
-  auto kern = gemm_tc_kernel<BN, STAGES, BF16, PAIR>;
+  auto kern = gemm_tc_kernel<BN, STAGES, BF16, PAIR, XF>;
   static unsigned attr_done = 0;  // per-device bit: dynamic smem opt-in is a per-device attribute
   if (!(attr_done & (1u << (c->device & 31)))) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) != cudaSuccess)
@@ -547,7 +699,7 @@ static int max_pairs(Ctx* c) {
   int& mp = g_max_pairs[c->device & 31];
   if (mp) return mp;
   using S = GemmSmem<256, 6, true>;
-  auto kern = gemm_tc_kernel<256, 6, false, true>;
+  auto kern = gemm_tc_kernel<256, 6, false, true, false>;
   mp = c->num_sms / 2;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
@@ -697,21 +849,26 @@ int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
   return s > 1 ? 2 : 1;
 }
 
-static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
+template <bool XF>
+static int dispatch_xf(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
   if (pair) {
     switch (bn) {
-      case 256: return bf16 ? launch_variant<256, 6, true, true>(c, p) : launch_variant<256, 6, false, true>(c, p);
-      case 192: return bf16 ? launch_variant<192, 6, true, true>(c, p) : launch_variant<192, 6, false, true>(c, p);
-      case 160: return bf16 ? launch_variant<160, 7, true, true>(c, p) : launch_variant<160, 7, false, true>(c, p);
-      default: return bf16 ? launch_variant<128, 8, true, true>(c, p) : launch_variant<128, 8, false, true>(c, p);
+      case 256: return bf16 ? launch_variant<256, 6, true, true, XF>(c, p) : launch_variant<256, 6, false, true, XF>(c, p);
+      case 192: return bf16 ? launch_variant<192, 6, true, true, XF>(c, p) : launch_variant<192, 6, false, true, XF>(c, p);
+      case 160: return bf16 ? launch_variant<160, 7, true, true, XF>(c, p) : launch_variant<160, 7, false, true, XF>(c, p);
+      default: return bf16 ? launch_variant<128, 8, true, true, XF>(c, p) : launch_variant<128, 8, false, true, XF>(c, p);
     }
   }
   switch (bn) {
-    case 256: return bf16 ? launch_variant<256, 4, true, false>(c, p) : launch_variant<256, 4, false, false>(c, p);
-    case 192: return bf16 ? launch_variant<192, 4, true, false>(c, p) : launch_variant<192, 4, false, false>(c, p);
-    case 160: return bf16 ? launch_variant<160, 5, true, false>(c, p) : launch_variant<160, 5, false, false>(c, p);
-    default: return bf16 ? launch_variant<128, 6, true, false>(c, p) : launch_variant<128, 6, false, false>(c, p);
+    case 256: return bf16 ? launch_variant<256, 4, true, false, XF>(c, p) : launch_variant<256, 4, false, false, XF>(c, p);
+    case 192: return bf16 ? launch_variant<192, 4, true, false, XF>(c, p) : launch_variant<192, 4, false, false, XF>(c, p);
+    case 160: return bf16 ? launch_variant<160, 5, true, false, XF>(c, p) : launch_variant<160, 5, false, false, XF>(c, p);
+    default: return bf16 ? launch_variant<128, 6, true, false, XF>(c, p) : launch_variant<128, 6, false, false, XF>(c, p);
   }
+}
+
+static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
+  return p.gn_tab ? dispatch_xf<true>(c, p, bn, bf16, pair) : dispatch_xf<false>(c, p, bn, bf16, pair);
 }
 
 int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, void* splitk_ws) {
@@ -793,7 +950,7 @@ static GemmParams base_params() {
 // Public building blocks used by the fused blocks and the U-Net plan ---------------------------
 int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
                 const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
-                int rowvec_div, void* splitk_ws) {
+                int rowvec_div, void* splitk_ws, const GnFuse* gnf, int gnf_hw) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 64 || (X2 && (K1 <= 0 || K1 % 64 || K1 >= K)))
     return set_error(c, DI_EINVAL, "linear: K and K1 must be multiples of 64");
   if (geglu && (N % 128)) return set_error(c, DI_EINVAL, "linear_geglu: F must be a multiple of 64");
@@ -827,6 +984,13 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
   p.geglu = geglu;
   p.vec_ok = vec_rows_ok(Y, p.ldo, out_f32 ? 4 : 2) && (!R || vec_rows_ok(R, N, res_f32 ? 4 : 2));
   (void)bn;
+  if (gnf && gnf->tab) {  // rows are pixels of images of gnf_hw pixels (GnFuse on a 1x1 projection)
+    if (gnf_hw <= 0) return set_error(c, DI_EINVAL, "linear: fused GroupNorm needs the pixels per image");
+    p.gn_tab = gnf->tab;
+    p.gn_silu = gnf->silu;
+    p.gn_C = K;
+    p.gn_HW = gnf_hw;
+  }
   int chosen, splits;
   int pair;
   choose_tiling(c, M, N, p.num_k, geglu, &chosen, &splits, &pair);
@@ -836,7 +1000,7 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
 
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
-                 void* y, int out_f32, int temb_ld, void* splitk_ws) {
+                 void* y, int out_f32, int temb_ld, void* splitk_ws, const GnFuse* gnf) {
   if (C1 <= 0 || C1 % 64 || (x2 && (C2 <= 0 || C2 % 64)) || Co % 16 || (stride != 1 && stride != 2))
     return set_error(c, DI_EINVAL, "conv3x3: channels must be multiples of 64 (Co of 16), stride 1 or 2");
   if (stride == 2 && (x2 || (H % 2) || (W % 2)))
@@ -880,6 +1044,14 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
   p.ldo = Co;
   p.out_f32 = out_f32;
   p.vec_ok = vec_rows_ok(y, Co, out_f32 ? 4 : 2) && (!residual || vec_rows_ok(residual, Co, res_f32 ? 4 : 2));
+  if (gnf && gnf->tab) {
+    if (stride != 1) return set_error(c, DI_EUNSUPPORTED, "conv3x3: fused GroupNorm needs stride 1");
+    p.gn_tab = gnf->tab;
+    p.gn_silu = gnf->silu;
+    p.gn_C = Cin;
+    p.gn_HW = H * W;
+    p.conv_bh = (int)bh;
+  }
   int chosen, splits;
   int pair;
   choose_tiling(c, p.M, Co, p.num_k, 0, &chosen, &splits, &pair);
@@ -925,14 +1097,15 @@ int di_linear(di_ctx_t h, int dtype, const void* X1, int K1, const void* X2, int
               const float* bias, const void* R, void* Y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
-  return gemm_linear(c, dtype, X1, K1, X2, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1, nullptr);
+  return gemm_linear(c, dtype, X1, K1, X2, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1, nullptr, nullptr, 0);
 }
 
 int di_linear_geglu(di_ctx_t h, int dtype, const void* X, int M, int K, const void* W, int F, const float* bias,
                     void* Y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16) || F % 64) return DI_EINVAL;
-  return gemm_linear(c, dtype, X, K, nullptr, M, K, W, 2 * F, bias, nullptr, 0, Y, 0, 1, nullptr, 1, nullptr);
+  return gemm_linear(c, dtype, X, K, nullptr, M, K, W, 2 * F, bias, nullptr, 0, Y, 0, 1, nullptr, 1, nullptr, nullptr,
+                     0);
 }
 
 int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,
@@ -940,7 +1113,17 @@ int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x
                     void* y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
-  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr);
+  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr,
+                      nullptr);
+}
+
+int di_conv3x3_nhwc_gn(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,
+                       const void* Wt, int Co, const float* bias, const float* temb, const void* residual,
+                       const float* gn_table, int silu, void* y) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16) || !gn_table) return DI_EINVAL;
+  const GnFuse f{reinterpret_cast<const float2*>(gn_table), silu ? 1 : 0};
+  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, 1, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr, &f);
 }
 
 int di_pack_conv3x3(di_ctx_t h, int dtype, const float* w, int Co, int Ci, void* out) {

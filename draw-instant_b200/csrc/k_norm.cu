@@ -151,6 +151,129 @@ __global__ void gn_nhwc_partial(const T* __restrict__ x1, int C1, const T* __res
   cluster_sync();  // the other CTAs' shared memory stays alive until rank 0 has read it
 }
 
+// GroupNorm folded into a consumer's operand load: one cluster of kTabCluster CTAs per image computes
+// the group statistics (each CTA a slice of the pixels, folded by the rank-0 CTA through distributed
+// shared memory in fixed rank order) and writes the per-channel affine of the normalisation,
+// table[n][c] = (scale, shift) with scale = gamma[c] * rstd[g], shift = beta[c] - mean[g] * scale,
+// so the consumer applies y = x * scale + shift (then SiLU) to the raw activations as it loads them.
+constexpr int kTabCluster = 16;
+
+template <typename T>
+__global__ void gn_table_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2, int HW, int G,
+                                float eps, const float* __restrict__ gamma, const float* __restrict__ beta,
+                                float2* __restrict__ table) {
+  pdl_begin();
+  extern __shared__ float sh[];
+  __shared__ float s_grp[2 * 128];
+  __shared__ float s_mean[128], s_rstd[128];
+  const int C = C1 + C2, V = blockDim.x, R = blockDim.y;
+  const int n = blockIdx.y, rank = (int)cluster_ctarank();
+  const int v = threadIdx.x, r = threadIdx.y, tid = r * V + v, nthr = V * R;
+  const int per = (HW + kTabCluster - 1) / kTabCluster;
+  float* ssum = sh;         // [R][C]
+  float* ssq = sh + R * C;  // [R][C]
+  {
+    float s[8], q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { s[j] = 0.f; q[j] = 0.f; }
+    const int c = v * 8;
+    const int p0 = rank * per, p1 = min(HW, p0 + per);
+    const T* base = c < C1 ? x1 + (size_t)n * HW * C1 + c : x2 + (size_t)n * HW * C2 + (c - C1);
+    const size_t ld = c < C1 ? C1 : C2;
+    for (int pr = p0 + r; pr < p1; pr += kGnRows * R) {
+      uint4 raw[kGnRows];
+#pragma unroll
+      for (int u = 0; u < kGnRows; ++u) {
+        const int p = pr + u * R;
+        if constexpr (sizeof(T) == 2)
+          if (p < p1) raw[u] = __ldg(reinterpret_cast<const uint4*>(base + (size_t)p * ld));
+      }
+#pragma unroll
+      for (int u = 0; u < kGnRows; ++u) {
+        const int p = pr + u * R;
+        if (p < p1) {
+          float f[8];
+          if constexpr (sizeof(T) == 4) load8<T>(base + (size_t)p * ld, f);
+          else load8<T>(reinterpret_cast<const T*>(&raw[u]), f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) { s[j] += f[j]; q[j] += f[j] * f[j]; }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { ssum[r * C + c + j] = s[j]; ssq[r * C + c + j] = q[j]; }
+  }
+  __syncthreads();
+  for (int cc = tid; cc < C; cc += nthr) {
+    float s = 0.f, q = 0.f;
+    for (int rr = 0; rr < R; ++rr) { s += ssum[rr * C + cc]; q += ssq[rr * C + cc]; }
+    ssum[cc] = s;
+    ssq[cc] = q;
+  }
+  __syncthreads();
+  const int cpg = C / G;
+  for (int g = tid; g < G; g += nthr) {
+    float s = 0.f, q = 0.f;
+    for (int cc = g * cpg; cc < (g + 1) * cpg; ++cc) { s += ssum[cc]; q += ssq[cc]; }
+    s_grp[2 * g] = s;
+    s_grp[2 * g + 1] = q;
+  }
+  cluster_sync();
+  if (rank == 0) {
+    const uint32_t base_addr = smem_u32(s_grp);
+    for (int g = tid; g < G; g += nthr) {
+      float s = 0.f, q = 0.f;
+      for (int k = 0; k < kTabCluster; ++k) {
+        const uint32_t a = mapa_shared(base_addr, (uint32_t)k) + 8u * g;
+        s += ld_dsmem_f32(a);
+        q += ld_dsmem_f32(a + 4);
+      }
+      const float cnt = (float)cpg * (float)HW;
+      const float mean = s / cnt;
+      const float var = fmaxf(q / cnt - mean * mean, 0.0f);
+      s_mean[g] = mean;
+      s_rstd[g] = 1.0f / sqrtf(var + eps);
+    }
+    __syncthreads();
+    for (int cc = tid; cc < C; cc += nthr) {
+      const int g = cc / cpg;
+      const float sc = s_rstd[g] * gamma[cc];
+      table[(size_t)n * C + cc] = make_float2(sc, beta[cc] - s_mean[g] * sc);
+    }
+  }
+  cluster_sync();
+}
+
+// Normalise with a precomputed (scale, shift) table (gn_table_nhwc): one 8-channel vector per thread,
+// y = silu?(x * scale + shift); table rows are read through L1 (they are tiny and shared by all pixels).
+template <typename Tin, typename Tout>
+__global__ void gn_apply_table(const Tin* __restrict__ x1, int C1, const Tin* __restrict__ x2, int C2, int HW,
+                               const float2* __restrict__ table, int silu, size_t total, Tout* __restrict__ y) {
+  pdl_begin();
+  const int C = C1 + C2, V = C / 8;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int v = (int)(e % V);
+    const size_t pix = e / V;  // n * HW + p
+    const int n = (int)(pix / HW), c = v * 8;
+    float f[8];
+    if (c < C1) load8<Tin>(x1 + pix * C1 + c, f);
+    else load8<Tin>(x2 + pix * C2 + (c - C1), f);
+    const float4* t = reinterpret_cast<const float4*>(table + (size_t)n * C + c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 q = __ldg(t + j);
+      float a = fmaf(f[2 * j], q.x, q.y), b = fmaf(f[2 * j + 1], q.z, q.w);
+      if (silu) {
+        a = __fdividef(a, 1.0f + __expf(-a));
+        b = __fdividef(b, 1.0f + __expf(-b));
+      }
+      f[2 * j] = a;
+      f[2 * j + 1] = b;
+    }
+    store8<Tout>(y + pix * C + c, f);
+  }
+}
+
 // Normalise pass.  Block = V threads (one 8-channel vector each) x R pixel rows, so every thread keeps
 // the same 8 channels for the whole grid and applies them as one FMA per element with per-thread
 // scale / shift (gamma * rstd, beta - mean * gamma * rstd); two pixels per thread per round.
@@ -343,6 +466,55 @@ int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1,
   return set_error(c, DI_EINVAL, "group_norm_nhwc: dtype combination");
 }
 
+// Statistics of concat(x1, x2) -> table[N][C] of (scale, shift) for an operand-fused GroupNorm.
+int gn_table_nhwc(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G, float eps,
+                  const float* gamma, const float* beta, float2* table) {
+  const int C = C1 + C2;
+  if (C % 8 || C1 % 8 || G <= 0 || G > 128 || C % G || N <= 0 || HW <= 0)
+    return set_error(c, DI_EINVAL, "gn_table_nhwc: bad shape");
+  const int V = C / 8;
+  if (V > 1024) return set_error(c, DI_EUNSUPPORTED, "gn_table_nhwc: too many channels");
+  const int R = std::max(1, 256 / V);
+  const size_t shm = sizeof(float) * 2 * R * C;
+  static unsigned attr_done = 0;  // per-device bit: clusters of 16 need the non-portable size opt-in
+  if (!(attr_done & (1u << (c->device & 31)))) {
+    if (cudaFuncSetAttribute(gn_table_kernel<__half>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(gn_table_kernel<__nv_bfloat16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+            cudaSuccess)
+      return set_error(c, DI_ECUDA, "gn_table_nhwc: cluster attribute");
+    attr_done |= 1u << (c->device & 31);
+  }
+  if (dtype == DI_BF16)
+    launch_k_cluster(gn_table_kernel<__nv_bfloat16>, dim3(kTabCluster, N), dim3(V, R), shm, c->stream, kTabCluster,
+                     static_cast<const __nv_bfloat16*>(x1), C1, static_cast<const __nv_bfloat16*>(x2), C2, HW, G, eps,
+                     gamma, beta, table);
+  else
+    launch_k_cluster(gn_table_kernel<__half>, dim3(kTabCluster, N), dim3(V, R), shm, c->stream, kTabCluster,
+                     static_cast<const __half*>(x1), C1, static_cast<const __half*>(x2), C2, HW, G, eps, gamma, beta,
+                     table);
+  return check_launch(c, "gn_table_nhwc");
+}
+
+// GroupNorm(+SiLU) of concat(x1, x2) through the statistics table: two launches (cluster statistics,
+// then a fully parallel elementwise normalise).  `table` holds N * C (scale, shift) pairs.
+int gn_nhwc_via_table(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                      float eps, const float* gamma, const float* beta, int silu, void* y, float2* table) {
+  int r = gn_table_nhwc(c, dtype, x1, C1, x2, C2, N, HW, G, eps, gamma, beta, table);
+  if (r) return r;
+  const int C = C1 + C2;
+  const size_t total = (size_t)N * HW * (C / 8);
+  const int blocks = (int)std::max<size_t>(1, std::min<size_t>((total + 255) / 256, (size_t)16 * c->num_sms));
+  if (dtype == DI_BF16)
+    launch_k(gn_apply_table<__nv_bfloat16, __nv_bfloat16>, blocks, 256, 0, c->stream,
+             static_cast<const __nv_bfloat16*>(x1), C1, static_cast<const __nv_bfloat16*>(x2), C2, HW, table, silu,
+             total, static_cast<__nv_bfloat16*>(y));
+  else
+    launch_k(gn_apply_table<__half, __half>, blocks, 256, 0, c->stream, static_cast<const __half*>(x1), C1,
+             static_cast<const __half*>(x2), C2, HW, table, silu, total, static_cast<__half*>(y));
+  return check_launch(c, "gn_apply_table");
+}
+
 size_t gn_nhwc_ws_bytes(int N, int HW, int G) {
   int chunks, cl;
   gn_geometry(HW, &chunks, &cl);
@@ -389,6 +561,13 @@ int di_group_norm_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void
   Ctx* c = ctx_of(h);
   if (!c) return DI_EINVAL;
   return group_norm_nhwc(c, dtype, dtype, x1, C1, x2, x2 ? C2 : 0, N, HW, G, eps, gamma, beta, fuse_silu, y, nullptr);
+}
+
+int di_gn_table_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                     float eps, const float* gamma, const float* beta, float* table) {
+  Ctx* c = ctx_of(h);
+  if (!c || !table || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
+  return gn_table_nhwc(c, dtype, x1, C1, x2, x2 ? C2 : 0, N, HW, G, eps, gamma, beta, reinterpret_cast<float2*>(table));
 }
 
 int di_group_norm(di_ctx_t h, const float* X, const float* gamma, const float* beta, float* Y, const void* cfg32,

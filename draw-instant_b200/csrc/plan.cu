@@ -33,14 +33,18 @@ namespace di {
 
 int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
                 const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
-                int rowvec_div, void* splitk_ws = nullptr);
+                int rowvec_div, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr, int gnf_hw = 0);
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
-                 void* y, int out_f32, int temb_ld, void* splitk_ws = nullptr);
+                 void* y, int out_f32, int temb_ld, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr);
 int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1, const void* x2, int C2, int N,
                     int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
                     void* partial_ws);
 size_t gn_nhwc_ws_bytes(int N, int HW, int G);
+int gn_table_nhwc(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G, float eps,
+                  const float* gamma, const float* beta, float2* table);
+int gn_nhwc_via_table(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                      float eps, const float* gamma, const float* beta, int silu, void* y, float2* table);
 int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu);
 int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* g, const float* b, void* y, int rows,
                int D, float eps);
@@ -513,6 +517,55 @@ struct Plan {
     return y;
   }
 
+  // GroupNorm statistics of concat(x1, x2) as a per-(image, channel) affine table for a consumer GEMM
+  // that normalises its operand as it loads it (GnFuse): no normalised tensor is written.
+  const float2* gn_tab(const std::string& pre, const Act& x1, const Act* x2, float eps) {
+    const int C = x1.C + (x2 ? x2->C : 0), HW = x1.H * x1.W;
+    const float* g = vec(pre + ".weight", C, 1, 1);
+    const float* b = vec(pre + ".bias", C, 2, 1);
+    float2* tab = static_cast<float2*>(tmp(sizeof(float2) * (size_t)x1.N * C));
+    Ctx* cc = c;
+    const Act a = x1;
+    const void* p2 = x2 ? x2->p : nullptr;
+    const int C2 = x2 ? x2->C : 0;
+    record([=] { return gn_table_nhwc(cc, DI_F16, a.p, a.C, p2, C2, a.N, HW, 32, eps, g, b, tab); }, 2, 0,
+           (double)x1.N * HW * C * 2, 1);
+    return tab;
+  }
+
+  // A consumer GEMM's view of GroupNorm(+SiLU)(concat(x1, x2)).  gn_mode 0: two-pass GroupNorm into a
+  // temporary (per-chunk partials); 1: cluster statistics table + elementwise normalise into a
+  // temporary; 2: statistics table only, the consumer normalises its operand as it loads it (GnFuse).
+  struct GnOp {
+    const void* x1;
+    int C1;
+    const void* x2;
+    int C2;
+    const float2* tab;  // non-null: fused (raw inputs above)
+    int silu;
+  };
+  int gn_mode = [] {  // diagnostics: DI_GN_MODE selects the GroupNorm strategy
+    const char* e = getenv("DI_GN_MODE");
+    return (e && e[0] >= '0' && e[0] <= '2') ? e[0] - '0' : 1;
+  }();
+  GnOp gn_op(const std::string& pre, const Act& x1, const Act* x2, float eps, int silu) {
+    const int C = x1.C + (x2 ? x2->C : 0);
+    if (gn_mode == 2) return GnOp{x1.p, x1.C, x2 ? x2->p : nullptr, x2 ? x2->C : 0, gn_tab(pre, x1, x2, eps), silu};
+    if (gn_mode == 0) return GnOp{gn(pre, x1, x2, eps, silu), C, nullptr, 0, nullptr, 0};
+    const int HW = x1.H * x1.W;
+    const float* g = vec(pre + ".weight", C, 1, 1);
+    const float* b = vec(pre + ".bias", C, 2, 1);
+    void* y = tmp((size_t)x1.N * HW * C * 2);
+    float2* tab = static_cast<float2*>(tmp(sizeof(float2) * (size_t)x1.N * C));
+    Ctx* cc = c;
+    const Act a = x1;
+    const void* p2 = x2 ? x2->p : nullptr;
+    const int C2 = x2 ? x2->C : 0;
+    record([=] { return gn_nhwc_via_table(cc, DI_F16, a.p, a.C, p2, C2, a.N, HW, 32, eps, g, b, silu, y, tab); }, 2, 0,
+           3.0 * x1.N * HW * C * 2, 2);
+    return GnOp{y, C, nullptr, 0, nullptr, 0};
+  }
+
   // GroupNorm(+SiLU) of concat(x1, x2) into a temporary.
   void* gn(const std::string& pre, const Act& x1, const Act* x2, float eps, int silu) {
     const int C = x1.C + (x2 ? x2->C : 0), HW = x1.H * x1.W;
@@ -535,9 +588,13 @@ struct Plan {
     return upload_f16(host_param(name, (size_t)N * K, 0, K, N));
   }
   void linear(const void* X, int M, int K, const void* W, int N, const float* b, const void* R, void* Y,
-              const void* X2 = nullptr, int K1 = 0) {
+              const void* X2 = nullptr, int K1 = 0, const float2* gtab = nullptr, int gsilu = 0, int ghw = 0) {
     Ctx* cc = c;
-    record([=] { return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1, splitk); },
+    record([=] {
+      const GnFuse f{gtab, gsilu};
+      return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1, splitk,
+                         gtab ? &f : nullptr, ghw);
+    },
            0, 2.0 * M * N * K, 2.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1)), gemm_kernel_count(c, M, N, K, 0));
   }
 
@@ -551,7 +608,7 @@ struct Plan {
   Act resnet(const std::string& pre, const Act& x1, const Act* x2, int Co) {
     tmp_reset();
     const int Ci = x1.C + (x2 ? x2->C : 0);
-    void* a = gn(pre + ".norm1", x1, x2, 1e-5f, 1);
+    const GnOp g1 = gn_op(pre + ".norm1", x1, x2, 1e-5f, 1);
     // time projection rows appended to the shared GEMV
     {
       auto w = host_param(pre + ".time_emb_proj.weight", (size_t)Co * 1280, 0, 1280, Co);
@@ -571,10 +628,13 @@ struct Plan {
     Ctx* cc = c;
     const int N = x1.N, H = x1.H, W = x1.W;
     Plan* self = this;
-    record([=] { return gemm_conv3x3(cc, DI_F16, a, Ci, nullptr, 0, N, H, W, 1, w1, Co, b1,
-                                     self->temb_all + toff, nullptr, 0, h.p, 0, self->tproj_ld, splitk); },
+    record([=] {
+      const GnFuse f{g1.tab, g1.silu};
+      return gemm_conv3x3(cc, DI_F16, g1.x1, g1.C1, g1.x2, g1.C2, N, H, W, 1, w1, Co, b1, self->temb_all + toff, nullptr,
+                          0, h.p, 0, self->tproj_ld, splitk, g1.tab ? &f : nullptr);
+    },
            0, 2.0 * N * H * W * Co * 9 * Ci, 2.0 * ((double)N * H * W * (Ci + Co) + 9.0 * Co * Ci), gemm_kernel_count(c, N * H * W, Co, 9 * Ci, 0));
-    void* a2 = gn(pre + ".norm2", h, nullptr, 1e-5f, 1);
+    const GnOp g2 = gn_op(pre + ".norm2", h, nullptr, 1e-5f, 1);
     const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
     const float* b2 = bias_padded(pre + ".conv2.bias", Co, Co, Co * 9);
     const void* res = x1.p;
@@ -586,8 +646,11 @@ struct Plan {
       res = s;
     }
     Act y = new_act(N, H, W, Co);
-    record([=] { return gemm_conv3x3(cc, DI_F16, a2, Co, nullptr, 0, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0,
-                                     Co, splitk); },
+    record([=] {
+      const GnFuse f{g2.tab, g2.silu};
+      return gemm_conv3x3(cc, DI_F16, g2.x1, g2.C1, g2.x2, g2.C2, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0, Co,
+                          splitk, g2.tab ? &f : nullptr);
+    },
            0, 2.0 * N * H * W * Co * 9 * Co, 2.0 * ((double)N * H * W * 3 * Co + 9.0 * Co * Co), gemm_kernel_count(c, N * H * W, Co, 9 * Co, 0));
     return y;
   }
@@ -597,11 +660,11 @@ struct Plan {
     tmp_reset();
     const int N = x.N, HW = x.H * x.W, C = x.C, M = N * HW, heads = C / 64;
     const std::string tb = pre + ".transformer_blocks.0";
-    void* a = gn(pre + ".norm", x, nullptr, 1e-6f, 0);
+    const GnOp gx = gn_op(pre + ".norm", x, nullptr, 1e-6f, 0);
     const void* wpi = lin_weight(pre + ".proj_in.weight", C, C);
     const float* bpi = vec(pre + ".proj_in.bias", C, 0, C);
     void* h0 = tmp((size_t)M * C * 2);
-    linear(a, M, C, wpi, C, bpi, nullptr, h0);
+    linear(gx.x1, M, C, wpi, C, bpi, nullptr, h0, nullptr, 0, gx.tab, 0, HW);
     Ctx* cc = c;
     // --- self attention ---
     const float* g1 = vec(tb + ".norm1.weight", C, 1, 1);
@@ -834,13 +897,16 @@ static int build_unet(UNetPlan* u) {
   }
   // conv_norm_out + SiLU, conv_out 320 -> 4 (padded to 16)
   P.tmp_reset();
-  void* a = P.gn("conv_norm_out", h, nullptr, 1e-5f, 1);
+  const Plan::GnOp go = P.gn_op("conv_norm_out", h, nullptr, 1e-5f, 1);
   {
     const void* w = P.conv_weight("conv_out.weight", 4, 320, 320, 16);
     const float* b = P.bias_padded("conv_out.bias", 4, 16, 320 * 9);
     void* y16 = P.act_alloc((size_t)B * H * W * 16 * 2);
-    P.record([=] { return gemm_conv3x3(cc, DI_F16, a, 320, nullptr, 0, B, H, W, 1, w, 16, b, nullptr, nullptr, 0, y16,
-                                       0, 16, sk); },
+    P.record([=] {
+      const GnFuse f{go.tab, go.silu};
+      return gemm_conv3x3(cc, DI_F16, go.x1, 320, nullptr, 0, B, H, W, 1, w, 16, b, nullptr, nullptr, 0, y16, 0, 16, sk,
+                          go.tab ? &f : nullptr);
+    },
              0, 2.0 * B * H * W * 4 * 9 * 320, (double)B * H * W * (640 + 32), gemm_kernel_count(cc, B * H * W, 16, 9 * 320, 0));
     float* out = u->out;
     P.record([=] {

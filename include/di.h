@@ -162,6 +162,17 @@ DI_API int di_conv3x3_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, cons
                     int stride, const void* Wt, int Co, const float* bias, const float* temb, const void* residual,
                     void* y);
 /* Packs a reference-layout fp32 conv weight [Co][Ci][3][3] into the [Co][3][3][Ci] dtype layout used above. */
+/* GroupNorm fused into the conv's operand load (no normalised tensor in memory).  di_gn_table_nhwc
+ * reduces concat(x1, x2) [N, HW, C1 + C2] to table[N][C] = (scale, shift) float pairs (8 bytes per
+ * channel) with scale = gamma * rstd, shift = beta - mean * scale (fused-groupnorm.js:145-227
+ * statistics).  di_conv3x3_nhwc_gn is di_conv3x3_nhwc (stride 1) applied to silu?(x * scale + shift)
+ * of the raw x1/x2, the normalisation done in shared memory between the TMA load and the tensor core
+ * (fused-resnet.js:121-208 chain: GN -> SiLU -> conv3x3 -> +temb / +residual). */
+DI_API int di_gn_table_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW,
+                            int G, float eps, const float* gamma, const float* beta, float* table);
+DI_API int di_conv3x3_nhwc_gn(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H,
+                              int W, const void* Wt, int Co, const float* bias, const float* temb,
+                              const void* residual, const float* gn_table, int silu, void* y);
 DI_API int di_pack_conv3x3(di_ctx_t ctx, int dtype, const float* w_oihw, int Co, int Ci, void* w_packed);
 
 /* Attention, head dim 64: O = softmax(Q K^T / 8) V per (b, h).  layout 0 = token-major [B,S,H,64]

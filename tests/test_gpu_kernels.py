@@ -193,3 +193,53 @@ def test_tembed(ctx, dib, oracle):
     torch.cuda.synchronize()
     ref = oracle.tembed(t, W1, b1, W2, b2, 320, 1280)
     assert rel_err(_np(Y), ref) < 1e-4
+
+
+@pytest.mark.parametrize("N,H,W,C1,C2,Co,silu", [
+    (1, 64, 64, 320, 0, 320, 1), (1, 16, 16, 256, 128, 128, 1), (2, 8, 8, 640, 320, 320, 1),
+    (1, 32, 32, 640, 0, 640, 0), (2, 4, 4, 128, 0, 64, 1)])
+def test_conv3x3_fused_group_norm(ctx, dib, oracle, N, H, W, C1, C2, Co, silu):
+    """GroupNorm(+SiLU) applied in the conv's operand load (di_gn_table_nhwc + di_conv3x3_nhwc_gn) against
+    the oracle's GN -> SiLU -> conv3x3 (+temb +residual) on the same inputs (fused-resnet.js:121-208)."""
+    import torch
+    rng = np.random.default_rng(7 * N + H + C1 + C2 + Co + silu)
+    Ci = C1 + C2
+    HW = H * W
+    x = _round(rng.standard_normal((N, HW, Ci)) * 1.5 + 0.3)
+    g = (1 + 0.1 * rng.standard_normal(Ci)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(Ci)).astype(np.float32)
+    w = _round(rng.standard_normal((Co, Ci, 3, 3)) / np.sqrt(9 * Ci))
+    bias = rng.standard_normal(Co).astype(np.float32)
+    temb = rng.standard_normal((N, Co)).astype(np.float32)
+    res = _round(rng.standard_normal((N, H, W, Co)))
+    X1 = _t(x[..., :C1])
+    X2 = _t(x[..., C1:]) if C2 else None
+    Gt, Bt = _t(g, "f32"), _t(b, "f32")
+    L = dib.lib()
+    tab = torch.empty((N, Ci, 2), dtype=torch.float32, device="cuda")
+    ctx.check(L.di_gn_table_nhwc(ctx.h, 1, X1.data_ptr(), C1, X2.data_ptr() if C2 else None, C2, N, HW, 32, 1e-5,
+                                 Gt.data_ptr(), Bt.data_ptr(), tab.data_ptr()), "gn_table")
+    Wp = torch.empty((Co, 9 * Ci), dtype=torch.float16, device="cuda")
+    ctx.check(L.di_pack_conv3x3(ctx.h, 1, _t(w, "f32").data_ptr(), Co, Ci, Wp.data_ptr()), "pack")
+    Y = torch.empty((N, H, W, Co), dtype=torch.float16, device="cuda")
+    Bi, Tb, R = _t(bias, "f32"), _t(temb, "f32"), _t(res)
+    ctx.check(L.di_conv3x3_nhwc_gn(ctx.h, 1, X1.data_ptr(), C1, X2.data_ptr() if C2 else None, C2, N, H, W,
+                                   Wp.data_ptr(), Co, Bi.data_ptr(), Tb.data_ptr(), R.data_ptr(), tab.data_ptr(), silu,
+                                   Y.data_ptr()), "conv_gn")
+    torch.cuda.synchronize()
+    xn = np.ascontiguousarray(np.transpose(x, (0, 2, 1)))
+    a = oracle.group_norm(xn, g, b, N, Ci, HW, 32, 1e-5, silu=bool(silu)).reshape(N, Ci, H, W)
+    # statistics: the table against the oracle's mean / rstd composition
+    xg = x.reshape(N, HW, 32, Ci // 32).astype(np.float64)
+    mean = xg.mean(axis=(1, 3))
+    rstd = 1 / np.sqrt(np.maximum((xg * xg).mean(axis=(1, 3)) - mean ** 2, 0) + 1e-5)
+    sc = np.repeat(rstd, Ci // 32, axis=1) * g
+    sh = b - np.repeat(mean, Ci // 32, axis=1) * sc
+    tb = tab.cpu().numpy()
+    assert rel_err(tb[..., 0], sc) < 1e-4 and rel_err(tb[..., 1], sh) < 1e-3
+    ref = oracle.conv(a, w, bias, N, Ci, H, W, Co, 3, 1, 1)
+    ref = np.transpose(ref, (0, 2, 3, 1)) + temb[:, None, None, :] + res
+    got = _np(Y)
+    assert rel_err(got, ref) < TOL
+    assert cosine(got, ref) > 0.9999
+    assert ctx.fault() == 0
