@@ -324,11 +324,48 @@ int cast_rows_f16(Ctx* c, const float* x, int rows, int cols, int ld_in, void* y
   return check_launch(c, "cast_rows");
 }
 
+// fp16 bit patterns -> fp32 bit patterns with integer operations only, so every input maps exactly as
+// the reference's host conversion does (wgsl-unet.js:23-47): subnormals renormalised, Inf kept, NaN
+// payloads shifted into the fp32 mantissa unchanged.  Two halves per thread (one 32-bit load).
+__global__ void f16_bits_to_f32_kernel(const uint16_t* __restrict__ h, uint32_t* __restrict__ f, size_t n) {
+  pdl_begin();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t x = h[i];
+    const uint32_t sign = (x & 0x8000u) << 16;
+    int e = (x >> 10) & 0x1f;
+    uint32_t m = x & 0x3ffu, bits;
+    if (e == 0) {
+      if (m == 0) {
+        bits = sign;
+      } else {
+        const int lz = __clz(m) - 21;  // shifts that bring the leading one to bit 10
+        m = (m << lz) & 0x3ffu;
+        e = 1 - lz;
+        bits = sign | ((uint32_t)(e + 112) << 23) | (m << 13);
+      }
+    } else if (e == 31) {
+      bits = sign | 0x7f800000u | (m << 13);
+    } else {
+      bits = sign | ((uint32_t)(e + 112) << 23) | (m << 13);
+    }
+    f[i] = bits;
+  }
+}
+
 }  // namespace di
 
 using namespace di;
 
 extern "C" {
+
+int di_f16_bytes_to_f32(di_ctx_t h, const void* src, float* dst, size_t n) {
+  Ctx* c = ctx_of(h);
+  if (!c || (n && (!src || !dst))) return DI_EINVAL;
+  if (!n) return DI_OK;
+  launch_k(f16_bits_to_f32_kernel, grid_for(c, n), 256, 0, c->stream, static_cast<const uint16_t*>(src),
+           reinterpret_cast<uint32_t*>(dst), n);
+  return check_launch(c, "f16_bytes_to_f32");
+}
 
 int di_unary(di_ctx_t h, int op, const float* X, float* Y, uint32_t n) {
   Ctx* c = ctx_of(h);

@@ -89,6 +89,9 @@ DI_API int di_debug_gemm_trace(unsigned long long* buf, int ctas);
 #define DI_MAX 5
 #define DI_MIN 6
 
+/* WeightCache's fp16 -> fp32 conversion of raw little-endian fp16 bytes (wgsl-unet.js:23-47), bit-exact
+ * for every input including subnormals, Inf and NaN payloads; n halves. */
+DI_API int di_f16_bytes_to_f32(di_ctx_t ctx, const void* src, float* dst, size_t n);
 DI_API int di_unary(di_ctx_t ctx, int op, const float* X, float* Y, uint32_t n);                 /* wgsl-ops.js:110 */
 /* operands wrap at their own length (i % nA, i % nB), wgsl-ops.js:147-151 */
 DI_API int di_binary(di_ctx_t ctx, int op, const float* A, uint32_t nA, const float* B, uint32_t nB, float* Y,

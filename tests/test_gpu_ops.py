@@ -236,3 +236,18 @@ def test_zero_length_and_bad_ops(ctx, ops, dib):
     with pytest.raises(dib.DIError):  # rank 5 broadcast
         ops.binaryBcast(ctx, "Add")(enc, X, X, Y, ops.createUniform(ctx, np.array([5] + [0] * 19, np.uint32)), 4)
     ctx.clear_fault()
+
+
+def test_f16_bytes_to_f32_all_patterns(ctx, dib, oracle):
+    """WeightCache conversion (wgsl-unet.js:23-47) on the device: all 65536 fp16 bit patterns, bit-exact."""
+    import torch
+    h = np.arange(65536, dtype=np.uint16)
+    src = torch.from_numpy(h.view(np.int16).copy()).cuda()
+    dst = torch.empty(65536, dtype=torch.float32, device="cuda")
+    ctx.check(dib.lib().di_f16_bytes_to_f32(ctx.h, src.data_ptr(), dst.data_ptr(), 65536), "f16_bytes_to_f32")
+    got = dst.cpu().numpy().view(np.uint32)
+    ref = oracle.f16_to_f32(h).view(np.uint32)
+    np.testing.assert_array_equal(got, ref)
+    # Inf / NaN patterns keep their payload in the fp32 mantissa: sign | 0x7f800000 | mant << 13
+    sp = h[(h >> 10 & 0x1F) == 31].astype(np.uint32)
+    np.testing.assert_array_equal(got[sp], ((sp & 0x8000) << 16) | 0x7F800000 | ((sp & 0x3FF) << 13))
