@@ -77,6 +77,7 @@ SIGNATURES = {
     "di_linear_geglu": (_I, [_P, _I, _P, _I, _I, _P, _I, _P, _P]),
     "di_conv3x3_nhwc": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P]),
     "di_pack_conv3x3": (_I, [_P, _I, _P, _I, _I, _P]),
+    "di_conv3x3_nhwc_act": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _I, _P]),
     "di_gn_table_nhwc": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _F, _P, _P, _P]),
     "di_conv3x3_nhwc_gn": (_I, [_P, _I, _P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _I, _P]),
     "di_attention": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I]),

@@ -49,6 +49,7 @@ struct GemmParams {
   void* out;
   int ldo, out_f32;
   int geglu;
+  int act_silu;  // SiLU after bias / row vector, before the residual (y = silu(acc + b) + r)
   int vec_ok;  // 16-byte aligned rows for out / residual: vectorised epilogue
   int b_early;     // weights are constant data: fetch the first B stages before the dependency wait
   int splits;      // K splits; > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
@@ -548,6 +549,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                     if (nb + j < n_out) v[j] += rv[j];
                 }
               }
+              if (p.act_silu) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+              }
               if (p.residual) {
                 if (full && p.vec_ok) {
                   float rr[32];
@@ -723,7 +728,7 @@ static int max_pairs(Ctx* c) {
 // Sums the split-K partials and applies the epilogue (bias, per-image row vector, residual or GEGLU).
 __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
                               const float* __restrict__ rowvec, int rowvec_div, int rowvec_ld, const void* residual,
-                              int ldr, int res_f32, void* out, int ldo, int out_f32, int geglu, int bf16) {
+                              int ldr, int res_f32, void* out, int ldo, int out_f32, int geglu, int bf16, int act) {
   pdl_begin();
   const size_t slice = (size_t)M * N;
   const int NO = geglu ? N / 2 : N;
@@ -742,6 +747,7 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
       for (int j = 0; j < 4; ++j) {
         if (bias) f[j] += bias[o + j];
         if (rowvec) f[j] += rowvec[(size_t)(m / rowvec_div) * rowvec_ld + o + j];
+        if (act) f[j] = silu_f(f[j]);
         if (residual) f[j] += load_one(residual, (size_t)m * ldr + o + j, res_f32, bf16);
         store_one(out, (size_t)m * ldo + o + j, f[j], out_f32, bf16);
       }
@@ -756,6 +762,7 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
       for (int z = 0; z < splits; ++z) v += part[z * slice + (size_t)m * N + o];
       if (bias) v += bias[o];
       if (rowvec) v += rowvec[(size_t)(m / rowvec_div) * rowvec_ld + o];
+      if (act) v = silu_f(v);
       if (residual) v += load_one(residual, (size_t)m * ldr + o, res_f32, bf16);
       store_one(out, (size_t)m * ldo + o, v, out_f32, bf16);
     } else {
@@ -888,7 +895,7 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
     launch_k(splitk_reduce, blocks, 256, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,
-             p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32, p.geglu, bf16);
+             p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32, p.geglu, bf16, p.act_silu);
     return check_launch(c, "splitk_reduce");
   }
   return dispatch_variant(c, p, bn, bf16, pair);
@@ -1000,7 +1007,7 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
 
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
-                 void* y, int out_f32, int temb_ld, void* splitk_ws, const GnFuse* gnf) {
+                 void* y, int out_f32, int temb_ld, void* splitk_ws, const GnFuse* gnf, int act) {
   if (C1 <= 0 || C1 % 64 || (x2 && (C2 <= 0 || C2 % 64)) || Co % 16 || (stride != 1 && stride != 2))
     return set_error(c, DI_EINVAL, "conv3x3: channels must be multiples of 64 (Co of 16), stride 1 or 2");
   if (stride == 2 && (x2 || (H % 2) || (W % 2)))
@@ -1044,6 +1051,7 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
   p.ldo = Co;
   p.out_f32 = out_f32;
   p.vec_ok = vec_rows_ok(y, Co, out_f32 ? 4 : 2) && (!residual || vec_rows_ok(residual, Co, res_f32 ? 4 : 2));
+  p.act_silu = act;
   if (gnf && gnf->tab) {
     if (stride != 1) return set_error(c, DI_EUNSUPPORTED, "conv3x3: fused GroupNorm needs stride 1");
     p.gn_tab = gnf->tab;
@@ -1114,7 +1122,16 @@ int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
   return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr,
-                      nullptr);
+                      nullptr, 0);
+}
+
+int di_conv3x3_nhwc_act(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,
+                        int stride, const void* Wt, int Co, const float* bias, const float* temb,
+                        const void* residual, int act, void* y) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16) || act < 0 || act > 1) return DI_EINVAL;
+  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, stride, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr,
+                      nullptr, act);
 }
 
 int di_conv3x3_nhwc_gn(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,
@@ -1123,7 +1140,7 @@ int di_conv3x3_nhwc_gn(di_ctx_t h, int dtype, const void* x1, int C1, const void
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16) || !gn_table) return DI_EINVAL;
   const GnFuse f{reinterpret_cast<const float2*>(gn_table), silu ? 1 : 0};
-  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, 1, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr, &f);
+  return gemm_conv3x3(c, dtype, x1, C1, x2, C2, N, H, W, 1, Wt, Co, bias, temb, residual, 0, y, 0, Co, nullptr, &f, 0);
 }
 
 int di_pack_conv3x3(di_ctx_t h, int dtype, const float* w, int Co, int Ci, void* out) {

@@ -36,7 +36,8 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
                 int rowvec_div, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr, int gnf_hw = 0);
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
-                 void* y, int out_f32, int temb_ld, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr);
+                 void* y, int out_f32, int temb_ld, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr,
+                 int act = 0);
 int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1, const void* x2, int C2, int N,
                     int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
                     void* partial_ws);

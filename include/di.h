@@ -165,6 +165,11 @@ DI_API int di_conv3x3_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, cons
                     int stride, const void* Wt, int Co, const float* bias, const float* temb, const void* residual,
                     void* y);
 /* Packs a reference-layout fp32 conv weight [Co][Ci][3][3] into the [Co][3][3][Ci] dtype layout used above. */
+/* di_conv3x3_nhwc with an activation in the epilogue: act 1 = y = silu(conv + bias + temb) + residual
+ * (fused-conv.js:50-100 epilogue 'silu_fn(sum) + residual'); act 0 = di_conv3x3_nhwc. */
+DI_API int di_conv3x3_nhwc_act(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H,
+                               int W, int stride, const void* Wt, int Co, const float* bias, const float* temb,
+                               const void* residual, int act, void* y);
 /* GroupNorm fused into the conv's operand load (no normalised tensor in memory).  di_gn_table_nhwc
  * reduces concat(x1, x2) [N, HW, C1 + C2] to table[N][C] = (scale, shift) float pairs (8 bytes per
  * channel) with scale = gamma * rstd, shift = beta - mean * scale (fused-groupnorm.js:145-227
