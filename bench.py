@@ -160,6 +160,7 @@ def run_reference(args, rank, world):
         return
     import oracle
     oracle.build()
+    oracle.set_threads(len(os.sched_getaffinity(0)))  # all host threads (torchrun defaults OpenMP to one)
     load_package()
     unet_mod = importlib.import_module("draw_instant_b200.unet")
     seed = 3
@@ -285,11 +286,10 @@ def main():
         return
 
     import torch
-    import torch.distributed as dist
     torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     dib = load_package()
+    R = importlib.import_module("draw_instant_b200.replicas")
+    R.init("nccl", torch.device("cuda", local))
     unet_mod = importlib.import_module("draw_instant_b200.unet")
     ctx = dib.Context(local)
     B = args.batch
@@ -304,9 +304,7 @@ def main():
         u.forward()
     torch.cuda.synchronize()
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    barrier = R.barrier
 
     sampler = ClockSampler(local)
     barrier()
@@ -317,15 +315,11 @@ def main():
         for _ in range(args.steps):
             u.forward()
         if world > 1:  # the job's one collective: gather every replica's predicted latents (NCCL / NVLink)
-            gathered = [torch.empty_like(u.out) for _ in range(world)]
-            dist.all_gather(gathered, u.out)
+            R.gather(u.out)
         ev1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    t = torch.tensor([ev0.elapsed_time(ev1)], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total = float(t.item())
+    ms_total = R.max_over_ranks(ev0.elapsed_time(ev1), "cuda")
     value = world * args.steps / (ms_total / 1e3)
     ms_step = ms_total / args.steps
     step_flops = unet_mod.unet_flops(B, 64, 64)
@@ -358,10 +352,8 @@ def main():
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
             host_step()
-        te = torch.tensor([time.perf_counter() - t0], device="cuda")
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        line["e2e"] = {"value": world * e2e_steps / float(te.item()), "unit": "steps/s",
+        te = R.max_over_ranks(time.perf_counter() - t0, "cuda")
+        line["e2e"] = {"value": world * e2e_steps / te, "unit": "steps/s",
                        "h2d_bytes_per_step": int(h_lat.numel() * 4 + B * 4 + h_ctx.numel() * 4),
                        "d2h_bytes_per_step": int(h_out.numel() * 4)}
 
@@ -397,8 +389,7 @@ def main():
                                         "sample": f"failed: {e}"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    R.finish()
 
 
 if __name__ == "__main__":

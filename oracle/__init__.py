@@ -55,6 +55,7 @@ _SIGS = {
     "o_transformer_block": [_f, _f, _I, _I, _I, _I, _I, _U64, _I, _f],
     "o_unet_forward": [_f, _f, _f, _I, _I, _I, _I, _U64, _f],
     "o_num_threads": [],
+    "o_set_threads": [_I],
     "o_param_seconds": [],
     "o_clear_cache": [],
 }
@@ -300,6 +301,10 @@ def unet_forward(latent, t, ctx, seed):
 
 def num_threads() -> int:
     return lib().o_num_threads()
+
+
+def set_threads(n: int) -> None:
+    lib().o_set_threads(int(n))
 
 
 def param_seconds() -> float:

@@ -820,6 +820,13 @@ void o_unet_forward(const float* latent, const float* tvals, const float* ctx, i
 double o_param_seconds() { return g_param_seconds; }
 void o_clear_cache() { g_unet_cache.clear(); }
 
+void o_set_threads(int n) {  // torchrun sets OMP_NUM_THREADS=1 for multi-process jobs; the baseline uses all cores
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
 int o_num_threads() {
 #ifdef _OPENMP
   return omp_get_max_threads();
