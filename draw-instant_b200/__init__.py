@@ -93,6 +93,15 @@ SIGNATURES = {
     "di_unet_forward": (_I, [_P]),
     "di_unet_forward_host": (_I, [_P, _P, _P, _P, _P]),
     "di_unet_destroy": (None, [_P]),
+    "di_vae_create": (_I, [_P, _I, _I, _I, ctypes.c_uint64, _P, _P, ctypes.POINTER(_P)]),
+    "di_vae_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "di_vae_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "di_vae_ops": (_I, [_P, ctypes.POINTER(_I), _P, _P, _P, _P]),
+    "di_vae_profile_kind": (_I, [_P, _I, _I, ctypes.POINTER(_F)]),
+    "di_vae_forward": (_I, [_P]),
+    "di_vae_forward_host": (_I, [_P, _P, _P]),
+    "di_vae_destroy": (None, [_P]),
+    "di_vae_debug_copy": (_I, [_P, _I, _SZ, _P, _SZ]),
     "di_resnet_block_create": (_I, [_P, _I, _I, _I, _I, _I, ctypes.c_uint64, _F, _I, _P, _P, ctypes.POINTER(_P)]),
     "di_resnet_block_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)]),
     "di_resnet_block_run": (_I, [_P]),

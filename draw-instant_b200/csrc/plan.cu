@@ -132,6 +132,59 @@ __global__ void latent_out_kernel(const __half* __restrict__ x, int Cp, float* _
     y[i] = __half2float(x[(n * HW + p) * Cp + c]);
   }
 }
+// Row softmax in place on fp16 scores (the scale is folded into the query projection): one 256-thread
+// block per row, eight columns per thread per step, fp32 max / sum (block reductions in a fixed order).
+__global__ void softmax_rows_f16(__half* __restrict__ s, int cols) {
+  pdl_begin();
+  __shared__ float red[8];
+  __half* row = s + (size_t)blockIdx.x * cols;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  float mx = -INFINITY;
+  for (int c = t * 8; c < cols; c += 256 * 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      mx = fmaxf(mx, fmaxf(f.x, f.y));
+    }
+  }
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[wid] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  __syncthreads();
+  const float ml = mx * 1.4426950408889634f;
+  float sum = 0.f;
+  for (int c = t * 8; c < cols; c += 256 * 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      sum += exp2f(fmaf(f.x, 1.4426950408889634f, -ml)) + exp2f(fmaf(f.y, 1.4426950408889634f, -ml));
+    }
+  }
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) red[wid] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int w = 0; w < 8; ++w) sum += red[w];
+  const float inv = 1.0f / sum;
+  for (int c = t * 8; c < cols; c += 256 * 8) {
+    uint4 u = *reinterpret_cast<const uint4*>(row + c);
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      h[j] = __floats2half2_rn(exp2f(fmaf(f.x, 1.4426950408889634f, -ml)) * inv,
+                               exp2f(fmaf(f.y, 1.4426950408889634f, -ml)) * inv);
+    }
+    *reinterpret_cast<uint4*>(row + c) = u;
+  }
+}
+
 // Nearest 2x upsample, NHWC, 16-byte vectors (index math of wgsl-ops.js:921-943 with W_out = 2 W_in).
 __global__ void upsample2_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, int N, int H, int W, int Cv) {
   pdl_begin();
@@ -412,6 +465,14 @@ struct Plan {
   // Enqueue one forward on the plan's stream, ordered after / before the context stream.
   int forward() {
     if (err) return err;
+    if (const char* e = getenv("DI_PLAN_LIMIT")) {  // diagnostics: run only the first k ops, eagerly
+      const size_t k = std::min<size_t>(ops.size(), (size_t)std::max(0, atoi(e)));
+      for (size_t i = 0; i < k; ++i) {
+        const int r = ops[i]();
+        if (r) return r;
+      }
+      return cudaStreamSynchronize(c->stream) == cudaSuccess ? DI_OK : DI_ECUDA;
+    }
     cudaEventRecord(ev_in, c->stream);
     cudaStreamWaitEvent(stream, ev_in, 0);
     cudaStream_t saved = c->stream;
@@ -483,9 +544,22 @@ struct Plan {
     return upload_f32(b);
   }
 
+  // Chain plans (the VAE decoder: every op reads only its immediate input) take activations from a ring
+  // of `act_ring` buffers instead of one allocation each.
+  std::vector<void*> act_ring;
+  size_t act_ring_bytes = 0, act_ring_next = 0;
   Act new_act(int N, int H, int W, int C) {
     Act a;
     a.N = N; a.H = H; a.W = W; a.C = C;
+    if (!act_ring.empty()) {
+      if (a.bytes() > act_ring_bytes) {
+        fail(DI_ENOMEM, "plan: activation ring too small");
+        a.p = nullptr;
+        return a;
+      }
+      a.p = act_ring[act_ring_next++ % act_ring.size()];
+      return a;
+    }
     a.p = act_alloc(a.bytes());
     return a;
   }
@@ -606,12 +680,12 @@ struct Plan {
   float* temb_all = nullptr;            // [B, tproj_rows] fp32, computed once per forward
   int tproj_ld = 0;
 
-  Act resnet(const std::string& pre, const Act& x1, const Act* x2, int Co) {
+  Act resnet(const std::string& pre, const Act& x1, const Act* x2, int Co, float eps = 1e-5f, bool temb = true) {
     tmp_reset();
     const int Ci = x1.C + (x2 ? x2->C : 0);
-    const GnOp g1 = gn_op(pre + ".norm1", x1, x2, 1e-5f, 1);
+    const GnOp g1 = gn_op(pre + ".norm1", x1, x2, eps, 1);
     // time projection rows appended to the shared GEMV
-    {
+    if (temb) {
       auto w = host_param(pre + ".time_emb_proj.weight", (size_t)Co * 1280, 0, 1280, Co);
       auto b = host_param(pre + ".time_emb_proj.bias", Co, 0, 1280);
       round_f16(w);
@@ -620,7 +694,7 @@ struct Plan {
       tproj_b.insert(tproj_b.end(), b.begin(), b.end());
     }
     const int toff = tproj_rows;
-    tproj_rows += Co;
+    if (temb) tproj_rows += Co;
     const void* w1 = conv_weight(pre + ".conv1.weight", Co, Ci, Ci, Co);
     const float* b1 = bias_padded(pre + ".conv1.bias", Co, Co, Ci * 9);
     Act h;
@@ -631,11 +705,12 @@ struct Plan {
     Plan* self = this;
     record([=] {
       const GnFuse f{g1.tab, g1.silu};
-      return gemm_conv3x3(cc, DI_F16, g1.x1, g1.C1, g1.x2, g1.C2, N, H, W, 1, w1, Co, b1, self->temb_all + toff, nullptr,
-                          0, h.p, 0, self->tproj_ld, splitk, g1.tab ? &f : nullptr);
+      return gemm_conv3x3(cc, DI_F16, g1.x1, g1.C1, g1.x2, g1.C2, N, H, W, 1, w1, Co, b1,
+                          temb ? self->temb_all + toff : nullptr, nullptr, 0, h.p, 0, self->tproj_ld, splitk,
+                          g1.tab ? &f : nullptr);
     },
            0, 2.0 * N * H * W * Co * 9 * Ci, 2.0 * ((double)N * H * W * (Ci + Co) + 9.0 * Co * Ci), gemm_kernel_count(c, N * H * W, Co, 9 * Ci, 0));
-    const GnOp g2 = gn_op(pre + ".norm2", h, nullptr, 1e-5f, 1);
+    const GnOp g2 = gn_op(pre + ".norm2", h, nullptr, eps, 1);
     const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
     const float* b2 = bias_padded(pre + ".conv2.bias", Co, Co, Co * 9);
     const void* res = x1.p;
@@ -753,6 +828,92 @@ struct Plan {
 
   // Builds the time-projection GEMV once every ResNet block has appended its rows; `at` is the op
   // index it must run at (right after the timestep embedding).
+  // The VAE's mid-block attention (diffusers Attention: GroupNorm(32, 1e-6), one head of C channels,
+  // biased q / k / v / out projections, residual).  Per image: S = q k^T (the 1/sqrt(C) scale folded into
+  // the query projection), an fp16 row softmax, O = P V with V^T = Wv a^T from one GEMM (the v bias is
+  // folded into the out-projection bias: softmax rows sum to one), then out-projection + residual.
+  Act vae_attention(const std::string& pre, const Act& x) {
+    tmp_reset();
+    const int N = x.N, HW = x.H * x.W, C = x.C, M = N * HW;
+    if (HW % 64 || C % 64) {
+      fail(DI_EUNSUPPORTED, "vae attention: H*W and C must be multiples of 64");
+      return x;
+    }
+    const int saved_mode = gn_mode;
+    gn_mode = 1;  // V^T = Wv a^T takes the normalised activations as its B operand: materialise them
+    const GnOp g = gn_op(pre + ".group_norm", x, nullptr, 1e-6f, 0);
+    gn_mode = saved_mode;
+    const float scale = 1.0f / std::sqrt((float)C);
+    auto wq = host_param(pre + ".to_q.weight", (size_t)C * C, 0, C, C);
+    auto bq = host_param(pre + ".to_q.bias", C, 0, C);
+    round_f16(wq);
+    round_f16(bq);
+    for (auto& v : wq) v *= scale;
+    for (auto& v : bq) v *= scale;
+    const void* Wq = upload_f16(wq);
+    const float* Bq = upload_f32(bq);
+    const void* Wk = lin_weight(pre + ".to_k.weight", C, C);
+    const float* Bk = vec(pre + ".to_k.bias", C, 0, C);
+    auto wv = host_param(pre + ".to_v.weight", (size_t)C * C, 0, C, C);
+    auto bv = host_param(pre + ".to_v.bias", C, 0, C);
+    auto wo = host_param(pre + ".to_out.0.weight", (size_t)C * C, 0, C, C);
+    auto bo = host_param(pre + ".to_out.0.bias", C, 0, C);
+    round_f16(wv);
+    round_f16(bv);
+    round_f16(wo);
+    round_f16(bo);
+    for (int o = 0; o < C; ++o) {  // bo' = bo + Wo bv
+      double acc = bo[o];
+      for (int k = 0; k < C; ++k) acc += (double)wo[(size_t)o * C + k] * bv[k];
+      bo[o] = (float)acc;
+    }
+    const void* Wv = upload_f16(wv);
+    const void* Wo = upload_f16(wo);
+    const float* Bo = upload_f32(bo);
+    void* q = tmp((size_t)M * C * 2);
+    void* k = tmp((size_t)M * C * 2);
+    void* vt = tmp((size_t)C * HW * 2);
+    void* sc = tmp((size_t)HW * HW * 2);
+    void* o = tmp((size_t)M * C * 2);
+    if (err) return x;
+    linear(g.x1, M, C, Wq, C, Bq, nullptr, q, nullptr, 0, g.tab, 0, HW);
+    linear(g.x1, M, C, Wk, C, Bk, nullptr, k, nullptr, 0, g.tab, 0, HW);
+    Ctx* cc = c;
+    void* sk = splitk;
+    for (int n = 0; n < N; ++n) {
+      const size_t off = (size_t)n * HW * C * 2;
+      const char* qn = static_cast<const char*>(q) + off;
+      const char* kn = static_cast<const char*>(k) + off;
+      const char* an = static_cast<const char*>(g.x1) + off;
+      char* on = static_cast<char*>(o) + off;
+      const float2* tab = g.tab ? g.tab + (size_t)n * C : nullptr;
+      // these three GEMMs take activations as their B operand: no weight-tile fetch before the dependency wait
+      record([=] {
+        cc->weights_const = false;
+        return gemm_linear(cc, DI_F16, qn, C, nullptr, HW, C, kn, HW, nullptr, nullptr, 0, sc, 0, 0, nullptr, 1, sk);
+      },
+             1, 2.0 * HW * HW * C, 2.0 * (2.0 * HW * C + (double)HW * HW), gemm_kernel_count(cc, HW, HW, C, 0));
+      record([=] {
+        launch_k(softmax_rows_f16, HW, 256, 0, cc->stream, static_cast<__half*>(sc), HW);
+        return check_launch(cc, "softmax_rows_f16");
+      }, 1, 0, 4.0 * HW * HW);
+      record([=] {
+        cc->weights_const = false;
+        const GnFuse f{tab, 0};
+        return gemm_linear(cc, DI_F16, Wv, C, nullptr, C, C, an, HW, nullptr, nullptr, 0, vt, 0, 0, nullptr, 1, sk,
+                           tab ? &f : nullptr, HW);
+      }, 0, 2.0 * C * HW * C, 2.0 * (2.0 * C * C + (double)HW * C), gemm_kernel_count(cc, C, HW, C, 0));
+      record([=] {
+        cc->weights_const = false;
+        return gemm_linear(cc, DI_F16, sc, HW, nullptr, HW, HW, vt, C, nullptr, nullptr, 0, on, 0, 0, nullptr, 1, sk);
+      },
+             1, 2.0 * HW * HW * C, 2.0 * ((double)HW * HW + 2.0 * C * HW), gemm_kernel_count(cc, HW, C, HW, 0));
+    }
+    Act y = new_act(N, x.H, x.W, C);
+    linear(o, M, C, Wo, C, Bo, x.p, y.p);
+    return y;
+  }
+
   void finish_time_proj(size_t at, const float* temb, int B) {
     const void* W = upload_f16(tproj_w);
     const float* b = upload_f32(tproj_b);
@@ -1009,7 +1170,119 @@ static int build_tblock(TBPlan* t) {
 // ---------------------------------------------------------------------------------------------
 using namespace di;
 
+// SD VAE decoder (diffusers AutoencoderKL.decode: post_quant_conv + Decoder, block_out_channels
+// 128/256/512/512, 3 ResNets per up block, GroupNorm 32 eps 1e-6, one mid-block attention), the graph
+// vae-wgsl.js:99-118 runs (latent / 0.18215 first).  Latent [B,4,h,w] fp32 NCHW -> image [B,3,8h,8w].
+struct VaePlan {
+  Plan P;
+  int B = 1, h = 64, w = 64;
+  float* latent = nullptr;  // [B,4,h,w] fp32 NCHW (input)
+  float* image = nullptr;   // [B,3,8h,8w] fp32 NCHW (output)
+};
+
+static size_t vae_ring_bytes(int B, int h, int w) {  // largest activation: 256 channels at 8h x 8w
+  return (size_t)B * 64 * h * w * 256 * 2;
+}
+static size_t vae_tmp_bytes(int B, int h, int w) {
+  // largest ResNet working set: GroupNorm output (256 ch) + conv1 output, GroupNorm output and shortcut
+  // (128 ch each) at 8h x 8w; attention at h x w (q, k, o, V^T, scores) is smaller for the U-Net's sizes
+  const size_t px = (size_t)B * 64 * h * w;
+  const size_t resnet = px * (256 + 3 * 128) * 2 + (size_t)B * 256 * 16;
+  const size_t hw = (size_t)h * w;
+  const size_t attn = (size_t)B * hw * 512 * 2 * 4 + hw * 512 * 2 + hw * hw * 2 + (size_t)B * 512 * 16;
+  return std::max(resnet, attn) + (64 << 20);
+}
+
+static int build_vae(VaePlan* v) {
+  Plan& P = v->P;
+  const int B = v->B, h = v->h, w = v->w;
+  Ctx* cc = P.c;
+  void* sk = P.splitk;
+  v->latent = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 4 * h * w));
+  v->image = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 3 * 64 * h * w));
+  for (int i = 0; i < 3; ++i) P.act_ring.push_back(P.act_alloc(vae_ring_bytes(B, h, w)));
+  P.act_ring_bytes = vae_ring_bytes(B, h, w);
+  if (P.err) return P.err;
+  // latent NCHW fp32 -> NHWC fp16 padded to 64 channels
+  Act lat = P.new_act(B, h, w, 64);
+  {
+    const float* src = v->latent;
+    void* dst = lat.p;
+    P.record([=] {
+      const size_t n = (size_t)B * h * w * 64;
+      launch_k(latent_in_kernel, (int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, cc->stream, src,
+               static_cast<__half*>(dst), B, 4, h * w, 64);
+      return check_launch(cc, "vae latent_in");
+    }, 3, 0, (double)B * h * w * (16 + 128));
+  }
+  // post_quant_conv (1x1, 4 -> 4) with the 1/0.18215 latent scaling folded into its weight; channels
+  // padded to 64 (zero rows / columns) so conv_in reads a 64-channel input
+  Act z = P.new_act(B, h, w, 64);
+  {
+    auto wq = P.host_param("post_quant_conv.weight", 16, 0, 4, 4);
+    auto bq = P.host_param("post_quant_conv.bias", 4, 0, 4);
+    Plan::round_f16(wq);
+    Plan::round_f16(bq);
+    std::vector<float> wp(64 * 64, 0.0f), bp(64, 0.0f);
+    for (int o = 0; o < 4; ++o) {
+      for (int i = 0; i < 4; ++i) wp[o * 64 + i] = wq[o * 4 + i] / 0.18215f;
+      bp[o] = bq[o];
+    }
+    P.linear(lat.p, B * h * w, 64, P.upload_f16(wp), 64, P.upload_f32(bp), nullptr, z.p);
+  }
+  // conv_in 4 (padded 64) -> 512
+  Act x;
+  {
+    const void* wt = P.conv_weight("decoder.conv_in.weight", 512, 4, 64, 512);
+    const float* bt = P.bias_padded("decoder.conv_in.bias", 512, 512, 4 * 9);
+    x = P.new_act(B, h, w, 512);
+    const Act zz = z, xx = x;
+    P.record([=] { return gemm_conv3x3(cc, DI_F16, zz.p, 64, nullptr, 0, B, h, w, 1, wt, 512, bt, nullptr, nullptr, 0,
+                                       xx.p, 0, 512, sk); },
+             0, 2.0 * B * h * w * 512 * 9 * 4, (double)B * h * w * (128 + 1024), gemm_kernel_count(cc, B * h * w, 512, 9 * 64, 0));
+  }
+  // mid block
+  x = P.resnet("decoder.mid_block.resnets.0", x, nullptr, 512, 1e-6f, false);
+  x = P.vae_attention("decoder.mid_block.attentions.0", x);
+  x = P.resnet("decoder.mid_block.resnets.1", x, nullptr, 512, 1e-6f, false);
+  // up blocks
+  const int chans[4] = {512, 512, 256, 128};
+  for (int i = 0; i < 4; ++i) {
+    for (int j = 0; j < 3; ++j)
+      x = P.resnet("decoder.up_blocks." + std::to_string(i) + ".resnets." + std::to_string(j), x, nullptr, chans[i],
+                   1e-6f, false);
+    if (i < 3) {
+      P.tmp_reset();
+      x = P.conv3x3("decoder.up_blocks." + std::to_string(i) + ".upsamplers.0.conv", P.upsample(x), chans[i], 1);
+    }
+  }
+  // conv_norm_out + SiLU, conv_out 128 -> 3 (padded to 16), NHWC fp16 -> NCHW fp32
+  P.tmp_reset();
+  const Plan::GnOp go = P.gn_op("decoder.conv_norm_out", x, nullptr, 1e-6f, 1);
+  const int H = x.H, W = x.W;
+  {
+    const void* wt = P.conv_weight("decoder.conv_out.weight", 3, 128, 128, 16);
+    const float* bt = P.bias_padded("decoder.conv_out.bias", 3, 16, 128 * 9);
+    void* y16 = P.tmp((size_t)B * H * W * 16 * 2);
+    P.record([=] {
+      const GnFuse f{go.tab, go.silu};
+      return gemm_conv3x3(cc, DI_F16, go.x1, 128, nullptr, 0, B, H, W, 1, wt, 16, bt, nullptr, nullptr, 0, y16, 0, 16, sk,
+                          go.tab ? &f : nullptr);
+    }, 0, 2.0 * B * H * W * 3 * 9 * 128, (double)B * H * W * (256 + 32), gemm_kernel_count(cc, B * H * W, 16, 9 * 128, 0));
+    float* out = v->image;
+    P.record([=] {
+      const size_t n = (size_t)B * 3 * H * W;
+      launch_k(latent_out_kernel, (int)std::min<size_t>((n + 255) / 256, 8192), 256, 0, cc->stream,
+               static_cast<const __half*>(y16), 16, out, B, 3, H * W);
+      return check_launch(cc, "vae image_out");
+    }, 3, 0, (double)B * H * W * (32 + 12));
+  }
+  cudaDeviceSynchronize();
+  return P.err;
+}
+
 struct di_unet_s { UNetPlan u; };
+struct di_vae_s { VaePlan v; };
 struct di_resnet_s { ResPlan r; };
 struct di_tblock_s { TBPlan t; };
 
@@ -1106,6 +1379,78 @@ DI_API int di_unet_forward_host(di_unet_t u, const float* latent, const float* t
 }
 
 DI_API void di_unet_destroy(di_unet_t u) { delete u; }
+
+DI_API int di_vae_create(di_ctx_t h, int B, int lh, int lw, uint64_t seed, di_weight_fn fn, void* user, di_vae_t* out) {
+  Ctx* c = ctx_of(h);
+  if (!c || !out || B <= 0 || lh <= 0 || lw <= 0 || (lh * lw) % 64) return DI_EINVAL;
+  *out = nullptr;
+  auto* s = new di_vae_s();
+  s->v.B = B; s->v.h = lh; s->v.w = lw;
+  if (!s->v.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, vae_tmp_bytes(B, lh, lw))) {
+    delete s;
+    return set_error(c, DI_ENOMEM, "vae: allocation");
+  }
+  int r = build_vae(&s->v);
+  if (r) {
+    std::string m = s->v.P.errmsg;
+    delete s;
+    return set_error(c, r, "vae build: " + m);
+  }
+  *out = s;
+  return DI_OK;
+}
+DI_API int di_vae_io(di_vae_t v, float** latent, float** image) {
+  if (!v) return DI_EINVAL;
+  if (latent) *latent = v->v.latent;
+  if (image) *image = v->v.image;
+  return DI_OK;
+}
+DI_API int di_vae_info(di_vae_t v, int* launches, size_t* weight_bytes, size_t* act_bytes) {
+  if (!v) return DI_EINVAL;
+  if (launches) *launches = v->v.P.launches;
+  if (weight_bytes) *weight_bytes = v->v.P.weight_bytes;
+  if (act_bytes) *act_bytes = v->v.P.act_bytes;
+  return DI_OK;
+}
+DI_API int di_vae_ops(di_vae_t v, int* n_ops, int* kinds, double* flops, double* bytes, int* kernels) {
+  if (!v || !n_ops) return DI_EINVAL;
+  const auto& I = v->v.P.info;
+  *n_ops = (int)I.size();
+  for (size_t i = 0; i < I.size(); ++i) {
+    if (kinds) kinds[i] = I[i].kind;
+    if (flops) flops[i] = I[i].flops;
+    if (bytes) bytes[i] = I[i].bytes;
+    if (kernels) kernels[i] = I[i].kernels;
+  }
+  return DI_OK;
+}
+DI_API int di_vae_profile_kind(di_vae_t v, int kind, int reps, float* ms) {
+  if (!v || !ms || reps <= 0) return DI_EINVAL;
+  return v->v.P.profile_kind(kind, reps, ms);
+}
+DI_API int di_vae_forward(di_vae_t v) { return v ? v->v.P.forward() : DI_EINVAL; }
+DI_API int di_vae_forward_host(di_vae_t v, const float* latent, float* image) {
+  if (!v || !latent || !image) return DI_EINVAL;
+  VaePlan& p = v->v;
+  Ctx* c = p.P.c;
+  const size_t nl = (size_t)p.B * 4 * p.h * p.w, ni = (size_t)p.B * 3 * 64 * p.h * p.w;
+  cudaMemcpyAsync(p.latent, latent, nl * 4, cudaMemcpyHostToDevice, c->stream);
+  int r = p.P.forward();
+  if (r) return r;
+  cudaMemcpyAsync(image, p.image, ni * 4, cudaMemcpyDeviceToHost, c->stream);
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return set_error(c, DI_ECUDA, "vae forward_host sync");
+  return DI_OK;
+}
+DI_API void di_vae_destroy(di_vae_t v) { delete v; }
+// Diagnostics: copy bytes of activation-ring buffer `idx` (idx < 0: the temporary arena) to the host.
+DI_API int di_vae_debug_copy(di_vae_t v, int idx, size_t off, void* dst, size_t bytes) {
+  if (!v || !dst) return DI_EINVAL;
+  Plan& P = v->v.P;
+  const char* src = idx < 0 ? P.tmp_base : (idx < (int)P.act_ring.size() ? static_cast<const char*>(P.act_ring[idx]) : nullptr);
+  if (!src) return DI_EINVAL;
+  cudaStreamSynchronize(P.c->stream);
+  return cudaMemcpy(dst, src + off, bytes, cudaMemcpyDeviceToHost) == cudaSuccess ? DI_OK : DI_ECUDA;
+}
 
 DI_API int di_resnet_block_create(di_ctx_t h, int N, int C, int H, int W, int Tdim, uint64_t seed, float eps,
                                   int temb_silu, di_weight_fn fn, void* user, di_resnet_t* out) {

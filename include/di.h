@@ -204,6 +204,7 @@ DI_API int di_tembed(di_ctx_t ctx, const float* t, int B, const float* W1, const
 typedef struct di_unet_s* di_unet_t;
 typedef struct di_resnet_s* di_resnet_t;
 typedef struct di_tblock_s* di_tblock_t;
+typedef struct di_vae_s* di_vae_t;
 typedef int (*di_weight_fn)(const char* name, size_t n, float* dst, void* user);
 
 /* The seeded parameter generator: key = mix64(seed*0x9E3779B97F4A7C15 + fnv1a64(name)),
@@ -235,6 +236,23 @@ DI_API void di_unet_destroy(di_unet_t u);
 /* Config-1 ResNet block, fp32 NCHW in and out (fused-resnet.js:121-208 + the timestep add it omits,
  * fused-resnet.js:9-12): y = conv2(silu(gn2(conv1(silu(gn1(x))) + Wt.act(temb) + bt))) + x;
  * act = SiLU when temb_silu (diffusers), identity otherwise.  Names: norm1/conv1/time_emb_proj/norm2/conv2. */
+/* SD VAE decoder (config 5's image decode; vae-wgsl.js:99-118 runs it through the same executor):
+ * diffusers AutoencoderKL decode = latent / 0.18215 -> post_quant_conv -> Decoder (conv_in 4->512, mid
+ * ResNet / single-head attention / ResNet, up blocks 512, 512, 256, 128 with 3 ResNets each and 2x
+ * nearest upsample + conv, GroupNorm(32, 1e-6) + SiLU, conv_out 128->3).  Latent [B,4,h,w] fp32 NCHW
+ * (h*w a multiple of 64), image [B,3,8h,8w] fp32 NCHW; parameter names are diffusers' (post_quant_conv.*,
+ * decoder.*).  Activations reuse a ring of buffers (the decoder is a chain). */
+DI_API int di_vae_create(di_ctx_t ctx, int B, int h, int w, uint64_t seed, di_weight_fn fn, void* user, di_vae_t* out);
+DI_API int di_vae_io(di_vae_t v, float** latent, float** image);
+DI_API int di_vae_info(di_vae_t v, int* launches, size_t* weight_bytes, size_t* act_bytes);
+DI_API int di_vae_ops(di_vae_t v, int* n_ops, int* kinds, double* flops, double* bytes, int* kernels);
+DI_API int di_vae_profile_kind(di_vae_t v, int kind, int reps, float* ms);
+DI_API int di_vae_forward(di_vae_t v);
+DI_API int di_vae_forward_host(di_vae_t v, const float* latent, float* image);
+DI_API void di_vae_destroy(di_vae_t v);
+/* Diagnostics: copy `bytes` at `off` of activation-ring buffer idx (idx < 0: temporary arena) to host. */
+DI_API int di_vae_debug_copy(di_vae_t v, int idx, size_t off, void* dst, size_t bytes);
+
 DI_API int di_resnet_block_create(di_ctx_t ctx, int N, int C, int H, int W, int Tdim, uint64_t seed, float eps,
                                   int temb_silu, di_weight_fn fn, void* user, di_resnet_t* out);
 DI_API int di_resnet_block_io(di_resnet_t r, float** x, float** temb, float** y);

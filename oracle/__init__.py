@@ -54,6 +54,7 @@ _SIGS = {
     "o_resnet_block": [_f, _f, _I, _I, _I, _I, _I, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _F, _I, _f],
     "o_transformer_block": [_f, _f, _I, _I, _I, _I, _I, _U64, _I, _f],
     "o_unet_forward": [_f, _f, _f, _I, _I, _I, _I, _U64, _f],
+    "o_vae_decode": [_f, _I, _I, _I, _U64, _f],
     "o_num_threads": [],
     "o_set_threads": [_I],
     "o_param_seconds": [],
@@ -296,6 +297,14 @@ def unet_forward(latent, t, ctx, seed):
     out = np.empty_like(_c(latent))
     tv = _c(np.broadcast_to(np.asarray(t, np.float32), (B,)))
     lib().o_unet_forward(_c(latent).ravel(), tv, _c(ctx).ravel(), B, H, W, Sk, seed, out.ravel())
+    return out
+
+
+def vae_decode(latent, seed):
+    """SD VAE decoder on [B, 4, h, w] latents -> [B, 3, 8h, 8w] (latent / 0.18215 applied first)."""
+    B, _, h, w = latent.shape
+    out = np.empty((B, 3, 8 * h, 8 * w), np.float32)
+    lib().o_vae_decode(_c(latent).ravel(), B, h, w, seed, out.ravel())
     return out
 
 

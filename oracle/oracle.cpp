@@ -817,8 +817,71 @@ void o_unet_forward(const float* latent, const float* tvals, const float* ctx, i
   std::memcpy(out, h.d.data(), sizeof(float) * h.size());
 }
 
+// ---- SD VAE decoder (diffusers AutoencoderKL.decode; vae-wgsl.js:99-118 applies latent / 0.18215) ------
+Tensor4 resnet_nt(Params& P, const std::string& pre, const Tensor4& x, int Co, float eps) {
+  Tensor4 h = gn_p(P, pre + ".norm1", x, eps, true);
+  h = conv_p(P, pre + ".conv1", h, Co, 3, 1);
+  h = gn_p(P, pre + ".norm2", h, eps, true);
+  h = conv_p(P, pre + ".conv2", h, Co, 3, 1);
+  if (x.C != Co) {
+    Tensor4 s = conv_p(P, pre + ".conv_shortcut", x, Co, 1, 1);
+    for (size_t i = 0; i < h.size(); ++i) h.d[i] += s.d[i];
+  } else {
+    for (size_t i = 0; i < h.size(); ++i) h.d[i] += x.d[i];
+  }
+  return h;
+}
+
+// diffusers Attention in the VAE mid block: GroupNorm(32, 1e-6), one head of C channels (scale 1/sqrt(C)),
+// biased q / k / v / out projections, residual.
+Tensor4 vae_attn(Params& P, const std::string& pre, const Tensor4& x) {
+  Tensor4 nx = gn_p(P, pre + ".group_norm", x, 1e-6f, false);
+  const int N = x.N, C = x.C, HW = x.H * x.W;
+  std::vector<float> tok((size_t)N * HW * C);
+  for (int n = 0; n < N; ++n)
+    for (int c = 0; c < C; ++c)
+      for (int p = 0; p < HW; ++p) tok[((size_t)n * HW + p) * C + c] = nx.d[((size_t)n * C + c) * HW + p];
+  auto q = linear_p(P, pre + ".to_q", tok, N * HW, C, C, true);
+  auto k = linear_p(P, pre + ".to_k", tok, N * HW, C, C, true);
+  auto v = linear_p(P, pre + ".to_v", tok, N * HW, C, C, true);
+  std::vector<float> o((size_t)N * HW * C);
+  const AttnStrides st{(long long)HW * C, C, 0};
+  attention_rows(q.data(), k.data(), v.data(), o.data(), N, 1, HW, HW, C, st, st, st, nullptr, 0);
+  auto y = linear_p(P, pre + ".to_out.0", o, N * HW, C, C, true);
+  Tensor4 out = x;
+  for (int n = 0; n < N; ++n)
+    for (int c = 0; c < C; ++c)
+      for (int p = 0; p < HW; ++p) out.d[((size_t)n * C + c) * HW + p] += y[((size_t)n * HW + p) * C + c];
+  return out;
+}
+
+std::unordered_map<uint64_t, std::unordered_map<std::string, std::vector<float>>> g_vae_cache;
+
+void o_vae_decode(const float* latent, int B, int h, int w, uint64_t seed, float* image) {
+  Params P{seed, true, 0, {}, 0, &g_vae_cache[seed]};
+  Tensor4 z = t4(B, 4, h, w);
+  for (size_t i = 0; i < z.size(); ++i) z.d[i] = (float)((double)latent[i] / 0.18215);
+  z = conv_p(P, "post_quant_conv", z, 4, 1, 1);
+  Tensor4 x = conv_p(P, "decoder.conv_in", z, 512, 3, 1);
+  x = resnet_nt(P, "decoder.mid_block.resnets.0", x, 512, 1e-6f);
+  x = vae_attn(P, "decoder.mid_block.attentions.0", x);
+  x = resnet_nt(P, "decoder.mid_block.resnets.1", x, 512, 1e-6f);
+  const int ch[4] = {512, 512, 256, 128};
+  for (int i = 0; i < 4; ++i) {
+    const std::string pre = "decoder.up_blocks." + std::to_string(i);
+    for (int j = 0; j < 3; ++j) x = resnet_nt(P, pre + ".resnets." + std::to_string(j), x, ch[i], 1e-6f);
+    if (i < 3) x = conv_p(P, pre + ".upsamplers.0.conv", upsample2(x), ch[i], 3, 1);
+  }
+  x = gn_p(P, "decoder.conv_norm_out", x, 1e-6f, true);
+  x = conv_p(P, "decoder.conv_out", x, 3, 3, 1);
+  std::memcpy(image, x.d.data(), sizeof(float) * x.size());
+}
+
 double o_param_seconds() { return g_param_seconds; }
-void o_clear_cache() { g_unet_cache.clear(); }
+void o_clear_cache() {
+  g_unet_cache.clear();
+  g_vae_cache.clear();
+}
 
 void o_set_threads(int n) {  // torchrun sets OMP_NUM_THREADS=1 for multi-process jobs; the baseline uses all cores
 #ifdef _OPENMP

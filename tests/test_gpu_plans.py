@@ -93,3 +93,21 @@ def test_unet_full_size_properties(ctx, dib, oracle):
     b = u.forward_host(lat, 999.0, cx)
     assert np.all(np.isfinite(a)) and np.array_equal(a, b)
     assert u.launches > 100
+
+
+@pytest.mark.parametrize("B,h,w", [(1, 8, 8), (2, 8, 16)])
+def test_vae_decoder_vs_oracle(ctx, dib, oracle, B, h, w):
+    """SD VAE decoder (config 5's decode) at small latents: cosine >= 0.999 and max-rel <= 1e-2 against the
+    oracle's diffusers-Decoder restatement on the same seeded weights."""
+    import importlib
+    vae = importlib.import_module("draw_instant_b200.vae")
+    seed = 4
+    v = vae.VAEDecoder(ctx, B=B, h=h, w=w, seed=seed)
+    lat = oracle.gen_normal(seed, "latent", B * 4 * h * w).reshape(B, 4, h, w) * 0.18215
+    got = v.forward_host(lat)
+    ref = oracle.vae_decode(lat, seed)
+    assert got.shape == (B, 3, 8 * h, 8 * w)
+    assert np.all(np.isfinite(got))
+    assert cosine(got, ref) >= 0.999
+    assert rel_err(got, ref) <= 1e-2
+    assert ctx.fault() == 0
