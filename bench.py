@@ -197,6 +197,34 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def vae_result(ctx, pk, src):
+    """Config 5's image decode: SD VAE decoder, latent [B, 4, 64, 64] -> image [B, 3, 512, 512], fp16."""
+    import torch
+    vae = importlib.import_module("draw_instant_b200.vae")
+    out = {}
+    for B in (1, 8):
+        v = vae.VAEDecoder(ctx, B=B, h=64, w=64, seed=4)
+        v.latent.normal_(0, 0.18215)
+        for _ in range(3):
+            v.forward()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            v.forward()
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / 5
+        fl = vae.vae_flops(B, 64, 64)
+        out[f"B{B}"] = {"ms": ms, "images_per_s": B / (ms / 1e3), "tflops": fl / (ms / 1e3) / 1e12,
+                        "frac": fl / (ms / 1e3) / 1e12 / pk["bf16_tflops"], "gflop": fl / 1e9,
+                        "launches": v.launches}
+        del v
+    out["bound"] = "tensor"
+    out["peak_source"] = f"{src} bf16_tflops (burst)"
+    return out
+
+
 def time_events(fn, iters, stream):
     import torch
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -380,6 +408,10 @@ def main():
             "time_by_kind_ms": {names[k]: v for k, v in kind_ms.items()}}
         if rank == 0 and world == 1:
             line["blocks"] = block_results(dib, ctx, pk, src)
+            try:
+                line["blocks"]["vae_decode_512"] = vae_result(ctx, pk, src)
+            except Exception as e:  # a reported extra; never fail the bench line on it
+                line["blocks"]["vae_decode_512"] = {"error": str(e)}
             try:
                 v, sample, cores = cpu_baseline(unet_mod)
                 line["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": cores, "kind": "port",

@@ -272,8 +272,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       for (int u = cta0; u < units && !*abort_flag; u += cstride) {
         int m0, n0, sp, kb0, kb1;
         decode(u, m0, n0, sp, kb0, kb1);
-        int img = 0, y0 = 0;
-        if (p.mode != 0) { img = m0 / p.HWo; y0 = (m0 % p.HWo) / p.Wo; }
+        int img = 0, y0 = 0, x0 = 0;  // tile origin; x0 > 0 only for rows wider than a tile
+        if (p.mode != 0) {
+          img = m0 / p.HWo;
+          y0 = (m0 % p.HWo) / p.Wo;
+          x0 = (m0 % p.HWo) % p.Wo;
+        }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -292,10 +296,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             const int ky = tap / 3, kx = tap % 3;
             if (p.mode == 1) {
               const bool first = cb < p.k_split;
-              loadA4(dA, &p.tmA[first ? 0 : 1], s, (first ? cb : cb - p.k_split) * BK, kx - 1, y0 + ky - 1, img);
+              loadA4(dA, &p.tmA[first ? 0 : 1], s, (first ? cb : cb - p.k_split) * BK, x0 + kx - 1, y0 + ky - 1,
+                     img);
             } else {
               const int py = ky == 1 ? 0 : 1, px = kx == 1 ? 0 : 1;
-              loadA4(dA, &p.tmA[py * 2 + px], s, cb * BK, kx == 0 ? -1 : 0, y0 + (ky == 0 ? -1 : 0), img);
+              loadA4(dA, &p.tmA[py * 2 + px], s, cb * BK, x0 + (kx == 0 ? -1 : 0), y0 + (ky == 0 ? -1 : 0), img);
             }
           }
           if (!pre) load2(sB + s * S::B_BYTES, &p.tmB, s, kb * BK, n0 + brow);
@@ -379,11 +384,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           r_x[i] = 0;
           if (p.mode == 0) {
             r_img[i] = mr < p.M ? mr / p.gn_HW : -1;
-          } else {
-            const int rr = rw / p.Wo;
-            r_x[i] = rw % p.Wo;
-            r_img[i] = mr < p.M ? m0 / p.HWo + rr / p.conv_bh : -1;
-            r_y[i] = (m0 % p.HWo) / p.Wo + rr % p.conv_bh;
+          } else {  // output pixel of tile row rw (any tile geometry)
+            const int pix = mr % p.HWo;
+            r_img[i] = mr < p.M ? mr / p.HWo : -1;
+            r_y[i] = pix / p.Wo;
+            r_x[i] = pix % p.Wo;
           }
         }
         const int Ho = p.mode == 0 ? 0 : p.HWo / p.Wo;
@@ -915,7 +920,14 @@ bool tmap_kmajor(CUtensorMap* m, int dtype, const void* base, uint64_t rows, uin
 }
 
 // Conv tile geometry: 128 output pixels = bn images x bh rows x Wo columns.
+// Rows wider than 128 pixels (multiples of 128) are cut into 128-pixel tiles: box {64, 128, 1, 1}.
+static uint32_t conv_box_w(int Wo) { return (uint32_t)std::min(Wo, 128); }
 static bool conv_box(int Ho, int Wo, uint32_t* bh, uint32_t* bn) {
+  if (Wo > 128 && Wo % 128 == 0) {
+    *bh = 1;
+    *bn = 1;
+    return true;
+  }
   if (Wo <= 0 || Wo > 128 || (128 % Wo) != 0) return false;
   const int rows = std::min(Ho, 128 / Wo);
   if ((128 / Wo) % rows != 0) return false;
@@ -929,7 +941,7 @@ static bool tmap_conv_s1(CUtensorMap* m, int dtype, const void* base, int N, int
                          uint32_t bn, std::string* err) {
   uint64_t dims[4] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)N};
   uint64_t strides[3] = {(uint64_t)C * 2, (uint64_t)W * C * 2, (uint64_t)H * W * C * 2};
-  uint32_t box[4] = {64, (uint32_t)W, bh, bn};
+  uint32_t box[4] = {64, conv_box_w(W), bh, bn};
   return make_tmap(m, tdt(dtype), 4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, err);
 }
 
@@ -938,7 +950,7 @@ static bool tmap_conv_s2(CUtensorMap* m, int dtype, const void* base, int N, int
   const uint16_t* b = static_cast<const uint16_t*>(base) + ((size_t)py * W + px) * C;
   uint64_t dims[4] = {(uint64_t)C, (uint64_t)(W / 2), (uint64_t)(H / 2), (uint64_t)N};
   uint64_t strides[3] = {(uint64_t)C * 4, (uint64_t)W * C * 4, (uint64_t)H * W * C * 2};
-  uint32_t box[4] = {64, (uint32_t)(W / 2), bh, bn};
+  uint32_t box[4] = {64, conv_box_w(W / 2), bh, bn};
   return make_tmap(m, tdt(dtype), 4, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, err);
 }
 

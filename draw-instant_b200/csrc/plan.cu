@@ -626,7 +626,10 @@ struct Plan {
   GnOp gn_op(const std::string& pre, const Act& x1, const Act* x2, float eps, int silu) {
     const int C = x1.C + (x2 ? x2->C : 0);
     if (gn_mode == 2) return GnOp{x1.p, x1.C, x2 ? x2->p : nullptr, x2 ? x2->C : 0, gn_tab(pre, x1, x2, eps), silu};
-    if (gn_mode == 0) return GnOp{gn(pre, x1, x2, eps, silu), C, nullptr, 0, nullptr, 0};
+    // mode 0 also for large tensors: its statistics pass spreads each image over up to 128 CTAs, the
+    // table path over one 16-CTA cluster (latency-optimal for the U-Net's small maps only)
+    const size_t tensor_bytes = (size_t)x1.N * x1.H * x1.W * C * 2;
+    if (gn_mode == 0 || tensor_bytes > (16u << 20)) return GnOp{gn(pre, x1, x2, eps, silu), C, nullptr, 0, nullptr, 0};
     const int HW = x1.H * x1.W;
     const float* g = vec(pre + ".weight", C, 1, 1);
     const float* b = vec(pre + ".bias", C, 2, 1);

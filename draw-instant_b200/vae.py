@@ -85,6 +85,9 @@ class VAEDecoder:
         return ms.value
 
     def __del__(self):
-        if getattr(self, "h", None):
-            lib().di_vae_destroy(self.h)
-            self.h = None
+        try:
+            if getattr(self, "h", None):
+                lib().di_vae_destroy(self.h)
+                self.h = None
+        except Exception:  # interpreter shutdown
+            pass

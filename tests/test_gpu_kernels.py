@@ -100,7 +100,8 @@ def test_linear_geglu(ctx, dib, oracle, M, K, F):
 @pytest.mark.parametrize("N,H,W,C1,C2,Co,stride", [
     (1, 64, 64, 320, 0, 320, 1), (1, 32, 32, 640, 0, 640, 1), (2, 8, 8, 128, 0, 192, 1),
     (1, 16, 16, 256, 128, 128, 1), (1, 8, 8, 128, 64, 64, 1), (1, 64, 64, 128, 0, 128, 2),
-    (2, 16, 16, 64, 0, 128, 2), (1, 4, 4, 64, 0, 64, 1), (1, 2, 2, 64, 0, 64, 2)])
+    (2, 16, 16, 64, 0, 128, 2), (1, 4, 4, 64, 0, 64, 1), (1, 2, 2, 64, 0, 64, 2),
+    (1, 4, 256, 64, 0, 64, 1), (2, 4, 512, 64, 0, 128, 2), (1, 3, 384, 128, 64, 64, 1)])
 def test_conv3x3_nhwc(ctx, dib, oracle, N, H, W, C1, C2, Co, stride):
     import torch
     rng = np.random.default_rng(N + H + C1 + C2 + Co + stride)
@@ -156,7 +157,8 @@ def test_attention(ctx, dib, oracle, B, H, Sq, Skv, layout, dtype):
 
 
 @pytest.mark.parametrize("N,HW,C1,C2,G,silu", [(1, 4096, 320, 0, 32, 1), (2, 256, 1280, 1280, 32, 1),
-                                               (1, 64, 640, 320, 32, 0), (1, 1024, 1920, 0, 32, 1)])
+                                               (1, 64, 640, 320, 32, 0), (1, 1024, 1920, 0, 32, 1),
+                                               (1, 262144, 128, 0, 32, 1), (2, 65536, 256, 256, 32, 1)])
 def test_group_norm_nhwc(ctx, dib, oracle, N, HW, C1, C2, G, silu):
     import torch
     rng = np.random.default_rng(HW + C1)
@@ -197,7 +199,7 @@ def test_tembed(ctx, dib, oracle):
 
 @pytest.mark.parametrize("N,H,W,C1,C2,Co,silu", [
     (1, 64, 64, 320, 0, 320, 1), (1, 16, 16, 256, 128, 128, 1), (2, 8, 8, 640, 320, 320, 1),
-    (1, 32, 32, 640, 0, 640, 0), (2, 4, 4, 128, 0, 64, 1)])
+    (1, 32, 32, 640, 0, 640, 0), (2, 4, 4, 128, 0, 64, 1), (1, 4, 256, 128, 0, 64, 1)])
 def test_conv3x3_fused_group_norm(ctx, dib, oracle, N, H, W, C1, C2, Co, silu):
     """GroupNorm(+SiLU) applied in the conv's operand load (di_gn_table_nhwc + di_conv3x3_nhwc_gn) against
     the oracle's GN -> SiLU -> conv3x3 (+temb +residual) on the same inputs (fused-resnet.js:121-208)."""

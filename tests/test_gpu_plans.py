@@ -95,7 +95,7 @@ def test_unet_full_size_properties(ctx, dib, oracle):
     assert u.launches > 100
 
 
-@pytest.mark.parametrize("B,h,w", [(1, 8, 8), (2, 8, 16)])
+@pytest.mark.parametrize("B,h,w", [(1, 8, 8), (2, 8, 16), (1, 64, 64)])
 def test_vae_decoder_vs_oracle(ctx, dib, oracle, B, h, w):
     """SD VAE decoder (config 5's decode) at small latents: cosine >= 0.999 and max-rel <= 1e-2 against the
     oracle's diffusers-Decoder restatement on the same seeded weights."""
