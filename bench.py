@@ -225,6 +225,40 @@ def vae_result(ctx, pk, src):
     return out
 
 
+def t2i_result(ctx, pk, src, B=64, reps=3):
+    """Config 5: batched one-step text-to-image (text encoder -> U-Net B=64 -> VAE), images/s on one GPU,
+    with each stage's device time and its tensor-pipe fraction."""
+    import torch
+    t2i = importlib.import_module("draw_instant_b200.t2i")
+    t0 = time.perf_counter()
+    p = t2i.Text2Image(ctx, B=B, h=64, w=64, text_layers=24, seed=4)
+    build_s = time.perf_counter() - t0
+    g = torch.Generator(device="cuda").manual_seed(4)
+    p.ids.copy_(torch.randint(0, 49408, (B, 77), device="cuda", generator=g, dtype=torch.int32))
+    p.latent.copy_(torch.randn(B, 4, 64, 64, device="cuda", generator=g) * p.sigma0)
+    for _ in range(2):
+        p.forward()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ms = time_events(lambda: p.forward(), reps, stream)
+    stage_ms = [time_events(lambda k=k: p.forward(k), reps, stream) for k in range(3)]
+    fl = p.flops()
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    stages = {}
+    for i, n in enumerate(["text", "unet", "vae"]):
+        tf = fl[n] / (stage_ms[i] / 1e3) / 1e12
+        stages[n] = {"ms": stage_ms[i], "tflops": tf, "frac": tf / peak}
+    total = sum(fl.values())
+    out = {"batch": B, "ms": ms, "images_per_s": B / (ms / 1e3), "tflops": total / (ms / 1e3) / 1e12,
+           "gflop": total / 1e9, "stages": stages, "launches": p.launches, "build_s": build_s,
+           "finite": bool(torch.isfinite(p.image).all().item()),
+           "peak_source": f"{src} bf16_tflops_sustained (a step of a second or more)",
+           "data": "random token ids U[0,49408) x 77, latents N(0,1) x sigma0, seeded random-init weights"}
+    del p
+    torch.cuda.empty_cache()
+    return out
+
+
 def time_events(fn, iters, stream):
     import torch
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -412,6 +446,10 @@ def main():
                 line["blocks"]["vae_decode_512"] = vae_result(ctx, pk, src)
             except Exception as e:  # a reported extra; never fail the bench line on it
                 line["blocks"]["vae_decode_512"] = {"error": str(e)}
+            try:
+                line["blocks"]["t2i_config5"] = t2i_result(ctx, pk, src)
+            except Exception as e:  # a reported extra; never fail the bench line on it
+                line["blocks"]["t2i_config5"] = {"error": str(e)}
             try:
                 v, sample, cores = cpu_baseline(unet_mod)
                 line["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": cores, "kind": "port",

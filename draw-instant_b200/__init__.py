@@ -102,6 +102,22 @@ SIGNATURES = {
     "di_vae_forward_host": (_I, [_P, _P, _P]),
     "di_vae_destroy": (None, [_P]),
     "di_vae_debug_copy": (_I, [_P, _I, _SZ, _P, _SZ]),
+    "di_linear_act": (_I, [_P, _I, _P, _I, _I, _P, _I, _P, _P, _I, _P]),
+    "di_attention_causal": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I, _I]),
+    "di_unet_sched": (_I, [_P, ctypes.c_double, ctypes.c_double, ctypes.POINTER(_P)]),
+    "di_text_create": (_I, [_P, _I, _I, _I, ctypes.c_uint64, _P, _P, ctypes.POINTER(_P)]),
+    "di_text_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "di_text_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "di_text_ops": (_I, [_P, ctypes.POINTER(_I), _P, _P, _P, _P]),
+    "di_text_forward": (_I, [_P]),
+    "di_text_forward_host": (_I, [_P, _P, _P]),
+    "di_text_destroy": (None, [_P]),
+    "di_t2i_create": (_I, [_P, _I, _I, _I, _I, ctypes.c_uint64, _P, _P, ctypes.POINTER(_P)]),
+    "di_t2i_io": (_I, [_P] + [ctypes.POINTER(_P)] * 5),
+    "di_t2i_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ), ctypes.POINTER(_F)]),
+    "di_t2i_forward": (_I, [_P, _I]),
+    "di_t2i_forward_host": (_I, [_P, _P, _P, _P]),
+    "di_t2i_destroy": (None, [_P]),
     "di_resnet_block_create": (_I, [_P, _I, _I, _I, _I, _I, ctypes.c_uint64, _F, _I, _P, _P, ctypes.POINTER(_P)]),
     "di_resnet_block_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)]),
     "di_resnet_block_run": (_I, [_P]),
@@ -158,7 +174,7 @@ class DeviceView:
 
 def view(p, shape, dtype: str = "f32"):
     import torch
-    ts = {"f32": "<f4", "f16": "<f2"}[dtype]
+    ts = {"f32": "<f4", "f16": "<f2", "i32": "<i4"}[dtype]
     return torch.as_tensor(DeviceView(p if isinstance(p, int) else p.value, shape, ts), device="cuda")
 
 

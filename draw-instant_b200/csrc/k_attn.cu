@@ -38,6 +38,7 @@ struct AttnParams {
   long long o_sb, o_ss, o_sh;  // output strides in elements (image, token, head)
   int Sq, Skv, H;
   int layout;                  // 0: dims {64, H, S, B}; 1: dims {64, S, H, B}
+  int causal;                  // 1: query i attends to keys 0..i only (CLIP text encoder)
   float scale_log2;            // (1/sqrt(d)) * log2(e)
   int* err;
 };
@@ -98,7 +99,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int q0 = blockIdx.x * QT, h = blockIdx.y, b = blockIdx.z;
-  const int nt = (p.Skv + KT - 1) / KT;
+  // causal: the CTA's last query row q0 + QT - 1 sees keys up to that index only
+  const int nt = (min(p.Skv, p.causal ? q0 + QT : p.Skv) + KT - 1) / KT;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -211,7 +213,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
         }
       }
-      const int kvalid = p.Skv - j * KT;
+      int kvalid = p.Skv - j * KT;
+      if (p.causal) kvalid = min(kvalid, q0 + row + 1 - j * KT);  // key index <= query index
       if (kvalid < KT) {
 #pragma unroll
         for (int i = 0; i < KT; ++i)
@@ -341,9 +344,10 @@ bool attn_map(CUtensorMap* m, int dtype, const void* base, int B, int H, int S, 
 
 // ld_* = token row stride in elements for layout 0 (H*64 when packed); ignored for layout 1.
 int attention(Ctx* c, int dtype, const void* Q, const void* K, const void* V, void* O, int B, int H, int Sq, int Skv,
-              int layout, long long ld_q, long long ld_k, long long ld_v, long long ld_o) {
+              int layout, long long ld_q, long long ld_k, long long ld_v, long long ld_o, int causal) {
   if (B <= 0 || H <= 0 || Sq <= 0 || Skv <= 0 || (layout != 0 && layout != 1))
     return set_error(c, DI_EINVAL, "attention: bad shape");
+  if (causal && Sq != Skv) return set_error(c, DI_EINVAL, "attention: causal needs Sq == Skv");
   AttnParams p;
   memset(&p, 0, sizeof p);
   if (!attn_map(&p.tmQ, dtype, Q, B, H, Sq, layout, ld_q, QT) || !attn_map(&p.tmK, dtype, K, B, H, Skv, layout, ld_k, KT) ||
@@ -356,6 +360,7 @@ int attention(Ctx* c, int dtype, const void* Q, const void* K, const void* V, vo
   p.Skv = Skv;
   p.H = H;
   p.layout = layout;
+  p.causal = causal ? 1 : 0;
   p.scale_log2 = 0.125f * 1.4426950408889634f;
   p.err = c->d_err;
   auto kern = dtype == DI_BF16 ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
@@ -380,5 +385,13 @@ extern "C" int di_attention(di_ctx_t h, int dtype, const void* Q, const void* K,
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
   const long long ld = (long long)H * 64;
-  return attention(c, dtype, Q, K, V, O, B, H, Sq, Skv, layout, ld, ld, ld, ld);
+  return attention(c, dtype, Q, K, V, O, B, H, Sq, Skv, layout, ld, ld, ld, ld, 0);
+}
+
+extern "C" int di_attention_causal(di_ctx_t h, int dtype, const void* Q, const void* K, const void* V, void* O, int B,
+                                   int H, int S, int layout) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
+  const long long ld = (long long)H * 64;
+  return attention(c, dtype, Q, K, V, O, B, H, S, S, layout, ld, ld, ld, ld, 1);
 }

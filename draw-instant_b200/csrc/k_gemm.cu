@@ -49,7 +49,7 @@ struct GemmParams {
   void* out;
   int ldo, out_f32;
   int geglu;
-  int act_silu;  // SiLU after bias / row vector, before the residual (y = silu(acc + b) + r)
+  int act;  // after bias / row vector, before the residual: 0 none, 1 SiLU (y = silu(acc + b) + r), 2 GELU (erf)
   int vec_ok;  // 16-byte aligned rows for out / residual: vectorised epilogue
   int b_early;     // weights are constant data: fetch the first B stages before the dependency wait
   int splits;      // K splits; > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
@@ -554,9 +554,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                     if (nb + j < n_out) v[j] += rv[j];
                 }
               }
-              if (p.act_silu) {
+              if (p.act == 1) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+              } else if (p.act == 2) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
               }
               if (p.residual) {
                 if (full && p.vec_ok) {
@@ -752,7 +755,7 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
       for (int j = 0; j < 4; ++j) {
         if (bias) f[j] += bias[o + j];
         if (rowvec) f[j] += rowvec[(size_t)(m / rowvec_div) * rowvec_ld + o + j];
-        if (act) f[j] = silu_f(f[j]);
+        if (act) f[j] = act == 1 ? silu_f(f[j]) : gelu_erf(f[j]);
         if (residual) f[j] += load_one(residual, (size_t)m * ldr + o + j, res_f32, bf16);
         store_one(out, (size_t)m * ldo + o + j, f[j], out_f32, bf16);
       }
@@ -767,7 +770,7 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
       for (int z = 0; z < splits; ++z) v += part[z * slice + (size_t)m * N + o];
       if (bias) v += bias[o];
       if (rowvec) v += rowvec[(size_t)(m / rowvec_div) * rowvec_ld + o];
-      if (act) v = silu_f(v);
+      if (act) v = act == 1 ? silu_f(v) : gelu_erf(v);
       if (residual) v += load_one(residual, (size_t)m * ldr + o, res_f32, bf16);
       store_one(out, (size_t)m * ldo + o, v, out_f32, bf16);
     } else {
@@ -900,7 +903,7 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
     launch_k(splitk_reduce, blocks, 256, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,
-             p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32, p.geglu, bf16, p.act_silu);
+             p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32, p.geglu, bf16, p.act);
     return check_launch(c, "splitk_reduce");
   }
   return dispatch_variant(c, p, bn, bf16, pair);
@@ -969,7 +972,7 @@ static GemmParams base_params() {
 // Public building blocks used by the fused blocks and the U-Net plan ---------------------------
 int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
                 const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
-                int rowvec_div, void* splitk_ws, const GnFuse* gnf, int gnf_hw) {
+                int rowvec_div, void* splitk_ws, const GnFuse* gnf, int gnf_hw, int act) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 64 || (X2 && (K1 <= 0 || K1 % 64 || K1 >= K)))
     return set_error(c, DI_EINVAL, "linear: K and K1 must be multiples of 64");
   if (geglu && (N % 128)) return set_error(c, DI_EINVAL, "linear_geglu: F must be a multiple of 64");
@@ -1001,6 +1004,7 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
   p.ldo = geglu ? N / 2 : N;
   p.out_f32 = out_f32;
   p.geglu = geglu;
+  p.act = geglu ? 0 : act;
   p.vec_ok = vec_rows_ok(Y, p.ldo, out_f32 ? 4 : 2) && (!R || vec_rows_ok(R, N, res_f32 ? 4 : 2));
   (void)bn;
   if (gnf && gnf->tab) {  // rows are pixels of images of gnf_hw pixels (GnFuse on a 1x1 projection)
@@ -1063,7 +1067,7 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
   p.ldo = Co;
   p.out_f32 = out_f32;
   p.vec_ok = vec_rows_ok(y, Co, out_f32 ? 4 : 2) && (!residual || vec_rows_ok(residual, Co, res_f32 ? 4 : 2));
-  p.act_silu = act;
+  p.act = act;
   if (gnf && gnf->tab) {
     if (stride != 1) return set_error(c, DI_EUNSUPPORTED, "conv3x3: fused GroupNorm needs stride 1");
     p.gn_tab = gnf->tab;
@@ -1117,7 +1121,14 @@ int di_linear(di_ctx_t h, int dtype, const void* X1, int K1, const void* X2, int
               const float* bias, const void* R, void* Y) {
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16)) return DI_EINVAL;
-  return gemm_linear(c, dtype, X1, K1, X2, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1, nullptr, nullptr, 0);
+  return gemm_linear(c, dtype, X1, K1, X2, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1, nullptr, nullptr, 0, 0);
+}
+
+int di_linear_act(di_ctx_t h, int dtype, const void* X, int M, int K, const void* W, int N, const float* bias,
+                  const void* R, int act, void* Y) {
+  Ctx* c = ctx_of(h);
+  if (!c || (dtype != DI_F16 && dtype != DI_BF16) || act < 0 || act > 2) return DI_EINVAL;
+  return gemm_linear(c, dtype, X, K, nullptr, M, K, W, N, bias, R, 0, Y, 0, 0, nullptr, 1, nullptr, nullptr, 0, act);
 }
 
 int di_linear_geglu(di_ctx_t h, int dtype, const void* X, int M, int K, const void* W, int F, const float* bias,
@@ -1125,7 +1136,7 @@ int di_linear_geglu(di_ctx_t h, int dtype, const void* X, int M, int K, const vo
   Ctx* c = ctx_of(h);
   if (!c || (dtype != DI_F16 && dtype != DI_BF16) || F % 64) return DI_EINVAL;
   return gemm_linear(c, dtype, X, K, nullptr, M, K, W, 2 * F, bias, nullptr, 0, Y, 0, 1, nullptr, 1, nullptr, nullptr,
-                     0);
+                     0, 0);
 }
 
 int di_conv3x3_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W,

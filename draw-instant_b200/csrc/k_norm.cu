@@ -544,6 +544,7 @@ int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* 
                                                          rows, D, eps);                                         \
   return check_launch(c, "layer_norm")
   if (in_dtype == DI_F32 && out_dtype == DI_F32) { LN_CASE(float, float); }
+  if (in_dtype == DI_F32 && out_dtype == DI_F16) { LN_CASE(float, __half); }
   if (in_dtype == DI_F16 && out_dtype == DI_F16) { LN_CASE(__half, __half); }
   if (in_dtype == DI_BF16 && out_dtype == DI_BF16) { LN_CASE(__nv_bfloat16, __nv_bfloat16); }
 #undef LN_CASE

@@ -33,7 +33,7 @@ namespace di {
 
 int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M, int K, const void* W, int N,
                 const float* bias, const void* R, int res_f32, void* Y, int out_f32, int geglu, const float* rowvec,
-                int rowvec_div, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr, int gnf_hw = 0);
+                int rowvec_div, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr, int gnf_hw = 0, int act = 0);
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
                  const void* Wt, int Co, const float* bias, const float* temb, const void* residual, int res_f32,
                  void* y, int out_f32, int temb_ld, void* splitk_ws = nullptr, const GnFuse* gnf = nullptr,
@@ -50,7 +50,7 @@ int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu);
 int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* g, const float* b, void* y, int rows,
                int D, float eps);
 int attention(Ctx* c, int dtype, const void* Q, const void* K, const void* V, void* O, int B, int H, int Sq, int Skv,
-              int layout, long long ld_q, long long ld_k, long long ld_v, long long ld_o);
+              int layout, long long ld_q, long long ld_k, long long ld_v, long long ld_o, int causal = 0);
 int gemv(Ctx* c, const float* x, int B, int K, const void* W, int w_f16, const float* bias, int N, int silu_in,
          float* y, int ldy);
 int tembed(Ctx* c, const float* t, int B, const float* W1, const float* b1, const float* W2, const float* b2, int Din,
@@ -110,26 +110,71 @@ void synth_normal(uint64_t seed, const char* name, size_t n, float mean, float s
 
 namespace {
 
-__global__ void latent_in_kernel(const float* __restrict__ x, __half* __restrict__ y, int N, int C, int HW, int Cp) {
+// Latent NCHW fp32 -> NHWC fp16 padded to Cp channels.  sched (device, may be null) holds the Euler
+// scheduler's scaleModelInput factor in sched[0] (scheduler.js:95-101): the value fed to the U-Net is
+// float(double(x) * sched[0]), the reference's double multiply and Float32Array store.
+__global__ void latent_in_kernel(const float* __restrict__ x, __half* __restrict__ y, int N, int C, int HW, int Cp,
+                                 const double* __restrict__ sched) {
   pdl_begin();
   const size_t total = (size_t)N * HW * Cp;
+  const double scale = sched ? sched[0] : 1.0;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int c = i % Cp;
     const size_t np = i / Cp;
     const int p = np % HW;
     const size_t n = np / HW;
-    y[i] = __float2half_rn(c < C ? x[(n * C + c) * HW + p] : 0.f);
+    const float v = c < C ? (float)__dmul_rn((double)x[(n * C + c) * HW + p], scale) : 0.f;
+    y[i] = __float2half_rn(v);
   }
 }
-__global__ void latent_out_kernel(const __half* __restrict__ x, int Cp, float* __restrict__ y, int N, int C, int HW) {
+// U-Net output NHWC fp16 (Cp channels) -> NCHW fp32 noise prediction.  With `next`, also the Euler step
+// of scheduler.js:105-110: next = float(double(x_in) + sched[1] * double(eps)), sched[1] = sigma_{i+1} -
+// sigma_i, rounded like the reference (a double product, then a double sum, no fused multiply-add).
+__global__ void latent_out_kernel(const __half* __restrict__ x, int Cp, float* __restrict__ y, int N, int C, int HW,
+                                  const float* __restrict__ x_in, const double* __restrict__ sched,
+                                  float* __restrict__ next) {
   pdl_begin();
   const size_t total = (size_t)N * C * HW;
+  const double dt = sched ? sched[1] : 0.0;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int p = i % HW;
     const size_t nc = i / HW;
     const int c = nc % C;
     const size_t n = nc / C;
-    y[i] = __half2float(x[(n * HW + p) * Cp + c]);
+    const float e = __half2float(x[(n * HW + p) * Cp + c]);
+    y[i] = e;
+    if (next) next[i] = (float)__dadd_rn((double)x_in[i], __dmul_rn(dt, (double)e));
+  }
+}
+// CLIP text embeddings: x[t, :] = token_embedding[ids[t]] + position_embedding[t % S] (fp16 tables, fp32
+// sum).  Ids outside [0, V) are clamped for the read and flagged in the device error word.
+__global__ void embed_tokens_kernel(const int* __restrict__ ids, int tokens, int S, const __half* __restrict__ tok,
+                                    const __half* __restrict__ pos, int D, int V, float* __restrict__ x,
+                                    int* __restrict__ err) {
+  pdl_begin();
+  const int per = D / 8;
+  const size_t total = (size_t)tokens * per;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / per), c = (int)(i % per) * 8;
+    int id = ids[t];
+    if (id < 0 || id >= V) {
+      if (c == 0) atomicOr(err, DEVERR_BOUNDS);
+      id = id < 0 ? 0 : V - 1;
+    }
+    const uint4 a = *reinterpret_cast<const uint4*>(tok + (size_t)id * D + c);
+    const uint4 b = *reinterpret_cast<const uint4*>(pos + (size_t)(t % S) * D + c);
+    const __half2* ah = reinterpret_cast<const __half2*>(&a);
+    const __half2* bh = reinterpret_cast<const __half2*>(&b);
+    float r[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(ah[k]), g = __half22float2(bh[k]);
+      r[2 * k] = f.x + g.x;
+      r[2 * k + 1] = f.y + g.y;
+    }
+    float4* o = reinterpret_cast<float4*>(x + (size_t)t * D + c);
+    o[0] = make_float4(r[0], r[1], r[2], r[3]);
+    o[1] = make_float4(r[4], r[5], r[6], r[7]);
   }
 }
 // Row softmax in place on fp16 scores (the scale is folded into the query projection): one 256-thread
@@ -950,6 +995,9 @@ struct UNetPlan {
   float* tvals = nullptr;   // [B] fp32
   float* ctx32 = nullptr;   // [B,Sk,1024] fp32
   float* out = nullptr;     // [B,4,H,W] fp32 NCHW
+  float* next = nullptr;    // [B,4,H,W] fp32 NCHW: the Euler step latent + dt * out
+  double* sched = nullptr;  // device {scaleModelInput factor, sigma_{i+1} - sigma_i}; {1, 0} by default
+  float* ext_ctx = nullptr; // when set before building: the text-encoder output used as ctx32
   double gflop = 0;
 };
 
@@ -966,10 +1014,17 @@ static int build_unet(UNetPlan* u) {
   void* sk = P.splitk;
   u->latent = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 4 * H * W));
   u->tvals = static_cast<float*>(P.act_alloc(sizeof(float) * B));
-  u->ctx32 = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * Sk * 1024));
+  u->ctx32 = u->ext_ctx ? u->ext_ctx : static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * Sk * 1024));
   u->out = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 4 * H * W));
+  u->next = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 4 * H * W));
+  u->sched = static_cast<double*>(P.act_alloc(2 * sizeof(double)));
   __half* ctx16 = static_cast<__half*>(P.act_alloc(sizeof(__half) * (size_t)B * Sk * 1024));
   if (P.err) return P.err;
+  {
+    const double s0[2] = {1.0, 0.0};
+    cudaMemcpy(u->sched, s0, sizeof s0, cudaMemcpyHostToDevice);
+  }
+  const double* sched = u->sched;
   // inputs: ctx fp32 -> fp16, latent NCHW fp32 -> NHWC fp16 padded to 64 channels
   {
     const float* src = u->ctx32;
@@ -988,7 +1043,7 @@ static int build_unet(UNetPlan* u) {
     P.record([=] {
       const size_t n = (size_t)B * H * W * 64;
       launch_k(latent_in_kernel, (int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, cc->stream, 
-          src, static_cast<__half*>(dst), B, 4, H * W, 64);
+          src, static_cast<__half*>(dst), B, 4, H * W, 64, sched);
       return check_launch(cc, "latent_in");
     }, 3, 0, (double)B * H * W * (16 + 128));
   }
@@ -1074,12 +1129,14 @@ static int build_unet(UNetPlan* u) {
     },
              0, 2.0 * B * H * W * 4 * 9 * 320, (double)B * H * W * (640 + 32), gemm_kernel_count(cc, B * H * W, 16, 9 * 320, 0));
     float* out = u->out;
+    float* next = u->next;
+    const float* x_in = u->latent;
     P.record([=] {
       const size_t n = (size_t)B * 4 * H * W;
-      launch_k(latent_out_kernel, (int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream, 
-          static_cast<const __half*>(y16), 16, out, B, 4, H * W);
+      launch_k(latent_out_kernel, (int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, cc->stream,
+          static_cast<const __half*>(y16), 16, out, B, 4, H * W, x_in, sched, next);
       return check_launch(cc, "latent_out");
-    }, 3, 0, (double)B * H * W * (32 + 16));
+    }, 3, 0, (double)B * H * W * (32 + 16 + 32));
   }
   P.finish_time_proj(tproj_at, temb, B);
   cudaDeviceSynchronize();
@@ -1214,7 +1271,7 @@ static int build_vae(VaePlan* v) {
     P.record([=] {
       const size_t n = (size_t)B * h * w * 64;
       launch_k(latent_in_kernel, (int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, cc->stream, src,
-               static_cast<__half*>(dst), B, 4, h * w, 64);
+               static_cast<__half*>(dst), B, 4, h * w, 64, nullptr);
       return check_launch(cc, "vae latent_in");
     }, 3, 0, (double)B * h * w * (16 + 128));
   }
@@ -1276,7 +1333,7 @@ static int build_vae(VaePlan* v) {
     P.record([=] {
       const size_t n = (size_t)B * 3 * H * W;
       launch_k(latent_out_kernel, (int)std::min<size_t>((n + 255) / 256, 8192), 256, 0, cc->stream,
-               static_cast<const __half*>(y16), 16, out, B, 3, H * W);
+               static_cast<const __half*>(y16), 16, out, B, 3, H * W, nullptr, nullptr, nullptr);
       return check_launch(cc, "vae image_out");
     }, 3, 0, (double)B * H * W * (32 + 12));
   }
@@ -1284,7 +1341,144 @@ static int build_vae(VaePlan* v) {
   return P.err;
 }
 
+// OpenCLIP ViT-H text encoder as SD2.x / SD-Turbo use it (HF CLIPTextModel names): token + position
+// embeddings, `layers` pre-LN blocks (causal multi-head self-attention with biased q/k/v/out projections,
+// MLP 1024 -> 4096 -> 1024 with erf GELU), final LayerNorm.  The reference runs this model through ONNX
+// Runtime (text-encoder.js:69-174); its output is last_hidden_state [B, 77, 1024].
+// The residual stream stays fp32 (the GEMM epilogues add the residual in fp32 and write fp32);
+// LayerNorm outputs, q/k/v, attention output and the MLP hidden are fp16.
+struct TextPlan {
+  Plan P;
+  int B = 1, S = 77, layers = 24;
+  int* ids = nullptr;          // [B,S] int32 token ids (input)
+  float* hidden = nullptr;     // [B,S,1024] fp32 (output)
+  float* ext_hidden = nullptr; // when set before building: write the output here (the U-Net's context)
+};
+
+static constexpr int kTextD = 1024, kTextHeads = 16, kTextF = 4096, kTextVocab = 49408, kTextPos = 77;
+
+static size_t text_tmp_bytes(int, int) { return 1u << 20; }
+
+static int build_text(TextPlan* t) {
+  Plan& P = t->P;
+  const int B = t->B, S = t->S, D = kTextD, F = kTextF, M = B * S;
+  Ctx* cc = P.c;
+  void* sk = P.splitk;
+  t->ids = static_cast<int*>(P.act_alloc(sizeof(int) * (size_t)M));
+  t->hidden = t->ext_hidden ? t->ext_hidden : static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)M * D));
+  float* x = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)M * D));
+  __half* n = static_cast<__half*>(P.act_alloc(2 * (size_t)M * D));
+  __half* qkv = static_cast<__half*>(P.act_alloc(2 * (size_t)M * 3 * D));
+  __half* o = static_cast<__half*>(P.act_alloc(2 * (size_t)M * D));
+  __half* mid = static_cast<__half*>(P.act_alloc(2 * (size_t)M * F));
+  if (P.err) return P.err;
+  {
+    const void* tok = P.upload_f16(P.host_param("text_model.embeddings.token_embedding.weight",
+                                                (size_t)kTextVocab * D, 2, 1));
+    const void* pos = P.upload_f16(P.host_param("text_model.embeddings.position_embedding.weight",
+                                                (size_t)kTextPos * D, 2, 1));
+    const int* ids = t->ids;
+    P.record([=] {
+      const size_t total = (size_t)M * (D / 8);
+      launch_k(embed_tokens_kernel, (int)std::min<size_t>((total + 255) / 256, 4096), 256, 0, cc->stream, ids, M, S,
+               static_cast<const __half*>(tok), static_cast<const __half*>(pos), D, kTextVocab, x, cc->d_err);
+      return check_launch(cc, "embed_tokens");
+    }, 3, 0, (double)M * D * (2 + 2 + 4));
+  }
+  for (int l = 0; l < t->layers; ++l) {
+    const std::string pre = "text_model.encoder.layers." + std::to_string(l);
+    const float* g1 = P.vec(pre + ".layer_norm1.weight", D, 1, 1);
+    const float* b1 = P.vec(pre + ".layer_norm1.bias", D, 2, 1);
+    P.record([=] { return layer_norm(cc, DI_F32, DI_F16, x, g1, b1, n, M, D, 1e-5f); }, 2, 0, 6.0 * M * D);
+    std::vector<float> wqkv, bqkv;
+    for (const char* nm : {".self_attn.q_proj", ".self_attn.k_proj", ".self_attn.v_proj"}) {
+      auto w = P.host_param(pre + nm + ".weight", (size_t)D * D, 0, D, D);
+      auto b = P.host_param(pre + nm + ".bias", D, 0, D);
+      wqkv.insert(wqkv.end(), w.begin(), w.end());
+      bqkv.insert(bqkv.end(), b.begin(), b.end());
+    }
+    Plan::round_f16(bqkv);
+    const void* Wqkv = P.upload_f16(wqkv);
+    const float* Bqkv = P.upload_f32(bqkv);
+    P.linear(n, M, D, Wqkv, 3 * D, Bqkv, nullptr, qkv);
+    P.record([=] {
+      return attention(cc, DI_F16, qkv, qkv + D, qkv + 2 * D, o, B, kTextHeads, S, S, 0, 3 * D, 3 * D, 3 * D, D, 1);
+    }, 1, 2.0 * B * kTextHeads * (double)S * (S + 1) * 64, 2.0 * 4 * M * D);
+    const void* Wo = P.lin_weight(pre + ".self_attn.out_proj.weight", D, D);
+    const float* Bo = P.vec(pre + ".self_attn.out_proj.bias", D, 0, D);
+    P.record([=] { return gemm_linear(cc, DI_F16, o, D, nullptr, M, D, Wo, D, Bo, x, 1, x, 1, 0, nullptr, 1, sk); },
+             0, 2.0 * M * D * D, 2.0 * ((double)M * D + (double)D * D) + 8.0 * M * D, gemm_kernel_count(cc, M, D, D, 0));
+    const float* g2 = P.vec(pre + ".layer_norm2.weight", D, 1, 1);
+    const float* b2 = P.vec(pre + ".layer_norm2.bias", D, 2, 1);
+    P.record([=] { return layer_norm(cc, DI_F32, DI_F16, x, g2, b2, n, M, D, 1e-5f); }, 2, 0, 6.0 * M * D);
+    const void* W1 = P.lin_weight(pre + ".mlp.fc1.weight", F, D);
+    const float* B1 = P.vec(pre + ".mlp.fc1.bias", F, 0, D);
+    P.record([=] {
+      return gemm_linear(cc, DI_F16, n, D, nullptr, M, D, W1, F, B1, nullptr, 0, mid, 0, 0, nullptr, 1, sk, nullptr, 0,
+                         2);
+    }, 0, 2.0 * M * F * D, 2.0 * ((double)M * D + (double)F * D + (double)M * F), gemm_kernel_count(cc, M, F, D, 0));
+    const void* W2 = P.lin_weight(pre + ".mlp.fc2.weight", D, F);
+    const float* B2 = P.vec(pre + ".mlp.fc2.bias", D, 0, F);
+    P.record([=] { return gemm_linear(cc, DI_F16, mid, F, nullptr, M, F, W2, D, B2, x, 1, x, 1, 0, nullptr, 1, sk); },
+             0, 2.0 * M * D * F, 2.0 * ((double)M * F + (double)D * F) + 8.0 * M * D, gemm_kernel_count(cc, M, D, F, 0));
+  }
+  const float* gf = P.vec("text_model.final_layer_norm.weight", D, 1, 1);
+  const float* bf = P.vec("text_model.final_layer_norm.bias", D, 2, 1);
+  float* out = t->hidden;
+  P.record([=] { return layer_norm(cc, DI_F32, DI_F32, x, gf, bf, out, M, D, 1e-5f); }, 2, 0, 8.0 * M * D);
+  cudaDeviceSynchronize();
+  return P.err;
+}
+
+// Batched one-step text-to-image (config 5): text encoder -> U-Net (scaleModelInput fused into its input
+// conversion, the Euler step into its output conversion) -> VAE decoder; the text encoder writes the
+// U-Net's context directly.  The VAE decodes in chunks of up to 8 images (its 512x512 maps are 0.5 GB per
+// image at 256 channels): each chunk's latent is copied into the VAE plan's input and its image out to
+// the pipeline's image buffer.  Three plans (CUDA graphs) replayed in order on the context stream.
+struct T2IPlan {
+  TextPlan text;
+  UNetPlan unet;
+  VaePlan vae;
+  int vae_chunk = 1;
+  float* image = nullptr;  // [B,3,8h,8w] fp32
+  float sigma0 = 0.f;
+};
+
 struct di_unet_s { UNetPlan u; };
+struct di_text_s { TextPlan t; };
+struct di_t2i_s { T2IPlan p; };
+
+// Euler-discrete sigmas of scheduler.js:27-89 for n inference steps ("trailing" timesteps, the last sigma
+// 0): double arithmetic rounded to float at each Float32Array store, Math.round as floor(x + 0.5).
+static void euler_sigmas(int n, float* sig_out, float* ts_out) {
+  std::vector<float> betas(1000), alphas(1000), sig(1000);
+  const double b0 = std::sqrt(0.00085), b1 = std::sqrt(0.012);
+  for (int i = 0; i < 1000; ++i) {
+    const double v = b0 + (b1 - b0) * (i / 999.0);
+    betas[i] = (float)(v * v);
+  }
+  double prod = 1.0;
+  for (int i = 0; i < 1000; ++i) {
+    prod *= 1.0 - (double)betas[i];
+    alphas[i] = (float)prod;
+  }
+  for (int i = 0; i < 1000; ++i) sig[i] = (float)std::sqrt((1.0 - (double)alphas[i]) / (double)alphas[i]);
+  const double step = 1000.0 / n;
+  for (int i = 0; i < n; ++i) {
+    const float t = (float)std::floor(1000.0 - (i + 1) * step + step + 0.5) - 1.0f;
+    ts_out[i] = t;
+    double v;
+    if (t <= 0) v = sig[0];
+    else if (t >= 999) v = sig[999];
+    else {
+      const int k = (int)std::floor((double)t);
+      const double f = (double)t - k;
+      v = (double)sig[k] * (1 - f) + (double)sig[k + 1] * f;
+    }
+    sig_out[i] = (float)v;
+  }
+  sig_out[n] = 0.0f;
+}
 struct di_vae_s { VaePlan v; };
 struct di_resnet_s { ResPlan r; };
 struct di_tblock_s { TBPlan t; };
@@ -1318,6 +1512,19 @@ DI_API int di_unet_create(di_ctx_t h, int B, int H, int W, int ctx_len, uint64_t
     return set_error(c, r, "unet build: " + m);
   }
   *out = s;
+  return DI_OK;
+}
+
+// Scheduler on the device: the U-Net scales its latent input by `in_scale` (scaleModelInput) and writes
+// next = latent + dt * eps (the Euler step) beside the noise prediction.  Defaults 1 and 0.
+DI_API int di_unet_sched(di_unet_t u, double in_scale, double dt, float** next) {
+  if (!u) return DI_EINVAL;
+  const double v[2] = {in_scale, dt};
+  Ctx* c = u->u.P.c;
+  if (cudaMemcpyAsync(u->u.sched, v, sizeof v, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+      cudaStreamSynchronize(c->stream) != cudaSuccess)
+    return set_error(c, DI_ECUDA, "unet sched: copy");
+  if (next) *next = u->u.next;
   return DI_OK;
 }
 
@@ -1382,6 +1589,177 @@ DI_API int di_unet_forward_host(di_unet_t u, const float* latent, const float* t
 }
 
 DI_API void di_unet_destroy(di_unet_t u) { delete u; }
+
+// ---- text encoder -----------------------------------------------------------------------------
+DI_API int di_text_create(di_ctx_t h, int B, int S, int layers, uint64_t seed, di_weight_fn fn, void* user,
+                          di_text_t* out) {
+  Ctx* c = ctx_of(h);
+  if (!c || !out || B <= 0 || S <= 0 || S > kTextPos || layers <= 0) return DI_EINVAL;
+  *out = nullptr;
+  auto* s = new di_text_s();
+  s->t.B = B; s->t.S = S; s->t.layers = layers;
+  cudaSetDevice(c->device);
+  if (!s->t.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, text_tmp_bytes(B, S))) {
+    delete s;
+    return set_error(c, DI_ENOMEM, "text encoder: init");
+  }
+  int r = build_text(&s->t);
+  if (r) {
+    std::string m = s->t.P.errmsg;
+    delete s;
+    return set_error(c, r, "text encoder build: " + m);
+  }
+  *out = s;
+  return DI_OK;
+}
+DI_API int di_text_io(di_text_t t, int** ids, float** hidden) {
+  if (!t) return DI_EINVAL;
+  if (ids) *ids = t->t.ids;
+  if (hidden) *hidden = t->t.hidden;
+  return DI_OK;
+}
+DI_API int di_text_info(di_text_t t, int* launches, size_t* weight_bytes, size_t* act_bytes) {
+  if (!t) return DI_EINVAL;
+  if (launches) *launches = t->t.P.launches;
+  if (weight_bytes) *weight_bytes = t->t.P.weight_bytes;
+  if (act_bytes) *act_bytes = t->t.P.act_bytes;
+  return DI_OK;
+}
+DI_API int di_text_ops(di_text_t t, int* n_ops, int* kinds, double* flops, double* bytes, int* kernels) {
+  if (!t || !n_ops) return DI_EINVAL;
+  const auto& I = t->t.P.info;
+  *n_ops = (int)I.size();
+  for (size_t i = 0; i < I.size(); ++i) {
+    if (kinds) kinds[i] = I[i].kind;
+    if (flops) flops[i] = I[i].flops;
+    if (bytes) bytes[i] = I[i].bytes;
+    if (kernels) kernels[i] = I[i].kernels;
+  }
+  return DI_OK;
+}
+DI_API int di_text_forward(di_text_t t) { return t ? t->t.P.forward() : DI_EINVAL; }
+DI_API int di_text_forward_host(di_text_t t, const int* ids, float* hidden) {
+  if (!t || !ids || !hidden) return DI_EINVAL;
+  TextPlan& p = t->t;
+  Ctx* c = p.P.c;
+  const size_t n = (size_t)p.B * p.S;
+  for (size_t i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= kTextVocab) return set_error(c, DI_EINVAL, "text encoder: token id out of range");
+  cudaMemcpyAsync(p.ids, ids, n * 4, cudaMemcpyHostToDevice, c->stream);
+  int r = p.P.forward();
+  if (r) return r;
+  cudaMemcpyAsync(hidden, p.hidden, n * kTextD * 4, cudaMemcpyDeviceToHost, c->stream);
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return set_error(c, DI_ECUDA, "text forward_host sync");
+  return DI_OK;
+}
+DI_API void di_text_destroy(di_text_t t) { delete t; }
+
+// ---- one-step text-to-image (config 5) --------------------------------------------------------
+DI_API int di_t2i_create(di_ctx_t h, int B, int lh, int lw, int text_layers, uint64_t seed, di_weight_fn fn,
+                         void* user, di_t2i_t* out) {
+  Ctx* c = ctx_of(h);
+  if (!c || !out || B <= 0 || lh <= 0 || lw <= 0 || (lh % 8) || (lw % 8) || text_layers <= 0) return DI_EINVAL;
+  *out = nullptr;
+  auto* s = new di_t2i_s();
+  T2IPlan& p = s->p;
+  cudaSetDevice(c->device);
+  auto fail = [&](int r, const std::string& what) {
+    delete s;
+    return set_error(c, r, what);
+  };
+  p.unet.B = B; p.unet.H = lh; p.unet.W = lw; p.unet.Sk = kTextPos;
+  if (!p.unet.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, unet_tmp_bytes(B, lh, lw)))
+    return fail(DI_ENOMEM, "t2i: unet init");
+  // the U-Net plan owns the shared buffers: the context the text encoder writes, the decoded images
+  p.unet.ext_ctx = static_cast<float*>(p.unet.P.act_alloc(sizeof(float) * (size_t)B * kTextPos * kTextD));
+  p.image = static_cast<float*>(p.unet.P.act_alloc(sizeof(float) * (size_t)B * 3 * 64 * lh * lw));
+  int r = build_unet(&p.unet);
+  if (r) return fail(r, "t2i unet build: " + p.unet.P.errmsg);
+  p.text.B = B; p.text.S = kTextPos; p.text.layers = text_layers; p.text.ext_hidden = p.unet.ext_ctx;
+  if (!p.text.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, text_tmp_bytes(B, kTextPos)))
+    return fail(DI_ENOMEM, "t2i: text init");
+  r = build_text(&p.text);
+  if (r) return fail(r, "t2i text build: " + p.text.P.errmsg);
+  p.vae_chunk = 1;
+  for (int k = std::min(B, 8); k >= 1; --k)
+    if (B % k == 0) { p.vae_chunk = k; break; }
+  p.vae.B = p.vae_chunk; p.vae.h = lh; p.vae.w = lw;
+  if (!p.vae.P.init(c, seed, reinterpret_cast<WeightFn>(fn), user, vae_tmp_bytes(p.vae_chunk, lh, lw)))
+    return fail(DI_ENOMEM, "t2i: vae init");
+  r = build_vae(&p.vae);
+  if (r) return fail(r, "t2i vae build: " + p.vae.P.errmsg);
+  // one-step schedule: t = 999, scaleModelInput by 1/sqrt(sigma0^2 + 1), Euler step dt = 0 - sigma0
+  float sig[2], ts[1];
+  euler_sigmas(1, sig, ts);
+  p.sigma0 = sig[0];
+  std::vector<float> tv(B, ts[0]);
+  cudaMemcpy(p.unet.tvals, tv.data(), sizeof(float) * B, cudaMemcpyHostToDevice);
+  const double s0 = sig[0];
+  const double v[2] = {1.0 / std::sqrt(s0 * s0 + 1.0), (double)sig[1] - s0};
+  cudaMemcpy(p.unet.sched, v, sizeof v, cudaMemcpyHostToDevice);
+  *out = s;
+  return DI_OK;
+}
+DI_API int di_t2i_io(di_t2i_t t, int** ids, float** latent, float** image, float** ctx, float** eps) {
+  if (!t) return DI_EINVAL;
+  if (ids) *ids = t->p.text.ids;
+  if (latent) *latent = t->p.unet.latent;
+  if (image) *image = t->p.image;
+  if (ctx) *ctx = t->p.unet.ctx32;
+  if (eps) *eps = t->p.unet.out;
+  return DI_OK;
+}
+DI_API int di_t2i_info(di_t2i_t t, int* launches, size_t* weight_bytes, size_t* act_bytes, float* sigma0) {
+  if (!t) return DI_EINVAL;
+  const T2IPlan& p = t->p;
+  const int chunks = p.unet.B / p.vae_chunk;
+  if (launches) *launches = p.text.P.launches + p.unet.P.launches + chunks * p.vae.P.launches;
+  if (weight_bytes) *weight_bytes = p.text.P.weight_bytes + p.unet.P.weight_bytes + p.vae.P.weight_bytes;
+  if (act_bytes) *act_bytes = p.text.P.act_bytes + p.unet.P.act_bytes + p.vae.P.act_bytes;
+  if (sigma0) *sigma0 = p.sigma0;
+  return DI_OK;
+}
+// stage -1: the whole pipeline; 0 text encoder, 1 U-Net + scheduler, 2 VAE decoder.
+DI_API int di_t2i_forward(di_t2i_t t, int stage) {
+  if (!t || stage < -1 || stage > 2) return DI_EINVAL;
+  T2IPlan& p = t->p;
+  int r = DI_OK;
+  if (stage == -1 || stage == 0) r = p.text.P.forward();
+  if (r == DI_OK && (stage == -1 || stage == 1)) r = p.unet.P.forward();
+  if (r == DI_OK && (stage == -1 || stage == 2)) {
+    Ctx* c = p.unet.P.c;
+    const int k = p.vae_chunk;
+    const size_t lat = (size_t)4 * p.vae.h * p.vae.w, img = (size_t)3 * 64 * p.vae.h * p.vae.w;
+    for (int b0 = 0; r == DI_OK && b0 < p.unet.B; b0 += k) {
+      if (cudaMemcpyAsync(p.vae.latent, p.unet.next + b0 * lat, k * lat * 4, cudaMemcpyDeviceToDevice,
+                          c->stream) != cudaSuccess)
+        return set_error(c, DI_ECUDA, "t2i: latent chunk copy");
+      r = p.vae.P.forward();
+      if (r == DI_OK && cudaMemcpyAsync(p.image + b0 * img, p.vae.image, k * img * 4, cudaMemcpyDeviceToDevice,
+                                        c->stream) != cudaSuccess)
+        return set_error(c, DI_ECUDA, "t2i: image chunk copy");
+    }
+  }
+  return r;
+}
+DI_API int di_t2i_forward_host(di_t2i_t t, const int* ids, const float* latent, float* image) {
+  if (!t || !ids || !latent || !image) return DI_EINVAL;
+  T2IPlan& p = t->p;
+  Ctx* c = p.unet.P.c;
+  const int B = p.unet.B;
+  const size_t nid = (size_t)B * kTextPos, nl = (size_t)B * 4 * p.unet.H * p.unet.W;
+  const size_t ni = (size_t)B * 3 * 64 * p.unet.H * p.unet.W;
+  for (size_t i = 0; i < nid; ++i)
+    if (ids[i] < 0 || ids[i] >= kTextVocab) return set_error(c, DI_EINVAL, "t2i: token id out of range");
+  cudaMemcpyAsync(p.text.ids, ids, nid * 4, cudaMemcpyHostToDevice, c->stream);
+  cudaMemcpyAsync(p.unet.latent, latent, nl * 4, cudaMemcpyHostToDevice, c->stream);
+  int r = di_t2i_forward(t, -1);
+  if (r) return r;
+  cudaMemcpyAsync(image, p.image, ni * 4, cudaMemcpyDeviceToHost, c->stream);
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess) return set_error(c, DI_ECUDA, "t2i forward_host sync");
+  return DI_OK;
+}
+DI_API void di_t2i_destroy(di_t2i_t t) { delete t; }
 
 DI_API int di_vae_create(di_ctx_t h, int B, int lh, int lw, uint64_t seed, di_weight_fn fn, void* user, di_vae_t* out) {
   Ctx* c = ctx_of(h);

@@ -102,6 +102,14 @@ class UNet:
                                                   out.ctypes.data), "di_unet_forward_host")
         return out
 
+    def set_schedule(self, in_scale: float = 1.0, dt: float = 0.0):
+        """Scheduler on the device (scheduler.js:95-110): conv_in sees float(latent * in_scale) and the plan
+        writes `self.next` = float(latent + dt * eps) beside `self.out`.  Returns the `next` view."""
+        nx = ctypes.c_void_p()
+        self.ctx.check(lib().di_unet_sched(self.h, float(in_scale), float(dt), ctypes.byref(nx)), "di_unet_sched")
+        self.next = view(nx.value, (self.B, 4, self.H, self.W))
+        return self.next
+
     def close(self):
         if getattr(self, "h", None):
             lib().di_unet_destroy(self.h)

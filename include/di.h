@@ -155,6 +155,10 @@ DI_API int di_linear(di_ctx_t ctx, int dtype, const void* X1, int K1, const void
               const float* bias, const void* R, void* Y);
 /* GEGLU feed-forward up-projection: Y[M,F] = (X.Wv^T + bv) * gelu_erf(X.Wg^T + bg), W = [Wv; Wg] as [2F,K]
  * (diffusers GEGLU; erf GELU of wgsl-ops.js:69).  F multiple of 64. */
+/* Linear with an activation after the bias, before the residual: act 0 none, 1 SiLU, 2 erf GELU
+ * (wgsl-ops.js:69, the text encoder's MLP).  K multiple of 64. */
+DI_API int di_linear_act(di_ctx_t ctx, int dtype, const void* X, int M, int K, const void* W, int N, const float* bias,
+                         const void* R, int act, void* Y);
 DI_API int di_linear_geglu(di_ctx_t ctx, int dtype, const void* X, int M, int K, const void* W, int F, const float* bias,
                     void* Y);
 /* 3x3 conv, pad 1, stride 1 or 2, NHWC: x = concat(x1[...,C1], x2[...,C2]) (x2 may be NULL), W packed
@@ -188,6 +192,9 @@ DI_API int di_pack_conv3x3(di_ctx_t ctx, int dtype, const float* w_oihw, int Co,
  * Replaces WGSL_FUSED_ATTN (fused-attn.js:199-307) and the cross-attention kernel (fused-cross-attn.js:112-173). */
 DI_API int di_attention(di_ctx_t ctx, int dtype, const void* Q, const void* K, const void* V, void* O, int B, int H, int Sq,
                  int Skv, int layout);
+/* Causal attention (query i sees keys 0..i; the CLIP text encoder's self-attention), Sq = Skv = S. */
+DI_API int di_attention_causal(di_ctx_t ctx, int dtype, const void* Q, const void* K, const void* V, void* O, int B,
+                               int H, int S, int layout);
 
 /* Timestep embedding, fused-tembed.js:73-130: y[b] = W2 . silu(W1 . [cos||sin](t_b f) + b1) + b2 with
  * f_i = exp(-ln(1e4) i / (Din/2)); W1 [Dh,Din], W2 [Dh,Dh] row-major fp32; t, y fp32. */
@@ -205,6 +212,8 @@ typedef struct di_unet_s* di_unet_t;
 typedef struct di_resnet_s* di_resnet_t;
 typedef struct di_tblock_s* di_tblock_t;
 typedef struct di_vae_s* di_vae_t;
+typedef struct di_text_s* di_text_t;
+typedef struct di_t2i_s* di_t2i_t;
 typedef int (*di_weight_fn)(const char* name, size_t n, float* dst, void* user);
 
 /* The seeded parameter generator: key = mix64(seed*0x9E3779B97F4A7C15 + fnv1a64(name)),
@@ -232,10 +241,39 @@ DI_API int di_unet_forward(di_unet_t u);  /* enqueue one forward on the context 
 /* host buffers in, host buffer out, synchronous: the unetForwardWGSL(sample, timestep, cond) shape */
 DI_API int di_unet_forward_host(di_unet_t u, const float* latent, const float* t, const float* context, float* out);
 DI_API void di_unet_destroy(di_unet_t u);
+/* Scheduler on the device (scheduler.js:95-110): the U-Net feeds float(double(latent) * in_scale) to
+ * conv_in (scaleModelInput) and writes next = float(double(latent) + dt * double(eps)) (the Euler step,
+ * dt = sigma_{i+1} - sigma_i) beside its noise prediction.  Defaults: in_scale 1, dt 0.  *next receives
+ * the device buffer [B,4,H,W] fp32. */
+DI_API int di_unet_sched(di_unet_t u, double in_scale, double dt, float** next);
 
-/* Config-1 ResNet block, fp32 NCHW in and out (fused-resnet.js:121-208 + the timestep add it omits,
- * fused-resnet.js:9-12): y = conv2(silu(gn2(conv1(silu(gn1(x))) + Wt.act(temb) + bt))) + x;
- * act = SiLU when temb_silu (diffusers), identity otherwise.  Names: norm1/conv1/time_emb_proj/norm2/conv2. */
+/* OpenCLIP ViT-H text encoder (SD2.x / SD-Turbo; run by ONNX Runtime in the reference, text-encoder.js:
+ * 69-174): token ids [B,S] int32 (S <= 77, ids in [0, 49408)) -> last_hidden_state [B,S,1024] fp32.
+ * `layers` pre-LN blocks (causal 16-head self-attention, MLP 1024->4096->1024 with erf GELU), final
+ * LayerNorm; HF CLIPTextModel parameter names (text_model.embeddings.token_embedding.weight, ...). */
+DI_API int di_text_create(di_ctx_t ctx, int B, int S, int layers, uint64_t seed, di_weight_fn fn, void* user,
+                          di_text_t* out);
+DI_API int di_text_io(di_text_t t, int** ids, float** hidden);
+DI_API int di_text_info(di_text_t t, int* launches, size_t* weight_bytes, size_t* act_bytes);
+DI_API int di_text_ops(di_text_t t, int* n_ops, int* kinds, double* flops, double* bytes, int* kernels);
+DI_API int di_text_forward(di_text_t t);
+DI_API int di_text_forward_host(di_text_t t, const int* ids, float* hidden);
+DI_API void di_text_destroy(di_text_t t);
+
+/* Batched one-step text-to-image (config 5, pipeline.js's SD-Turbo generate path): text encoder ->
+ * U-Net at t = 999 with scaleModelInput and the Euler step on the device -> VAE decoder (in chunks of up
+ * to 8 images), on shared device buffers.  ids [B,77] int32; latent [B,4,h,w] fp32 = the noise already
+ * scaled by initNoiseSigma (sampleNoiseLatent); image [B,3,8h,8w] fp32.  One parameter seed for all
+ * three models. */
+DI_API int di_t2i_create(di_ctx_t ctx, int B, int h, int w, int text_layers, uint64_t seed, di_weight_fn fn,
+                         void* user, di_t2i_t* out);
+DI_API int di_t2i_io(di_t2i_t t, int** ids, float** latent, float** image, float** context, float** eps);
+DI_API int di_t2i_info(di_t2i_t t, int* launches, size_t* weight_bytes, size_t* act_bytes, float* sigma0);
+/* stage -1: the whole pipeline; 0 text encoder, 1 U-Net + scheduler, 2 VAE decoder */
+DI_API int di_t2i_forward(di_t2i_t t, int stage);
+DI_API int di_t2i_forward_host(di_t2i_t t, const int* ids, const float* latent, float* image);
+DI_API void di_t2i_destroy(di_t2i_t t);
+
 /* SD VAE decoder (config 5's image decode; vae-wgsl.js:99-118 runs it through the same executor):
  * diffusers AutoencoderKL decode = latent / 0.18215 -> post_quant_conv -> Decoder (conv_in 4->512, mid
  * ResNet / single-head attention / ResNet, up blocks 512, 512, 256, 128 with 3 ResNets each and 2x
@@ -253,6 +291,9 @@ DI_API void di_vae_destroy(di_vae_t v);
 /* Diagnostics: copy `bytes` at `off` of activation-ring buffer idx (idx < 0: temporary arena) to host. */
 DI_API int di_vae_debug_copy(di_vae_t v, int idx, size_t off, void* dst, size_t bytes);
 
+/* Config-1 ResNet block, fp32 NCHW in and out (fused-resnet.js:121-208 + the timestep add it omits,
+ * fused-resnet.js:9-12): y = conv2(silu(gn2(conv1(silu(gn1(x))) + Wt.act(temb) + bt))) + x;
+ * act = SiLU when temb_silu (diffusers), identity otherwise.  Names: norm1/conv1/time_emb_proj/norm2/conv2. */
 DI_API int di_resnet_block_create(di_ctx_t ctx, int N, int C, int H, int W, int Tdim, uint64_t seed, float eps,
                                   int temb_silu, di_weight_fn fn, void* user, di_resnet_t* out);
 DI_API int di_resnet_block_io(di_resnet_t r, float** x, float** temb, float** y);

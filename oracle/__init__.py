@@ -55,6 +55,8 @@ _SIGS = {
     "o_transformer_block": [_f, _f, _I, _I, _I, _I, _I, _U64, _I, _f],
     "o_unet_forward": [_f, _f, _f, _I, _I, _I, _I, _U64, _f],
     "o_vae_decode": [_f, _I, _I, _I, _U64, _f],
+    "o_attention_causal": [_f, _f, _f, _f, _I, _I, _I, _I],
+    "o_text_encode": [_i32, _I, _I, _I, _U64, _f],
     "o_num_threads": [],
     "o_set_threads": [_I],
     "o_param_seconds": [],
@@ -127,6 +129,22 @@ def sched_sigmas(n: int) -> np.ndarray:
     out = np.empty(n + 1, np.float32)
     lib().o_sched_sigmas(n, out)
     return out
+
+
+def sched_scale_input(x, sigma: float) -> np.ndarray:
+    """scaleModelInput (scheduler.js:95-101): float(double(x) / sqrt(sigma^2 + 1))."""
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().o_sched_scale_input(x.ravel(), y.ravel(), x.size, sigma)
+    return y
+
+
+def sched_step(x, eps, sig_i: float, sig_next: float) -> np.ndarray:
+    """Euler step (scheduler.js:105-110): float(double(x) + (sig_next - sig_i) * double(eps))."""
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().o_sched_step(x.ravel(), _c(eps).ravel(), y.ravel(), x.size, sig_i, sig_next)
+    return y
 
 
 def noise_latent(B: int, H: int, W: int, seed: int, sigma: float) -> np.ndarray:
@@ -305,6 +323,26 @@ def vae_decode(latent, seed):
     B, _, h, w = latent.shape
     out = np.empty((B, 3, 8 * h, 8 * w), np.float32)
     lib().o_vae_decode(_c(latent).ravel(), B, h, w, seed, out.ravel())
+    return out
+
+
+def attention_causal(q, k, v, layout=0):
+    """Causal attention, head dim 64: query i sees keys 0..i.  layout 0 [B,S,H,64], 1 [B,H,S,64]."""
+    if layout == 0:
+        B, S, H, _ = q.shape
+    else:
+        B, H, S, _ = q.shape
+    o = np.empty_like(_c(q))
+    lib().o_attention_causal(_c(q).ravel(), _c(k).ravel(), _c(v).ravel(), o.ravel(), B, H, S, layout)
+    return o
+
+
+def text_encode(ids, layers, seed):
+    """OpenCLIP ViT-H text encoder on int32 ids [B, S] -> [B, S, 1024] (final LayerNorm applied)."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    B, S = ids.shape
+    out = np.empty((B, S, 1024), np.float32)
+    lib().o_text_encode(ids.ravel(), B, S, layers, seed, out.ravel())
     return out
 
 

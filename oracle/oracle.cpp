@@ -235,7 +235,8 @@ void layer_norm(const float* x, const float* g, const float* b, float* y, int ro
 // both the token-major [B,S,H*64] and the head-major [B,H,S,64] layouts.
 struct AttnStrides { long long sb, ss, sh; };
 void attention_rows(const float* q, const float* k, const float* v, float* o, int B, int H, int Sq, int Skv,
-                    int D, AttnStrides qs, AttnStrides ks, AttnStrides os, const int* rows, int nrows) {
+                    int D, AttnStrides qs, AttnStrides ks, AttnStrides os, const int* rows, int nrows,
+                    bool causal = false) {
   const float scale = 1.0f / std::sqrt((float)D);
   const long long total = (long long)B * H * (rows ? nrows : Sq);
 #pragma omp parallel for schedule(dynamic, 16)
@@ -243,10 +244,11 @@ void attention_rows(const float* q, const float* k, const float* v, float* o, in
     const int per = rows ? nrows : Sq;
     const int bh = (int)(idx / per), qi = rows ? rows[idx % per] : (int)(idx % per);
     const int b = bh / H, h = bh % H;
-    std::vector<float> sc(Skv);
+    const int nk = causal ? std::min(Skv, qi + 1) : Skv;  // causal: keys 0..qi (CLIP text attention)
+    std::vector<float> sc(nk);
     const float* qr = q + b * qs.sb + (long long)qi * qs.ss + h * qs.sh;
     float m = -3.4e38f;
-    for (int j = 0; j < Skv; ++j) {
+    for (int j = 0; j < nk; ++j) {
       const float* kr = k + b * ks.sb + (long long)j * ks.ss + h * ks.sh;
       float d = 0.0f;
 #pragma omp simd reduction(+ : d)
@@ -255,12 +257,12 @@ void attention_rows(const float* q, const float* k, const float* v, float* o, in
       m = std::max(m, sc[j]);
     }
     float sum = 0.0f;
-    for (int j = 0; j < Skv; ++j) { sc[j] = std::exp(sc[j] - m); sum += sc[j]; }
+    for (int j = 0; j < nk; ++j) { sc[j] = std::exp(sc[j] - m); sum += sc[j]; }
     const float inv = 1.0f / sum;
     float* orow = o + b * os.sb + (long long)qi * os.ss + h * os.sh;
     for (int x = 0; x < D; ++x) {
       float acc = 0.0f;
-      for (int j = 0; j < Skv; ++j) acc += sc[j] * inv * v[b * ks.sb + (long long)j * ks.ss + h * ks.sh + x];
+      for (int j = 0; j < nk; ++j) acc += sc[j] * inv * v[b * ks.sb + (long long)j * ks.ss + h * ks.sh + x];
       orow[x] = acc;
     }
   }
@@ -713,6 +715,12 @@ void o_attention(const float* q, const float* k, const float* v, float* o, int B
   else { qs = {(long long)H * Sq * 64, 64, (long long)Sq * 64}; ks = {(long long)H * Skv * 64, 64, (long long)Skv * 64}; }
   attention_rows(q, k, v, o, B, H, Sq, Skv, 64, qs, ks, qs, rows, nrows);
 }
+void o_attention_causal(const float* q, const float* k, const float* v, float* o, int B, int H, int S, int layout) {
+  AttnStrides st;
+  if (layout == 0) st = {(long long)S * H * 64, H * 64, 64};
+  else st = {(long long)H * S * 64, 64, (long long)S * 64};
+  attention_rows(q, k, v, o, B, H, S, S, 64, st, st, st, nullptr, 0, true);
+}
 
 // fused-tembed.js:73-130: y = W2 . silu(W1 . [cos||sin](t f) + b1) + b2, W row-major [out,in].
 void o_tembed(const float* t, int B, const float* W1, const float* b1, const float* W2, const float* b2,
@@ -877,8 +885,45 @@ void o_vae_decode(const float* latent, int B, int h, int w, uint64_t seed, float
   std::memcpy(image, x.d.data(), sizeof(float) * x.size());
 }
 
+// ---- OpenCLIP ViT-H text encoder (SD2.x / SD-Turbo; ONNX Runtime in the reference, text-encoder.js:
+// 69-174).  HF CLIPTextModel: x = token_embedding[ids] + position_embedding; per layer
+// x += out_proj(causal_attn(q/k/v_proj(LN1(x)))), x += fc2(gelu(fc1(LN2(x)))); final LayerNorm.
+// GELU is the erf form of wgsl-ops.js:69 (the ONNX export's Erf op runs through the A&S erf there).
+std::unordered_map<uint64_t, std::unordered_map<std::string, std::vector<float>>> g_text_cache;
+
+void o_text_encode(const int32_t* ids, int B, int S, int layers, uint64_t seed, float* out) {
+  Params P{seed, true, 0, {}, 0, &g_text_cache[seed]};
+  const int D = 1024, F = 4096, V = 49408, H = 16, M = B * S;
+  const float* tok = P.get("text_model.embeddings.token_embedding.weight", (size_t)V * D, 2, 1);
+  const float* pos = P.get("text_model.embeddings.position_embedding.weight", (size_t)77 * D, 2, 1);
+  std::vector<float> x((size_t)M * D);
+  for (int t = 0; t < M; ++t)
+    for (int c = 0; c < D; ++c) x[(size_t)t * D + c] = tok[(size_t)ids[t] * D + c] + pos[(size_t)(t % S) * D + c];
+  for (int l = 0; l < layers; ++l) {
+    const std::string pre = "text_model.encoder.layers." + std::to_string(l);
+    auto n = ln_p(P, pre + ".layer_norm1", x, M, D);
+    auto q = linear_p(P, pre + ".self_attn.q_proj", n, M, D, D, true);
+    auto k = linear_p(P, pre + ".self_attn.k_proj", n, M, D, D, true);
+    auto v = linear_p(P, pre + ".self_attn.v_proj", n, M, D, D, true);
+    std::vector<float> o((size_t)M * D);
+    const AttnStrides st{(long long)S * D, D, 64};
+    attention_rows(q.data(), k.data(), v.data(), o.data(), B, H, S, S, 64, st, st, st, nullptr, 0, true);
+    auto y = linear_p(P, pre + ".self_attn.out_proj", o, M, D, D, true);
+    for (size_t i = 0; i < x.size(); ++i) x[i] += y[i];
+    n = ln_p(P, pre + ".layer_norm2", x, M, D);
+    auto h = linear_p(P, pre + ".mlp.fc1", n, M, D, F, true);
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)h.size(); ++i) h[i] = gelu_erf(h[i]);
+    y = linear_p(P, pre + ".mlp.fc2", h, M, F, D, true);
+    for (size_t i = 0; i < x.size(); ++i) x[i] += y[i];
+  }
+  x = ln_p(P, "text_model.final_layer_norm", x, M, D);
+  std::memcpy(out, x.data(), sizeof(float) * x.size());
+}
+
 double o_param_seconds() { return g_param_seconds; }
 void o_clear_cache() {
+  g_text_cache.clear();
   g_unet_cache.clear();
   g_vae_cache.clear();
 }

@@ -1,0 +1,139 @@
+"""Config 5's remaining stages: causal attention, the GELU linear epilogue, the OpenCLIP ViT-H text
+encoder, the scheduler on the device and the one-step text-to-image pipeline, against the CPU oracle
+on the same seeded weights.  Bars: max|d|/max|ref| <= 1e-2 and cosine >= 0.999; the scheduler
+arithmetic is bit-exact."""
+from __future__ import annotations
+
+import importlib
+
+import numpy as np
+import pytest
+
+from conftest import cosine, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("B,H,S", [(2, 16, 77), (1, 2, 200), (1, 1, 1), (1, 4, 129)])
+def test_causal_attention(ctx, dib, oracle, dtype, B, H, S):
+    import torch
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
+    rng = np.random.default_rng(S)
+    tq, tk, tv = (torch.from_numpy(rng.standard_normal((B, S, H, 64)).astype(np.float32)).to(tdt).cuda()
+                  for _ in range(3))
+    o = torch.empty_like(tq)
+    dt = dib.DI_F16 if dtype == "f16" else dib.DI_BF16
+    ctx.check(dib.lib().di_attention_causal(ctx.h, dt, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), o.data_ptr(),
+                                            B, H, S, 0), "di_attention_causal")
+    torch.cuda.synchronize()
+    ref = oracle.attention_causal(*(t.float().cpu().numpy() for t in (tq, tk, tv)))
+    got = o.float().cpu().numpy()
+    assert rel_err(got, ref) < (1e-2 if dtype == "f16" else 2e-2)
+    # query 0 sees key 0 only
+    assert np.allclose(got[:, 0], tv.float().cpu().numpy()[:, 0], atol=1e-2)
+
+
+def test_causal_needs_positive_size(ctx, dib):
+    import torch
+    t = torch.zeros(1, 8, 1, 64, dtype=torch.float16, device="cuda")
+    assert dib.lib().di_attention_causal(ctx.h, dib.DI_F16, t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(),
+                                         1, 1, 0, 0) != 0
+
+
+@pytest.mark.parametrize("act", [0, 1, 2])
+def test_linear_act(ctx, dib, oracle, act):
+    import torch
+    M, K, N = 300, 256, 192
+    rng = np.random.default_rng(act)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float16)).cuda()
+    w = torch.from_numpy((rng.standard_normal((N, K)) / 16).astype(np.float16)).cuda()
+    b = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).cuda()
+    r = torch.from_numpy(rng.standard_normal((M, N)).astype(np.float16)).cuda()
+    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    ctx.check(dib.lib().di_linear_act(ctx.h, dib.DI_F16, x.data_ptr(), M, K, w.data_ptr(), N, b.data_ptr(),
+                                      r.data_ptr(), act, y.data_ptr()), "di_linear_act")
+    torch.cuda.synchronize()
+    z = (x.float() @ w.float().T + b).cpu().numpy()
+    if act == 1:
+        z = oracle.unary(8, z)  # SiLU
+    elif act == 2:
+        z = oracle.unary(9, z)  # erf GELU, wgsl-ops.js:69
+    ref = z.reshape(M, N) + r.float().cpu().numpy()
+    assert rel_err(y.float().cpu().numpy(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("B,layers", [(2, 2), (1, 24)])
+def test_text_encoder_vs_oracle(ctx, dib, oracle, B, layers):
+    te = importlib.import_module("draw_instant_b200.text_encoder")
+    seed = 4
+    ids = np.random.default_rng(layers).integers(0, te.VOCAB, (B, 77)).astype(np.int32)
+    enc = te.TextEncoder(ctx, B=B, layers=layers, seed=seed)
+    got = enc.forward_host(ids)
+    ref = oracle.text_encode(ids, layers, seed)
+    assert got.shape == (B, 77, 1024) and np.all(np.isfinite(got))
+    assert cosine(got, ref) >= 0.999
+    assert rel_err(got, ref) <= 1e-2
+    # replays are bit-identical; causal: changing the last token leaves earlier positions unchanged
+    assert np.array_equal(enc.forward_host(ids), got)
+    ids2 = ids.copy()
+    ids2[:, -1] = (ids2[:, -1] + 1) % te.VOCAB
+    got2 = enc.forward_host(ids2)
+    assert np.array_equal(got2[:, :-1], got[:, :-1])
+    assert not np.array_equal(got2[:, -1], got[:, -1])
+    assert ctx.fault() == 0
+
+
+def test_text_encoder_rejects_bad_ids(ctx, dib):
+    te = importlib.import_module("draw_instant_b200.text_encoder")
+    enc = te.TextEncoder(ctx, B=1, layers=1, seed=4)
+    ids = np.zeros((1, 77), np.int32)
+    ids[0, 5] = te.VOCAB
+    with pytest.raises(dib.DIError):
+        enc.forward_host(ids)
+    assert ctx.fault() == 0
+
+
+def test_unet_schedule_on_device_bit_exact(ctx, dib, oracle):
+    """scaleModelInput fused into the latent conversion and the Euler step into the output conversion give
+    the reference's float32 results bit for bit (given the same noise prediction)."""
+    unet = importlib.import_module("draw_instant_b200.unet")
+    seed, B, H, W = 3, 1, 8, 8
+    u = unet.UNet(ctx, B=B, H=H, W=W, seed=seed)
+    sig = oracle.sched_sigmas(1)
+    s0 = float(sig[0])
+    lat = oracle.noise_latent(B, H, W, 7, s0)
+    cx = oracle.gen_normal(seed, "context", B * 77 * 1024).reshape(B, 77, 1024)
+    scaled = oracle.sched_scale_input(lat, s0)
+    eps_plain = u.forward_host(scaled, 999.0, cx)
+    nxt = u.set_schedule(1.0 / np.sqrt(s0 * s0 + 1.0), float(sig[1]) - s0)
+    eps = u.forward_host(lat, 999.0, cx)
+    assert np.array_equal(eps, eps_plain)
+    assert np.array_equal(nxt.cpu().numpy(), oracle.sched_step(lat, eps, s0, float(sig[1])))
+    u.set_schedule()  # back to the identity schedule
+    assert np.array_equal(u.forward_host(scaled, 999.0, cx), eps_plain)
+
+
+@pytest.mark.parametrize("B,h", [(2, 8), (9, 8)])
+def test_text_to_image_vs_oracle(ctx, dib, oracle, B, h):
+    """Pipeline parity; B = 9 decodes in VAE chunks of 3 images."""
+    t2i = importlib.import_module("draw_instant_b200.t2i")
+    seed, layers = 4, 2
+    p = t2i.Text2Image(ctx, B=B, h=h, w=h, text_layers=layers, seed=seed)
+    sig = oracle.sched_sigmas(1)
+    assert p.sigma0 == sig[0]
+    ids = np.random.default_rng(1).integers(0, 49408, (B, 77)).astype(np.int32)
+    lat = oracle.noise_latent(B, h, h, 11, float(sig[0]))
+    img = p.forward_host(ids, lat)
+    # the oracle composition: text -> U-Net(scaleModelInput(latent)) -> Euler step -> VAE
+    cx = oracle.text_encode(ids, layers, seed)
+    eps = oracle.unet_forward(oracle.sched_scale_input(lat, float(sig[0])), 999.0,
+                              cx.astype(np.float16).astype(np.float32), seed)
+    x0 = oracle.sched_step(lat, eps, float(sig[0]), float(sig[1]))
+    ref = oracle.vae_decode(x0, seed)
+    assert img.shape == (B, 3, 8 * h, 8 * h) and np.all(np.isfinite(img))
+    assert cosine(img, ref) >= 0.999
+    assert rel_err(img, ref) <= 1e-2
+    assert cosine(p.context.cpu().numpy(), cx) >= 0.999
+    assert cosine(p.eps.cpu().numpy(), eps) >= 0.999
+    assert ctx.fault() == 0
