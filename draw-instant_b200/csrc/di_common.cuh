@@ -23,6 +23,10 @@
 
 namespace di {
 
+// Largest split-K partial-sum buffer (fp32, splits x M x N) a GEMM may use: the size of a plan's
+// shared split-K buffer; the tiling model only picks splits that fit.
+constexpr size_t kSplitKWsBytes = 32u << 20;
+
 // ---------------------------------------------------------------------------------------------
 // Host-side context
 // ---------------------------------------------------------------------------------------------

@@ -811,7 +811,9 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
   }
   if (forced_bn && (!geglu || forced_bn % 128 == 0)) {
     *bn = forced_bn;
-    const int per = (num_k + forced_s - 1) / forced_s;
+    int fs = forced_s;
+    while (fs > 1 && (size_t)M * N * fs * 4 > kSplitKWsBytes) --fs;
+    const int per = (num_k + fs - 1) / fs;
     *splits = (num_k + per - 1) / per;
     *pair = forced_pair && M > BM;
     return;
@@ -843,6 +845,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
         const int per = (num_k + s - 1) / s;
         const int seff = (num_k + per - 1) / per;
         if (seff != s) continue;
+        if (s > 1 && (size_t)M * N * s * 4 > kSplitKWsBytes) break;  // partials must fit the buffer
         const long long units = (long long)mtiles * nt * s;
         const long long rounds = (units + slots - 1) / slots;
         double cost = (double)rounds * (per * kb_cost + 8.0) + 4.0;
@@ -895,6 +898,7 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
   p.n_tiles = p.geglu ? p.N / bn : (p.N + bn - 1) / bn;
   if (p.splits > 1) {
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
+    if (need > kSplitKWsBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
     p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
     if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
     p.staged = (p.N % 4 == 0 && reinterpret_cast<uintptr_t>(p.partial) % 16 == 0) ? 1 : 0;

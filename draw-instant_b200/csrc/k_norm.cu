@@ -408,6 +408,48 @@ __global__ void layer_norm_rows(const Tin* __restrict__ x, const float* __restri
   for (int i = lane; i < D; i += 32) y[(size_t)row * D + i] = from_f<Tout>((to_f<Tin>(xr[i]) - mean) * inv * g[i] + b[i]);
 }
 
+// LayerNorm with the row held in registers: one warp per row, lane l owns the 8-element chunks
+// l, l + 32, ... (NV chunks at most, D <= 256 NV), read once with 16/32-byte loads; the same
+// E[x^2] - mean^2 statistics as layer_norm_rows.  Needs D % 8 == 0 and 16-byte aligned rows.
+template <typename Tin, typename Tout, int NV>
+__global__ void layer_norm_rows_vec(const Tin* __restrict__ x, const float* __restrict__ g,
+                                    const float* __restrict__ b, Tout* __restrict__ y, int rows, int D, float eps) {
+  pdl_begin();
+  const int warps = blockDim.x / 32;
+  const int row = blockIdx.x * warps + threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nch = D / 8;
+  const Tin* xr = x + (size_t)row * D;
+  float v[NV][8];
+  float s = 0.f, q = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int ch = lane + 32 * k;
+    if (ch < nch) {
+      load8<Tin>(xr + ch * 8, v[k]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { s += v[k][i]; q += v[k][i] * v[k][i]; }
+    }
+  }
+  for (int o = 16; o; o >>= 1) { s += __shfl_xor_sync(~0u, s, o); q += __shfl_xor_sync(~0u, q, o); }
+  const float mean = s / (float)D;
+  const float var = fmaxf(q / (float)D - mean * mean, 0.0f);
+  const float inv = 1.0f / sqrtf(var + eps);
+  Tout* yr = y + (size_t)row * D;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int ch = lane + 32 * k;
+    if (ch < nch) {
+      float gg[8], bb[8], o8[8];
+      load8<float>(g + ch * 8, gg);
+      load8<float>(b + ch * 8, bb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = (v[k][i] - mean) * inv * gg[i] + bb[i];
+      store8<Tout>(yr + ch * 8, o8);
+    }
+  }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------------------------
@@ -539,7 +581,18 @@ int group_norm_nchw(Ctx* c, const float* x, const float* g, const float* b, floa
 int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* g, const float* b, void* y, int rows,
                int D, float eps) {
   const int blocks = (rows + 7) / 8;
+  // vector path: rows of whole 8-element chunks, 16-byte aligned base pointers (fp32 gamma / beta too)
+  const bool vec = D % 8 == 0 && D <= 2048 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                    reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+  const int nv = (D + 255) / 256;
+#define LN_VEC(TI, TO, NV)                                                                                     \
+  if (nv <= NV) {                                                                                             \
+    launch_k(layer_norm_rows_vec<TI, TO, NV>, blocks, 256, 0, c->stream, static_cast<const TI*>(x), g, b,     \
+             static_cast<TO*>(y), rows, D, eps);                                                              \
+    return check_launch(c, "layer_norm");                                                                     \
+  }
 #define LN_CASE(TI, TO)                                                                                         \
+  if (vec) { LN_VEC(TI, TO, 1) LN_VEC(TI, TO, 2) LN_VEC(TI, TO, 4) LN_VEC(TI, TO, 8) }                        \
   launch_k(layer_norm_rows<TI, TO>, blocks, 256, 0, c->stream, static_cast<const TI*>(x), g, b, static_cast<TO*>(y), \
                                                          rows, D, eps);                                         \
   return check_launch(c, "layer_norm")
@@ -548,6 +601,7 @@ int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* 
   if (in_dtype == DI_F16 && out_dtype == DI_F16) { LN_CASE(__half, __half); }
   if (in_dtype == DI_BF16 && out_dtype == DI_BF16) { LN_CASE(__nv_bfloat16, __nv_bfloat16); }
 #undef LN_CASE
+#undef LN_VEC
   return set_error(c, DI_EINVAL, "layer_norm: dtype combination");
 }
 

@@ -281,7 +281,7 @@ struct Plan {
   // split-K partial sums of the GEMM kernel (at most ~2 CTAs per SM x 128x128 fp32 tiles); ops run
   // in stream order, so one buffer serves every launch of the plan
   void* splitk = nullptr;
-  static constexpr size_t kSplitKBytes = 32u << 20;
+  static constexpr size_t kSplitKBytes = kSplitKWsBytes;
 
   // temporary bump arena (reset per block; stream order makes reuse safe)
   char* tmp_base = nullptr;
