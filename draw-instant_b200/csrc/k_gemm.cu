@@ -55,6 +55,9 @@ struct GemmParams {
   int splits;      // K splits; > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
+  int* tile_cnt;   // split-K fix-up counters, one per 32 x 32 output chunk (row-chunk * cnt_ld + col-chunk)
+  int cnt_ld, fixup;  // fixup: the last split of a chunk finishes it (no reduce launch)
+  int staged_out;  // the fix-up's output stores may use the staging slab (16-byte aligned output rows)
   int* err;
   unsigned long long* trace;  // diagnostics: kTracePoints %globaltimer stamps per CTA, or null
   // GroupNorm(+SiLU) of the A operand (GnFuse): applied in shared memory by the epilogue warps between
@@ -364,6 +367,139 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     const int row = q * 32 + lane;
     const int half = (warp - 2) / 4;  // which alternate column chunks this warp handles
     uint8_t* stg = sEpi + (warp - 2) * 4096;
+    // Epilogue on one row's 32 columns: bias, per-image row vector, activation, residual (not GEGLU).
+    auto epi = [&](float (&v)[32], int nb, int m) {
+      const int n_out = p.N;
+      const bool full = nb + 32 <= n_out;
+      if (p.bias) {
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < n_out) v[j] += p.bias[nb + j];
+        }
+      }
+      if (p.rowvec) {
+        const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.rowvec_ld + nb;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < n_out) v[j] += rv[j];
+        }
+      }
+      if (p.act == 1) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+      } else if (p.act == 2) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+      }
+      if (p.residual) {
+        if (full && p.vec_ok) {
+          float rr[32];
+          load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += rr[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < n_out) v[j] += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
+        }
+      }
+    };
+    // Stores one warp's 32 x 32 chunk (rows m0 + 32q .., columns nb ..): to the fp32 split-K partials
+    // (to_partial) or to the output, through the staging slab (staged) or row by row.
+    auto store_chunk = [&](const float (&v)[32], int nb, int m0, int m, int sp, bool to_partial, bool staged) {
+      const int n_out = to_partial ? p.N : (p.geglu ? p.N / 2 : p.N);
+      if (staged) {
+        // The warp's 32 x 32 tile goes through a swizzled staging slab (conflict-free writes of one row
+        // per lane), then is read back so that each store instruction writes whole 64/128-byte row
+        // segments of 8 or 4 rows (coalesced), instead of 32 rows 16 bytes at a time.
+        __syncwarp();  // the previous chunk's read-back is done
+        if (to_partial || p.out_f32) {
+          // 32 fp32 per row = 128 B; 16-byte chunk j of row r at j ^ (r & 7)
+          float4* rp = reinterpret_cast<float4*>(stg + lane * 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            rp[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          // 32 x 16-bit per row = 64 B; 16-byte chunk j of row r at j ^ ((r >> 1) & 3)
+          uint4* rp = reinterpret_cast<uint4*>(stg + lane * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float x0 = v[8 * j + 2 * k], x1 = v[8 * j + 2 * k + 1];
+              if (BF16) {
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+                w[k] = *reinterpret_cast<uint32_t*>(&h2);
+              } else {
+                __half2 h2 = __floats2half2_rn(x0, x1);
+                w[k] = *reinterpret_cast<uint32_t*>(&h2);
+              }
+            }
+            rp[j ^ ((lane >> 1) & 3)] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        __syncwarp();
+        const int mrow0 = m0 + q * 32;
+        if (to_partial || p.out_f32) {
+          float* base = to_partial ? p.partial + (size_t)sp * p.M * p.N : static_cast<float*>(p.out);
+          const int ld = to_partial ? p.N : p.ldo;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3), ch = lane & 7;
+            const float4 val = reinterpret_cast<const float4*>(stg + r * 128)[ch ^ (r & 7)];
+            const int mm = mrow0 + r, col = nb + ch * 4;
+            if (mm < p.M && col < n_out) {
+              float* d = base + (size_t)mm * ld + col;
+              if (col + 4 <= n_out) {
+                *reinterpret_cast<float4*>(d) = val;
+              } else {
+                const float t[4] = {val.x, val.y, val.z, val.w};
+                for (int k = 0; k < 4 && col + k < n_out; ++k) d[k] = t[k];
+              }
+            }
+          }
+        } else {
+          uint16_t* base = static_cast<uint16_t*>(p.out);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = i * 8 + (lane >> 2), ch = lane & 3;
+            const uint4 val = reinterpret_cast<const uint4*>(stg + r * 64)[ch ^ ((r >> 1) & 3)];
+            const int mm = mrow0 + r, col = nb + ch * 8;
+            if (mm < p.M && col < n_out) {
+              uint16_t* d = base + (size_t)mm * p.ldo + col;
+              if (col + 8 <= n_out) {
+                *reinterpret_cast<uint4*>(d) = val;
+              } else {
+                const uint32_t t[4] = {val.x, val.y, val.z, val.w};
+                for (int k = 0; k < 8 && col + k < n_out; ++k) d[k] = static_cast<uint16_t>(t[k >> 1] >> (16 * (k & 1)));
+              }
+            }
+          }
+        }
+      } else if (m < p.M) {
+        if (to_partial) {
+          float* dst = p.partial + ((size_t)sp * p.M + m) * p.N + nb;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < p.N) dst[j] = v[j];
+        } else if (p.vec_ok && nb + 32 <= n_out) {
+          store_row32(p.out, (size_t)m * p.ldo + nb, v, p.out_f32, BF16);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < n_out) store_one(p.out, (size_t)m * p.ldo + nb + j, v[j], p.out_f32, BF16);
+        }
+      }
+    };
     int lt = 0, xit = 0;
     for (int u = cta0; u < units; u += cstride, ++lt) {
       int m0, n0, sp, kb0, kb1;
@@ -531,135 +667,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             nb = n0 + c * 32;
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            if (!split && nb < n_out && m < p.M) {
-              const bool full = nb + 32 <= n_out;
-              if (p.bias) {
-                if (full) {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j)
-                    if (nb + j < n_out) v[j] += p.bias[nb + j];
-                }
-              }
-              if (p.rowvec) {
-                const float* rv = p.rowvec + (size_t)(m / p.rowvec_div) * p.rowvec_ld + nb;
-                if (full) {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] += __ldg(rv + j);
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j)
-                    if (nb + j < n_out) v[j] += rv[j];
-                }
-              }
-              if (p.act == 1) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
-              } else if (p.act == 2) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-              }
-              if (p.residual) {
-                if (full && p.vec_ok) {
-                  float rr[32];
-                  load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] += rr[j];
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j)
-                    if (nb + j < n_out) v[j] += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
-                }
-              }
-            }
+            if (!split && nb < n_out && m < p.M) epi(v, nb, m);
           }
         }
         if (!ok || nb >= n_out) continue;  // warp-uniform
-        if (p.staged) {
-          // The warp's 32 x 32 tile goes through a swizzled staging slab (conflict-free writes of one row
-          // per lane), then is read back so that each store instruction writes whole 64/128-byte row
-          // segments of 8 or 4 rows (coalesced), instead of 32 rows 16 bytes at a time.
-          __syncwarp();  // the previous chunk's read-back is done
-          if (split || p.out_f32) {
-            // 32 fp32 per row = 128 B; 16-byte chunk j of row r at j ^ (r & 7)
-            float4* rp = reinterpret_cast<float4*>(stg + lane * 128);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              rp[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
-            // 32 x 16-bit per row = 64 B; 16-byte chunk j of row r at j ^ ((r >> 1) & 3)
-            uint4* rp = reinterpret_cast<uint4*>(stg + lane * 64);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint32_t w[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float x0 = v[8 * j + 2 * k], x1 = v[8 * j + 2 * k + 1];
-                if (BF16) {
-                  __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-                  w[k] = *reinterpret_cast<uint32_t*>(&h2);
-                } else {
-                  __half2 h2 = __floats2half2_rn(x0, x1);
-                  w[k] = *reinterpret_cast<uint32_t*>(&h2);
-                }
-              }
-              rp[j ^ ((lane >> 1) & 3)] = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          }
-          __syncwarp();
-          const int mrow0 = m0 + q * 32;
-          if (split || p.out_f32) {
-            float* base = split ? p.partial + (size_t)sp * p.M * p.N : static_cast<float*>(p.out);
-            const int ld = split ? p.N : p.ldo;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int r = i * 4 + (lane >> 3), ch = lane & 7;
-              const float4 val = reinterpret_cast<const float4*>(stg + r * 128)[ch ^ (r & 7)];
-              const int mm = mrow0 + r, col = nb + ch * 4;
-              if (mm < p.M && col < n_out) {
-                float* d = base + (size_t)mm * ld + col;
-                if (col + 4 <= n_out) {
-                  *reinterpret_cast<float4*>(d) = val;
-                } else {
-                  const float t[4] = {val.x, val.y, val.z, val.w};
-                  for (int k = 0; k < 4 && col + k < n_out; ++k) d[k] = t[k];
-                }
-              }
-            }
-          } else {
-            uint16_t* base = static_cast<uint16_t*>(p.out);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int r = i * 8 + (lane >> 2), ch = lane & 3;
-              const uint4 val = reinterpret_cast<const uint4*>(stg + r * 64)[ch ^ ((r >> 1) & 3)];
-              const int mm = mrow0 + r, col = nb + ch * 8;
-              if (mm < p.M && col < n_out) {
-                uint16_t* d = base + (size_t)mm * p.ldo + col;
-                if (col + 8 <= n_out) {
-                  *reinterpret_cast<uint4*>(d) = val;
-                } else {
-                  const uint32_t t[4] = {val.x, val.y, val.z, val.w};
-                  for (int k = 0; k < 8 && col + k < n_out; ++k) d[k] = static_cast<uint16_t>(t[k >> 1] >> (16 * (k & 1)));
-                }
-              }
-            }
-          }
-        } else if (m < p.M) {
-          if (split) {
-            float* dst = p.partial + ((size_t)sp * p.M + m) * p.N + nb;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (nb + j < p.N) dst[j] = v[j];
-          } else if (p.vec_ok && nb + 32 <= n_out) {
-            store_row32(p.out, (size_t)m * p.ldo + nb, v, p.out_f32, BF16);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (nb + j < n_out) store_one(p.out, (size_t)m * p.ldo + nb + j, v[j], p.out_f32, BF16);
-          }
+        if (!split) {
+          store_chunk(v, nb, m0, m, sp, false, p.staged);
+          continue;
         }
+        store_chunk(v, nb, m0, m, sp, true, p.staged);
+        if (!p.fixup) continue;  // GEGLU partials: the reduce kernel finishes them
+        // Split-K fix-up without a reduce launch: the warp publishes its partial chunk, counts it on the
+        // chunk's counter, and the split that arrives last sums all partials (fixed order z = 0..s-1,
+        // so the result does not depend on arrival order), applies the epilogue and stores the output.
+        // Nobody waits: the other splits just move on.  The last arriver resets the counter to zero.
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          const int id = ((m0 + q * 32) >> 5) * p.cnt_ld + (nb >> 5);
+          last = atomicAdd(p.tile_cnt + id, 1) == p.splits - 1;
+          if (last) p.tile_cnt[id] = 0;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        if (m < p.M) {
+          const size_t slice = (size_t)p.M * p.N;
+          const float* src = p.partial + (size_t)m * p.N + nb;
+          if (nb + 32 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (int z = 0; z < p.splits; ++z) {
+              const float4* q4 = reinterpret_cast<const float4*>(src + z * slice);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t = __ldcg(q4 + j);
+                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float a = 0.f;
+              if (nb + j < p.N)
+                for (int z = 0; z < p.splits; ++z) a += __ldcg(src + z * slice + j);
+              v[j] = a;
+            }
+          }
+          epi(v, nb, m);
+        }
+        store_chunk(v, nb, m0, m, sp, false, p.staged_out);
       }
       tc_fence_before();
       __syncwarp();
@@ -812,7 +870,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
   if (forced_bn && (!geglu || forced_bn % 128 == 0)) {
     *bn = forced_bn;
     int fs = forced_s;
-    while (fs > 1 && (size_t)M * N * fs * 4 > kSplitKWsBytes) --fs;
+    while (fs > 1 && (size_t)M * N * fs * 4 > kSplitKPartialBytes) --fs;
     const int per = (num_k + fs - 1) / fs;
     *splits = (num_k + per - 1) / per;
     *pair = forced_pair && M > BM;
@@ -845,7 +903,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
         const int per = (num_k + s - 1) / s;
         const int seff = (num_k + per - 1) / per;
         if (seff != s) continue;
-        if (s > 1 && (size_t)M * N * s * 4 > kSplitKWsBytes) break;  // partials must fit the buffer
+        if (s > 1 && (size_t)M * N * s * 4 > kSplitKPartialBytes) break;  // partials must fit the buffer
         const long long units = (long long)mtiles * nt * s;
         const long long rounds = (units + slots - 1) / slots;
         double cost = (double)rounds * (per * kb_cost + 8.0) + 4.0;
@@ -864,7 +922,8 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
 int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
   int bn, s, pr;
   choose_tiling(c, M, N, K / 64, geglu, &bn, &s, &pr);
-  return s > 1 ? 2 : 1;
+  const bool fixup = !geglu && (size_t)((M + 31) / 32) * ((N + 31) / 32) <= kSplitKCounters;
+  return (s > 1 && !fixup) ? 2 : 1;
 }
 
 template <bool XF>
@@ -898,12 +957,17 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
   p.n_tiles = p.geglu ? p.N / bn : (p.N + bn - 1) / bn;
   if (p.splits > 1) {
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
-    if (need > kSplitKWsBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
-    p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
+    if (need > kSplitKPartialBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
+    // the workspace is kSplitKWsBytes: partials first, the fix-up counters (zero between launches) at the tail
+    p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, kSplitKWsBytes, 4));
     if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
     p.staged = (p.N % 4 == 0 && reinterpret_cast<uintptr_t>(p.partial) % 16 == 0) ? 1 : 0;
+    p.staged_out = p.vec_ok;
+    p.cnt_ld = (p.N + 31) / 32;
+    p.tile_cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(p.partial) + kSplitKPartialBytes);
+    p.fixup = (!p.geglu && (size_t)((p.M + 31) / 32) * p.cnt_ld <= kSplitKCounters) ? 1 : 0;
     int r = dispatch_variant(c, p, bn, bf16, pair);
-    if (r) return r;
+    if (r || p.fixup) return r;
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
     launch_k(splitk_reduce, blocks, 256, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,

@@ -294,6 +294,8 @@ struct Plan {
       if (k) cudaGraphExecDestroy(k);
     for (auto& e : pev) cudaEventDestroy(e);
     if (stream) { cudaStreamSynchronize(stream); cudaStreamDestroy(stream); }
+    if (side) { cudaStreamSynchronize(side); cudaStreamDestroy(side); }
+    for (auto& e : fork_ev) cudaEventDestroy(e);
     if (ev_in) cudaEventDestroy(ev_in);
     if (ev_out) cudaEventDestroy(ev_out);
     for (void* b : blocks) cudaFree(b);
@@ -393,6 +395,47 @@ struct Plan {
     });
     info.push_back({kind, flops, bytes, kernels});
     launches += kernels;
+  }
+
+  // Side branch: an op whose inputs are ready well before its consumer runs on a second stream, so
+  // the captured graph forks there and joins at the consumer (join(j) before the consumer's launch).
+  // The branch has its own split-K buffer; it may not share a temporary with the main chain.
+  cudaStream_t side = nullptr;
+  void* splitk_side = nullptr;
+  std::vector<cudaEvent_t> fork_ev;  // [2j] fork, [2j + 1] join
+  int record_fork(std::function<int()> f, int kind, double flops, double bytes, int kernels) {
+    if (!side) {
+      if (cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking) != cudaSuccess) {
+        fail(DI_ECUDA, "plan: side stream");
+        return -1;
+      }
+      splitk_side = dalloc(kSplitKBytes);
+      if (splitk_side) cudaMemset(splitk_side, 0, kSplitKBytes);
+    }
+    const int j = (int)fork_ev.size() / 2;
+    fork_ev.resize(fork_ev.size() + 2);
+    cudaEventCreateWithFlags(&fork_ev[2 * j], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&fork_ev[2 * j + 1], cudaEventDisableTiming);
+    Ctx* cc = c;
+    Plan* self = this;
+    ops.push_back([cc, self, j, f = std::move(f)] {
+      cudaEventRecord(self->fork_ev[2 * j], cc->stream);
+      cudaStreamWaitEvent(self->side, self->fork_ev[2 * j], 0);
+      cudaStream_t main_stream = cc->stream;
+      cc->stream = self->side;
+      cc->weights_const = true;
+      const int r = f();
+      cc->weights_const = false;
+      cc->stream = main_stream;
+      cudaEventRecord(self->fork_ev[2 * j + 1], self->side);
+      return r;
+    });
+    info.push_back({kind, flops, bytes, kernels});
+    launches += kernels;
+    return j;
+  }
+  void join(int j) const {
+    if (j >= 0) cudaStreamWaitEvent(c->stream, fork_ev[2 * j + 1], 0);
   }
 
   // Device time of the ops of one kind alone: a graph holding only those launches (same buffers, same
@@ -563,6 +606,7 @@ struct Plan {
     cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
     cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
     splitk = dalloc(kSplitKBytes);
+    if (splitk) cudaMemset(splitk, 0, kSplitKBytes);  // the split-K fix-up counters start at zero
     tmp_cap = tmp_bytes;
     tmp_base = static_cast<char*>(dalloc(tmp_bytes));
     act_bytes += tmp_bytes;
@@ -731,6 +775,26 @@ struct Plan {
   Act resnet(const std::string& pre, const Act& x1, const Act* x2, int Co, float eps = 1e-5f, bool temb = true) {
     tmp_reset();
     const int Ci = x1.C + (x2 ? x2->C : 0);
+    // 1x1 shortcut when the channel count changes: it reads only the block input, so it runs on the side
+    // branch while gn1 -> conv1 -> gn2 run on the main chain; conv2 joins it for the residual add
+    const void* res = x1.p;
+    int fork = -1;
+    if (Ci != Co) {
+      const void* ws = lin_weight(pre + ".conv_shortcut.weight", Co, Ci);
+      const float* bs = vec(pre + ".conv_shortcut.bias", Co, 0, Ci);
+      const int M = x1.N * x1.H * x1.W;
+      void* s = tmp((size_t)M * Co * 2);
+      Ctx* cc = c;
+      Plan* self = this;
+      const void* xa = x1.p;
+      const void* xb = x2 ? x2->p : nullptr;
+      const int K1 = x1.C;
+      fork = record_fork([=] {
+        return gemm_linear(cc, DI_F16, xa, xb ? K1 : Ci, xb, M, Ci, ws, Co, bs, nullptr, 0, s, 0, 0, nullptr, 1,
+                           self->splitk_side);
+      }, 0, 2.0 * M * Co * Ci, 2.0 * ((double)M * Ci + (double)Co * Ci + (double)M * Co), gemm_kernel_count(c, M, Co, Ci, 0));
+      res = s;
+    }
     const GnOp g1 = gn_op(pre + ".norm1", x1, x2, eps, 1);
     // time projection rows appended to the shared GEMV
     if (temb) {
@@ -761,16 +825,9 @@ struct Plan {
     const GnOp g2 = gn_op(pre + ".norm2", h, nullptr, eps, 1);
     const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
     const float* b2 = bias_padded(pre + ".conv2.bias", Co, Co, Co * 9);
-    const void* res = x1.p;
-    if (Ci != Co) {
-      const void* ws = lin_weight(pre + ".conv_shortcut.weight", Co, Ci);
-      const float* bs = vec(pre + ".conv_shortcut.bias", Co, 0, Ci);
-      void* s = tmp((size_t)N * H * W * Co * 2);
-      linear(x1.p, N * H * W, Ci, ws, Co, bs, nullptr, s, x2 ? x2->p : nullptr, x1.C);
-      res = s;
-    }
     Act y = new_act(N, H, W, Co);
     record([=] {
+      self->join(fork);
       const GnFuse f{g2.tab, g2.silu};
       return gemm_conv3x3(cc, DI_F16, g2.x1, g2.C1, g2.x2, g2.C2, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0, Co,
                           splitk, g2.tab ? &f : nullptr);
@@ -826,14 +883,28 @@ struct Plan {
       auto w = host_param(tb + nm, (size_t)C * Cctx, 0, Cctx, C);
       wkv.insert(wkv.end(), w.begin(), w.end());
     }
-    const void* Wkv = upload_f16(wkv);
-    void* kv = tmp((size_t)N * Sk * 2 * C * 2);
-    linear(ctx16, N * Sk, Cctx, Wkv, 2 * C, nullptr, nullptr, kv);
     void* o2 = tmp((size_t)M * C * 2);
-    record([=] {
-      const char* base = static_cast<const char*>(kv);
-      return attention(cc, DI_F16, q2, base, base + (size_t)C * 2, o2, N, heads, HW, Sk, 0, C, 2 * C, 2 * C, C);
-    }, 1, 4.0 * N * heads * HW * (double)Sk * 64, 2.0 * (2.0 * M * C + 2.0 * N * Sk * C));
+    if (batch_ctx_kv) {
+      // K / V rows appended to the plan's single context projection (finish_ctx_kv); this block reads its
+      // columns [off, off + 2C) of the [N*Sk, ctxkv_rows] result
+      const int off = ctxkv_rows;
+      ctxkv_w.insert(ctxkv_w.end(), wkv.begin(), wkv.end());
+      ctxkv_rows += 2 * C;
+      Plan* self = this;
+      record([=] {
+        const __half* base = self->ctxkv + off;
+        const long long ld = self->ctxkv_rows;
+        return attention(cc, DI_F16, q2, base, base + C, o2, N, heads, HW, Sk, 0, C, ld, ld, C);
+      }, 1, 4.0 * N * heads * HW * (double)Sk * 64, 2.0 * (2.0 * M * C + 2.0 * N * Sk * C));
+    } else {
+      const void* Wkv = upload_f16(wkv);
+      void* kv = tmp((size_t)N * Sk * 2 * C * 2);
+      linear(ctx16, N * Sk, Cctx, Wkv, 2 * C, nullptr, nullptr, kv);
+      record([=] {
+        const char* base = static_cast<const char*>(kv);
+        return attention(cc, DI_F16, q2, base, base + (size_t)C * 2, o2, N, heads, HW, Sk, 0, C, 2 * C, 2 * C, C);
+      }, 1, 4.0 * N * heads * HW * (double)Sk * 64, 2.0 * (2.0 * M * C + 2.0 * N * Sk * C));
+    }
     const void* wo2 = lin_weight(tb + ".attn2.to_out.0.weight", C, C);
     const float* bo2 = vec(tb + ".attn2.to_out.0.bias", C, 0, C);
     void* h2 = tmp((size_t)M * C * 2);
@@ -962,6 +1033,33 @@ struct Plan {
     return y;
   }
 
+  // Cross-attention K / V of every transformer from one GEMM over the (step-invariant) context:
+  // [N*Sk, Cctx] x [ctxkv_rows, Cctx]^T, inserted as op `at`, instead of one small GEMM per block.
+  bool batch_ctx_kv = false;
+  std::vector<float> ctxkv_w;
+  int ctxkv_rows = 0;
+  __half* ctxkv = nullptr;
+  void finish_ctx_kv(size_t at, const void* ctx16, int rows, int Cctx) {
+    const void* W = upload_f16(ctxkv_w);
+    ctxkv = static_cast<__half*>(act_alloc(sizeof(__half) * (size_t)rows * ctxkv_rows));
+    Ctx* cc = c;
+    const int N = ctxkv_rows;
+    __half* out = ctxkv;
+    void* sk = splitk;
+    info.insert(info.begin() + at, OpInfo{0, 2.0 * rows * N * Cctx, 2.0 * ((double)rows * Cctx + (double)N * Cctx +
+                                          (double)rows * N), gemm_kernel_count(c, rows, N, Cctx, 0)});
+    launches += gemm_kernel_count(c, rows, N, Cctx, 0);
+    ops.insert(ops.begin() + at, [=] {
+      cc->weights_const = true;
+      const int r = gemm_linear(cc, DI_F16, ctx16, Cctx, nullptr, rows, Cctx, W, N, nullptr, nullptr, 0, out, 0, 0,
+                                nullptr, 1, sk);
+      cc->weights_const = false;
+      return r;
+    });
+    ctxkv_w.clear();
+    ctxkv_w.shrink_to_fit();
+  }
+
   void finish_time_proj(size_t at, const float* temb, int B) {
     const void* W = upload_f16(tproj_w);
     const float* b = upload_f32(tproj_b);
@@ -1070,6 +1168,7 @@ static int build_unet(UNetPlan* u) {
     }, 3, 2.0 * B * 1280 * (320 + 1280), 4.0 * 1280 * (320 + 1280), 2 * ((B + 7) / 8));
   }
   const size_t tproj_at = P.ops.size();
+  P.batch_ctx_kv = true;
 
   // conv_in: 4 (padded to 64) -> 320
   Act h;
@@ -1139,6 +1238,7 @@ static int build_unet(UNetPlan* u) {
     }, 3, 0, (double)B * H * W * (32 + 16 + 32));
   }
   P.finish_time_proj(tproj_at, temb, B);
+  P.finish_ctx_kv(tproj_at, ctx16, B * Sk, 1024);
   cudaDeviceSynchronize();
   return P.err;
 }

@@ -1,0 +1,28 @@
+"""Split-K GEMMs, finished in the kernel by the last split of each 32 x 32 chunk (and, for GEGLU, by the
+reduce kernel): forced tilings in child processes, against torch fp32, with bit-identical repeats (the
+chunk counters return to zero after every launch)."""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+HERE = Path(__file__).resolve().parent
+
+
+@pytest.mark.parametrize("tiling", ["128,4", "256,3,1", "160,2", "128,1"])
+def test_split_k_forced(ctx, tiling):
+    env = dict(os.environ, DI_GEMM_TILING=tiling)
+    r = subprocess.run([sys.executable, str(HERE / "splitk_case.py")], cwd=HERE, env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    assert res.pop("fault") == 0
+    for name, (err, same) in res.items():
+        assert err < 1e-2, (name, err)
+        assert same, name
