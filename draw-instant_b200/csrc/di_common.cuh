@@ -26,10 +26,6 @@ namespace di {
 // Largest split-K partial-sum buffer (fp32, splits x M x N) a GEMM may use: the size of a plan's
 // shared split-K buffer; the tiling model only picks splits that fit.
 constexpr size_t kSplitKWsBytes = 32u << 20;
-// Its last 64 KB hold the in-kernel split-K fix-up counters (one int per 32 x 32 output chunk, zero
-// between launches); the partials use the rest.
-constexpr size_t kSplitKCounters = 16384;
-constexpr size_t kSplitKPartialBytes = kSplitKWsBytes - kSplitKCounters * sizeof(int);
 
 // ---------------------------------------------------------------------------------------------
 // Host-side context

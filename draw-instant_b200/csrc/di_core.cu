@@ -238,7 +238,6 @@ void* workspace(Ctx* c, size_t bytes, int slot) {
     w.ptr = nullptr;
     return nullptr;
   }
-  cudaMemset(w.ptr, 0, want);  // e.g. the split-K fix-up counters start at zero
   w.bytes = want;
   return w.ptr;
 }

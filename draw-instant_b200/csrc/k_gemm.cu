@@ -55,9 +55,6 @@ struct GemmParams {
   int splits;      // K splits; > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
-  int* tile_cnt;   // split-K fix-up counters, one per 32 x 32 output chunk (row-chunk * cnt_ld + col-chunk)
-  int cnt_ld, fixup;  // fixup: the last split of a chunk finishes it (no reduce launch)
-  int staged_out;  // the fix-up's output stores may use the staging slab (16-byte aligned output rows)
   int* err;
   unsigned long long* trace;  // diagnostics: kTracePoints %globaltimer stamps per CTA, or null
   // GroupNorm(+SiLU) of the A operand (GnFuse): applied in shared memory by the epilogue warps between
@@ -675,49 +672,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           store_chunk(v, nb, m0, m, sp, false, p.staged);
           continue;
         }
-        store_chunk(v, nb, m0, m, sp, true, p.staged);
-        if (!p.fixup) continue;  // GEGLU partials: the reduce kernel finishes them
-        // Split-K fix-up without a reduce launch: the warp publishes its partial chunk, counts it on the
-        // chunk's counter, and the split that arrives last sums all partials (fixed order z = 0..s-1,
-        // so the result does not depend on arrival order), applies the epilogue and stores the output.
-        // Nobody waits: the other splits just move on.  The last arriver resets the counter to zero.
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          const int id = ((m0 + q * 32) >> 5) * p.cnt_ld + (nb >> 5);
-          last = atomicAdd(p.tile_cnt + id, 1) == p.splits - 1;
-          if (last) p.tile_cnt[id] = 0;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
-        if (m < p.M) {
-          const size_t slice = (size_t)p.M * p.N;
-          const float* src = p.partial + (size_t)m * p.N + nb;
-          if (nb + 32 <= p.N && (p.N & 3) == 0) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-            for (int z = 0; z < p.splits; ++z) {
-              const float4* q4 = reinterpret_cast<const float4*>(src + z * slice);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 t = __ldcg(q4 + j);
-                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float a = 0.f;
-              if (nb + j < p.N)
-                for (int z = 0; z < p.splits; ++z) a += __ldcg(src + z * slice + j);
-              v[j] = a;
-            }
-          }
-          epi(v, nb, m);
-        }
-        store_chunk(v, nb, m0, m, sp, false, p.staged_out);
+        store_chunk(v, nb, m0, m, sp, true, p.staged);  // fp32 partials: the reduce kernel finishes them
       }
       tc_fence_before();
       __syncwarp();
@@ -870,7 +825,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
   if (forced_bn && (!geglu || forced_bn % 128 == 0)) {
     *bn = forced_bn;
     int fs = forced_s;
-    while (fs > 1 && (size_t)M * N * fs * 4 > kSplitKPartialBytes) --fs;
+    while (fs > 1 && (size_t)M * N * fs * 4 > kSplitKWsBytes) --fs;
     const int per = (num_k + fs - 1) / fs;
     *splits = (num_k + per - 1) / per;
     *pair = forced_pair && M > BM;
@@ -903,7 +858,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
         const int per = (num_k + s - 1) / s;
         const int seff = (num_k + per - 1) / per;
         if (seff != s) continue;
-        if (s > 1 && (size_t)M * N * s * 4 > kSplitKPartialBytes) break;  // partials must fit the buffer
+        if (s > 1 && (size_t)M * N * s * 4 > kSplitKWsBytes) break;  // partials must fit the buffer
         const long long units = (long long)mtiles * nt * s;
         const long long rounds = (units + slots - 1) / slots;
         double cost = (double)rounds * (per * kb_cost + 8.0) + 4.0;
@@ -922,8 +877,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
 int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
   int bn, s, pr;
   choose_tiling(c, M, N, K / 64, geglu, &bn, &s, &pr);
-  const bool fixup = !geglu && (size_t)((M + 31) / 32) * ((N + 31) / 32) <= kSplitKCounters;
-  return (s > 1 && !fixup) ? 2 : 1;
+  return s > 1 ? 2 : 1;
 }
 
 template <bool XF>
@@ -957,17 +911,12 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
   p.n_tiles = p.geglu ? p.N / bn : (p.N + bn - 1) / bn;
   if (p.splits > 1) {
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
-    if (need > kSplitKPartialBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
-    // the workspace is kSplitKWsBytes: partials first, the fix-up counters (zero between launches) at the tail
-    p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, kSplitKWsBytes, 4));
+    if (need > kSplitKWsBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
+    p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
     if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
     p.staged = (p.N % 4 == 0 && reinterpret_cast<uintptr_t>(p.partial) % 16 == 0) ? 1 : 0;
-    p.staged_out = p.vec_ok;
-    p.cnt_ld = (p.N + 31) / 32;
-    p.tile_cnt = reinterpret_cast<int*>(reinterpret_cast<char*>(p.partial) + kSplitKPartialBytes);
-    p.fixup = (!p.geglu && (size_t)((p.M + 31) / 32) * p.cnt_ld <= kSplitKCounters) ? 1 : 0;
     int r = dispatch_variant(c, p, bn, bf16, pair);
-    if (r || p.fixup) return r;
+    if (r) return r;
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
     launch_k(splitk_reduce, blocks, 256, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,

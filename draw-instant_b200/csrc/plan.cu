@@ -410,7 +410,6 @@ struct Plan {
         return -1;
       }
       splitk_side = dalloc(kSplitKBytes);
-      if (splitk_side) cudaMemset(splitk_side, 0, kSplitKBytes);
     }
     const int j = (int)fork_ev.size() / 2;
     fork_ev.resize(fork_ev.size() + 2);
@@ -606,7 +605,6 @@ struct Plan {
     cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
     cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
     splitk = dalloc(kSplitKBytes);
-    if (splitk) cudaMemset(splitk, 0, kSplitKBytes);  // the split-K fix-up counters start at zero
     tmp_cap = tmp_bytes;
     tmp_base = static_cast<char*>(dalloc(tmp_bytes));
     act_bytes += tmp_bytes;
@@ -779,7 +777,17 @@ struct Plan {
     // branch while gn1 -> conv1 -> gn2 run on the main chain; conv2 joins it for the residual add
     const void* res = x1.p;
     int fork = -1;
-    if (Ci != Co) {
+    static const bool fork_ok = [] {  // diagnostics: DI_PLAN_FORK=0 keeps the shortcut on the main chain
+      const char* e = getenv("DI_PLAN_FORK");
+      return !(e && e[0] == '0');
+    }();
+    if (Ci != Co && !fork_ok) {
+      const void* ws = lin_weight(pre + ".conv_shortcut.weight", Co, Ci);
+      const float* bs = vec(pre + ".conv_shortcut.bias", Co, 0, Ci);
+      void* s = tmp((size_t)x1.N * x1.H * x1.W * Co * 2);
+      linear(x1.p, x1.N * x1.H * x1.W, Ci, ws, Co, bs, nullptr, s, x2 ? x2->p : nullptr, x1.C);
+      res = s;
+    } else if (Ci != Co) {
       const void* ws = lin_weight(pre + ".conv_shortcut.weight", Co, Ci);
       const float* bs = vec(pre + ".conv_shortcut.bias", Co, 0, Ci);
       const int M = x1.N * x1.H * x1.W;

@@ -1,6 +1,5 @@
-"""Split-K GEMMs, finished in the kernel by the last split of each 32 x 32 chunk (and, for GEGLU, by the
-reduce kernel): forced tilings in child processes, against torch fp32, with bit-identical repeats (the
-chunk counters return to zero after every launch)."""
+"""GEMMs under forced tilings (K splits finished by the reduce kernel, paired and single CTAs, several
+tile widths) in child processes, against torch fp32, with bit-identical repeats."""
 from __future__ import annotations
 
 import json
