@@ -49,6 +49,10 @@ struct Ctx {
   // Set while a plan enqueues its ops: GEMM weight operands are not written by any kernel still in
   // flight, so they may be read before the programmatic-dependency wait.
   bool weights_const = false;
+  // When set (by a plan, around one GEMM call): the GEMM also accumulates GroupNorm(32) statistics of its
+  // fp16 output into gn_stats[image][group][3] (exact fixed point, see gn_fixed), images of gn_stats_hw rows.
+  long long* gn_stats = nullptr;
+  int gn_stats_hw = 0;
 };
 
 Ctx* ctx_of(di_ctx_t h);
@@ -369,6 +373,19 @@ __device__ __forceinline__ float erf_as(float x) {
                           0.254829592f) * t * __expf(-x * x);
   return x >= 0.0f ? y : -y;
 }
+// GroupNorm statistics in exact fixed point, so that atomic accumulation in any order gives the same bits.
+// For an fp16 value x (exact in fp32): s = x * 2^24 is an integer for every fp16 value; x^2 (22
+// significant bits, exact in fp32) splits into hi = floor(x^2 * 2^8) and lo = (x^2 * 2^8 - hi) * 2^40,
+// both integers.  Per group of up to 2^17 values none of the three sums leaves int64 for any fp16 x.
+// Sum = S / 2^24, sum of squares = HI / 2^8 + LO / 2^48.
+__device__ __forceinline__ void gn_fixed(float x, long long& s, long long& hi, long long& lo) {
+  s = __float2ll_rn(x * 16777216.0f);
+  const float q = x * x * 256.0f;
+  const float h = floorf(q);
+  hi = __float2ll_rn(h);
+  lo = __float2ll_rn((q - h) * 1099511627776.0f);
+}
+
 __device__ __forceinline__ float gelu_erf(float x) { return x * 0.5f * (1.0f + erf_as(x * 0.70710678f)); }
 
 template <typename T> __device__ __forceinline__ float to_f(T v);

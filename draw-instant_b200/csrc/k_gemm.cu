@@ -55,6 +55,8 @@ struct GemmParams {
   int splits;      // K splits; > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
+  long long* gstats;  // GroupNorm(32) statistics of the fp16 output (Ctx::gn_stats), or null
+  int g_cpg, g_hw;    // channels per group (N / 32), output rows per image
   int* err;
   unsigned long long* trace;  // diagnostics: kTracePoints %globaltimer stamps per CTA, or null
   // GroupNorm(+SiLU) of the A operand (GnFuse): applied in shared memory by the epilogue warps between
@@ -155,6 +157,50 @@ __device__ __forceinline__ void store_one(void* dst, size_t off, float v, int is
 // traffic per FLOP.  The leader (rank 0) issues the MMAs; the peer's TMA loads count their bytes on the
 // leader's `full` barrier; MMA commits arrive on `empty` / `tfull` in both CTAs; both CTAs' epilogue
 // warps release the accumulator on the leader's `tempty`.  Units then index 256-row M tiles.
+// GroupNorm(32) statistics of one warp's 32 x 32 output chunk (rows r0 .., lane = row, columns nb ..):
+// the values as stored (rounded to fp16), reduced over the warp per group, three int64 atomics per
+// group touched.  The chunk's rows belong to one image (rows per image are a multiple of 32).
+template <typename P>
+__device__ __forceinline__ void gn_stats_chunk(const float (&v)[32], int nb, int r0, int m, int lane, const P& p) {
+  // a 32-column chunk meets at most 5 groups for cpg >= 8 (the GroupNorm(32) consumers here have C >= 256)
+  const int cpg = p.g_cpg;
+  const int g0 = nb / cpg;
+  const int n = r0 / p.g_hw;
+  long long s[5] = {0, 0, 0, 0, 0}, hi[5] = {0, 0, 0, 0, 0}, lo[5] = {0, 0, 0, 0, 0};
+  if (m < p.M) {
+    int k = 0, next = (g0 + 1) * cpg - nb;  // chunk column where group g0 + k + 1 starts
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j == next) { ++k; next += cpg; }
+      if (nb + j < p.N) {
+        long long a, b, c;
+        gn_fixed(__half2float(__float2half_rn(v[j])), a, b, c);
+#pragma unroll
+        for (int t = 0; t < 5; ++t)
+          if (t == k) { s[t] += a; hi[t] += b; lo[t] += c; }
+      }
+    }
+  }
+  const int ng = min(5, min(31, (min(nb + 31, p.N - 1)) / cpg) - g0 + 1);
+#pragma unroll
+  for (int t = 0; t < 5; ++t) {
+    if (t >= ng) break;
+    long long a = s[t], b = hi[t], c = lo[t];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+      c += __shfl_xor_sync(0xffffffffu, c, o);
+    }
+    if (lane == 0) {
+      unsigned long long* d = reinterpret_cast<unsigned long long*>(p.gstats + ((size_t)n * 32 + g0 + t) * 3);
+      atomicAdd(d, (unsigned long long)a);
+      atomicAdd(d + 1, (unsigned long long)b);
+      atomicAdd(d + 2, (unsigned long long)c);
+    }
+  }
+}
+
 template <int BN, int STAGES, bool BF16, bool PAIR = false, bool XF = false>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmSmem<BN, STAGES, PAIR>;
@@ -667,6 +713,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             if (!split && nb < n_out && m < p.M) epi(v, nb, m);
           }
         }
+        if (p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
         if (!ok || nb >= n_out) continue;  // warp-uniform
         if (!split) {
           store_chunk(v, nb, m0, m, sp, false, p.staged);
@@ -751,6 +798,7 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
                               const float* __restrict__ rowvec, int rowvec_div, int rowvec_ld, const void* residual,
                               int ldr, int res_f32, void* out, int ldo, int out_f32, int geglu, int bf16, int act) {
   pdl_begin();
+
   const size_t slice = (size_t)M * N;
   const int NO = geglu ? N / 2 : N;
   if (!geglu && (N & 3) == 0 && (ldo & 3) == 0 && (!residual || (ldr & 3) == 0)) {
@@ -797,6 +845,64 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int M,
       store_one(out, (size_t)m * ldo + o, a * gelu_erf(g), out_f32, bf16);
     }
   }
+}
+
+// Split-K reduce of an fp16 output whose GroupNorm(32) statistics are wanted: grid (row blocks, images),
+// N / 4 threads per block, thread t owns columns 4t .. 4t + 3 for every row of its block (coalesced float4
+// partial loads), keeps its groups' fixed-point sums (gn_fixed) in registers, folds them through shared
+// memory, and the block adds 32 x 3 int64 per image to the statistics.
+__global__ void splitk_reduce_gn(const float* __restrict__ part, int splits, int M, int N, const float* __restrict__ bias,
+                                 const float* __restrict__ rowvec, int rowvec_div, int rowvec_ld,
+                                 const __half* __restrict__ residual, int ldr, __half* __restrict__ out, int ldo, int act,
+                                 long long* __restrict__ gstats, int cpg, int hw) {
+  pdl_begin();
+  __shared__ long long acc[32 * 3];
+  for (int i = threadIdx.x; i < 96; i += blockDim.x) acc[i] = 0;
+  __syncthreads();
+  const int n = blockIdx.y, rb = gridDim.x;
+  const int rows = (hw + rb - 1) / rb;
+  const int r0 = n * hw + blockIdx.x * rows, r1 = min(n * hw + hw, r0 + rows);
+  const int o = threadIdx.x * 4;
+  const size_t slice = (size_t)M * N;
+  const int ga = o / cpg, gb = (o + 3) / cpg;
+  long long s[2] = {0, 0}, hi[2] = {0, 0}, lo[2] = {0, 0};
+#pragma unroll 4
+  for (int m = r0; m < r1; ++m) {
+    float4 v = reinterpret_cast<const float4*>(part + (size_t)m * N + o)[0];
+    for (int z = 1; z < splits; ++z) {
+      const float4 w = reinterpret_cast<const float4*>(part + z * slice + (size_t)m * N + o)[0];
+      v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+    }
+    float f[4] = {v.x, v.y, v.z, v.w};
+    __half h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (bias) f[j] += bias[o + j];
+      if (rowvec) f[j] += rowvec[(size_t)(m / rowvec_div) * rowvec_ld + o + j];
+      if (act) f[j] = act == 1 ? silu_f(f[j]) : gelu_erf(f[j]);
+      if (residual) f[j] += __half2float(residual[(size_t)m * ldr + o + j]);
+      h[j] = __float2half_rn(f[j]);
+      long long a, b, c;
+      gn_fixed(__half2float(h[j]), a, b, c);
+      const int k = (o + j) / cpg - ga;
+      s[k] += a; hi[k] += b; lo[k] += c;
+    }
+    __half2* dst = reinterpret_cast<__half2*>(out + (size_t)m * ldo + o);
+    dst[0] = __halves2half2(h[0], h[1]);
+    dst[1] = __halves2half2(h[2], h[3]);
+  }
+  unsigned long long* sa = reinterpret_cast<unsigned long long*>(acc);
+  atomicAdd(sa + ga * 3, (unsigned long long)s[0]);
+  atomicAdd(sa + ga * 3 + 1, (unsigned long long)hi[0]);
+  atomicAdd(sa + ga * 3 + 2, (unsigned long long)lo[0]);
+  if (gb != ga) {
+    atomicAdd(sa + gb * 3, (unsigned long long)s[1]);
+    atomicAdd(sa + gb * 3 + 1, (unsigned long long)hi[1]);
+    atomicAdd(sa + gb * 3 + 2, (unsigned long long)lo[1]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 96; i += blockDim.x)
+    if (acc[i]) atomicAdd(reinterpret_cast<unsigned long long*>(gstats + (size_t)n * 96 + i), (unsigned long long)acc[i]);
 }
 
 }  // namespace
@@ -904,6 +1010,15 @@ static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool
 
 int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, void* splitk_ws) {
   p.err = c->d_err;
+  p.gstats = nullptr;
+  if (c->gn_stats) {
+    if (bf16 || p.out_f32 || p.geglu || p.N % 32 || p.N < 256 || p.N > 4096 || c->gn_stats_hw <= 0 || c->gn_stats_hw % 32 ||
+        p.M % c->gn_stats_hw || (p.residual && p.res_f32))
+      return set_error(c, DI_EINVAL, "gemm: GroupNorm statistics need fp16 output, N % 32 == 0, whole images");
+    p.gstats = c->gn_stats;
+    p.g_cpg = p.N / 32;
+    p.g_hw = c->gn_stats_hw;
+  }
   p.staged = (p.vec_ok && splits <= 1) ? 1 : 0;
   p.b_early = c->weights_const ? 1 : 0;
   p.splits = std::max(1, splits);
@@ -917,6 +1032,15 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
     p.staged = (p.N % 4 == 0 && reinterpret_cast<uintptr_t>(p.partial) % 16 == 0) ? 1 : 0;
     int r = dispatch_variant(c, p, bn, bf16, pair);
     if (r) return r;
+    if (p.gstats) {
+      // N / 4 <= 1024 threads; row blocks so that the grid covers the SMs about twice
+      const int imgs = p.M / p.g_hw;
+      const int rb = std::max(1, std::min(p.g_hw, (2 * c->num_sms + imgs - 1) / imgs));
+      launch_k(splitk_reduce_gn, dim3(rb, imgs), p.N / 4, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias,
+               p.rowvec, p.rowvec_div, p.rowvec_ld, static_cast<const __half*>(p.residual), p.ldr,
+               static_cast<__half*>(p.out), p.ldo, p.act, p.gstats, p.g_cpg, p.g_hw);
+      return check_launch(c, "splitk_reduce_gn");
+    }
     const size_t total = (size_t)p.M * (p.geglu ? p.N / 2 : p.N);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
     launch_k(splitk_reduce, blocks, 256, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,

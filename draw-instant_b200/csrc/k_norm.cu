@@ -244,6 +244,53 @@ __global__ void gn_table_kernel(const T* __restrict__ x1, int C1, const T* __res
   cluster_sync();
 }
 
+// GroupNorm(32) from statistics a producer GEMM accumulated in exact fixed point (gn_fixed):
+// stats[n][g] = {S, HI, LO} with sum = S / 2^24 and sum of squares = HI / 2^8 + LO / 2^48.  Grid
+// (blocks, N): each block builds image n's per-channel (scale, shift) table in shared memory (double
+// arithmetic, the variance clamped at 0 as in wgsl-ops.js:390-458), then normalises 8 channels per thread.
+template <typename T>
+__global__ void gn_apply_stats(const T* __restrict__ x, int C, int HW, const long long* __restrict__ stats,
+                               float eps, const float* __restrict__ gamma, const float* __restrict__ beta, int silu,
+                               T* __restrict__ y) {
+  pdl_begin();
+  extern __shared__ float2 gtab[];
+  __shared__ float2 gmr[32];  // per group (mean, rstd)
+  const int n = blockIdx.y, cpg = C / 32;
+  if (threadIdx.x < 32) {
+    const long long* st = stats + ((size_t)n * 32 + threadIdx.x) * 3;
+    const double cnt = (double)cpg * (double)HW;
+    const double sum = (double)st[0] * 0x1p-24;
+    const double sq = (double)st[1] * 0x1p-8 + (double)st[2] * 0x1p-48;
+    const double mean = sum / cnt;
+    const double var = fmax(sq / cnt - mean * mean, 0.0);
+    gmr[threadIdx.x] = make_float2((float)mean, (float)(1.0 / sqrt(var + (double)eps)));
+  }
+  __syncthreads();
+  for (int cc = threadIdx.x; cc < C; cc += blockDim.x) {
+    const float2 mr = gmr[cc / cpg];
+    const float sc = mr.y * gamma[cc];
+    gtab[cc] = make_float2(sc, beta[cc] - mr.x * sc);
+  }
+  __syncthreads();
+  const int V = C / 8;
+  const size_t per_img = (size_t)HW * V;
+  const T* xi = x + (size_t)n * HW * C;
+  T* yi = y + (size_t)n * HW * C;
+  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < per_img; e += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(e % V) * 8;
+    const size_t off = (e / V) * C + c;
+    float f[8];
+    load8<T>(xi + off, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float2 t = gtab[c + j];
+      const float z = fmaf(f[j], t.x, t.y);
+      f[j] = silu ? silu_f(z) : z;
+    }
+    store8<T>(yi + off, f);
+  }
+}
+
 // Normalise with a precomputed (scale, shift) table (gn_table_nhwc): one 8-channel vector per thread,
 // y = silu?(x * scale + shift); table rows are read through L1 (they are tiny and shared by all pixels).
 template <typename Tin, typename Tout>
@@ -576,6 +623,17 @@ int group_norm_nchw(Ctx* c, const float* x, const float* g, const float* b, floa
   const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)8 * c->num_sms);
   launch_k(gn_nchw_apply, blocks, 256, 0, c->stream, x, C, G, HW, chunks, partial, g, b, eps, silu, clamp, total, y);
   return check_launch(c, "group_norm_nchw");
+}
+
+// GroupNorm(32)(+SiLU) of x [N, HW, C] (fp16) from producer statistics (Ctx::gn_stats): one pass.
+int gn_apply_with_stats(Ctx* c, const void* x, int C, int N, int HW, const long long* stats, float eps,
+                        const float* gamma, const float* beta, int silu, void* y) {
+  if (C % 32 || C % 8 || N <= 0 || HW <= 0) return set_error(c, DI_EINVAL, "gn_apply_with_stats: shape");
+  const size_t per_img = (size_t)HW * (C / 8);
+  const int bx = (int)std::max<size_t>(1, std::min<size_t>((per_img + 255) / 256, (size_t)(8 * c->num_sms + N - 1) / N));
+  launch_k(gn_apply_stats<__half>, dim3(bx, N), 256, sizeof(float2) * C, c->stream, static_cast<const __half*>(x), C,
+           HW, stats, eps, gamma, beta, silu, static_cast<__half*>(y));
+  return check_launch(c, "gn_apply_stats");
 }
 
 int layer_norm(Ctx* c, int in_dtype, int out_dtype, const void* x, const float* g, const float* b, void* y, int rows,

@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <deque>
 #include <functional>
 #include <string>
 #include <thread>
@@ -42,6 +43,8 @@ int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1,
                     int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
                     void* partial_ws);
 size_t gn_nhwc_ws_bytes(int N, int HW, int G);
+int gn_apply_with_stats(Ctx* c, const void* x, int C, int N, int HW, const long long* stats, float eps,
+                        const float* gamma, const float* beta, int silu, void* y);
 int gn_table_nhwc(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G, float eps,
                   const float* gamma, const float* beta, float2* table);
 int gn_nhwc_via_table(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
@@ -254,9 +257,16 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restric
 
 typedef int (*WeightFn)(const char* name, size_t n, float* dst, void* user);
 
+// GroupNorm statistics of a GEMM-produced activation: `ptr` is set at build time when a GroupNorm
+// consumer asks for them; the producer's recorded op reads it when it runs (null: no statistics).
+struct GnStatSlot {
+  long long* ptr = nullptr;
+};
+
 struct Act {
   void* p = nullptr;
   int N = 0, H = 0, W = 0, C = 0;
+  GnStatSlot* st = nullptr;  // set when a GEMM epilogue can produce this tensor's GroupNorm(32) statistics
   size_t bytes() const { return (size_t)N * H * W * C * 2; }
 };
 
@@ -395,6 +405,39 @@ struct Plan {
     });
     info.push_back({kind, flops, bytes, kernels});
     launches += kernels;
+  }
+
+  // GroupNorm statistics arena (GnStatSlot): N x 32 groups x 3 int64 per requested tensor, zeroed at the
+  // start of every forward (run_ops).
+  std::deque<GnStatSlot> stat_slots;
+  long long* stats_base = nullptr;
+  size_t stats_cap = 0, stats_off = 0;  // in int64 units
+  GnStatSlot* new_stat_slot() {
+    stat_slots.emplace_back();
+    return &stat_slots.back();
+  }
+  long long* stats_alloc(int N) {
+    const size_t need = (size_t)N * 32 * 3;
+    if (!stats_base) {
+      stats_cap = need * 160;
+      stats_base = static_cast<long long*>(dalloc(stats_cap * sizeof(long long)));
+      if (!stats_base) return nullptr;
+    }
+    if (stats_off + need > stats_cap) {
+      fail(DI_ENOMEM, "plan: GroupNorm statistics arena exhausted");
+      return nullptr;
+    }
+    long long* r = stats_base + stats_off;
+    stats_off += need;
+    return r;
+  }
+  // GEMM call with the GroupNorm statistics of its output when a consumer asked for them
+  static int with_stats(Ctx* cc, const GnStatSlot* st, int hw, const std::function<int()>& f) {
+    cc->gn_stats = st ? st->ptr : nullptr;
+    cc->gn_stats_hw = hw;
+    const int r = f();
+    cc->gn_stats = nullptr;
+    return r;
   }
 
   // Side branch: an op whose inputs are ready well before its consumer runs on a second stream, so
@@ -542,6 +585,7 @@ struct Plan {
   }
 
   int run_ops() {
+    if (stats_off) cudaMemsetAsync(stats_base, 0, stats_off * sizeof(long long), c->stream);
     for (auto& f : ops) {
       int r = f();
       if (r) return r;
@@ -656,12 +700,18 @@ struct Plan {
     const void* w = conv_weight(pre + ".weight", Co, Ci, Ci, Co);
     const float* b = bias_padded(pre + ".bias", Co, Co, Ci * 9);
     Act y = new_act(x.N, x.H / stride, x.W / stride, Co);
+    y.st = new_stat_slot();
     Ctx* cc = c;
     const Act xx = x;
     const void* p2 = x2 ? x2->p : nullptr;
     const int C2 = x2 ? x2->C : 0;
-    record([=] { return gemm_conv3x3(cc, DI_F16, xx.p, xx.C, p2, C2, xx.N, xx.H, xx.W, stride, w, Co, b, nullptr,
-                                     nullptr, 0, y.p, 0, Co, splitk); },
+    void* sk = splitk;
+    record([=] {
+      return with_stats(cc, y.st, y.H * y.W, [&] {
+        return gemm_conv3x3(cc, DI_F16, xx.p, xx.C, p2, C2, xx.N, xx.H, xx.W, stride, w, Co, b, nullptr, nullptr, 0,
+                            y.p, 0, Co, sk);
+      });
+    },
            0, 2.0 * y.N * y.H * y.W * Co * 9 * Ci, (double)x.bytes() + 18.0 * Co * Ci + (double)y.bytes(), gemm_kernel_count(c, y.N * y.H * y.W, Co, 9 * Ci, 0));
     return y;
   }
@@ -710,8 +760,30 @@ struct Plan {
     const char* e = getenv("DI_GN_MODE");
     return (e && e[0] >= '0' && e[0] <= '2') ? e[0] - '0' : 1;
   }();
+  // DI_GN_STATS=1: GroupNorm statistics from the producing GEMM's epilogue (exact fixed-point atomics)
+  // instead of a statistics kernel.  Off by default: measured slower on B200 at batch 1 (208 vs 233
+  // steps/s) and at batch 64 (177 vs 183 images/s); the epilogue and split-K reduce work it adds
+  // outweighs the launch it removes.
+  bool use_stats = [] {
+    const char* e = getenv("DI_GN_STATS");
+    return e && e[0] == '1';
+  }();
   GnOp gn_op(const std::string& pre, const Act& x1, const Act* x2, float eps, int silu) {
     const int C = x1.C + (x2 ? x2->C : 0);
+    if (use_stats && gn_mode == 1 && !x2 && x1.st && C % 32 == 0 && C >= 256 && (x1.H * x1.W) % 32 == 0) {
+      // statistics from the producer GEMM's epilogue: one normalising pass, no statistics kernel
+      if (!x1.st->ptr) x1.st->ptr = stats_alloc(x1.N);
+      const int HW = x1.H * x1.W;
+      const float* g = vec(pre + ".weight", C, 1, 1);
+      const float* b = vec(pre + ".bias", C, 2, 1);
+      void* y = tmp((size_t)x1.N * HW * C * 2);
+      Ctx* cc = c;
+      const Act a = x1;
+      const long long* st = x1.st->ptr;
+      record([=] { return gn_apply_with_stats(cc, a.p, C, a.N, HW, st, eps, g, b, silu, y); }, 2, 0,
+             2.0 * x1.N * HW * C * 2, 1);
+      return GnOp{y, C, nullptr, 0, nullptr, 0};
+    }
     if (gn_mode == 2) return GnOp{x1.p, x1.C, x2 ? x2->p : nullptr, x2 ? x2->C : 0, gn_tab(pre, x1, x2, eps), silu};
     // mode 0 also for large tensors: its statistics pass spreads each image over up to 128 CTAs, the
     // table path over one 16-CTA cluster (latency-optimal for the U-Net's small maps only)
@@ -753,12 +825,16 @@ struct Plan {
     return upload_f16(host_param(name, (size_t)N * K, 0, K, N));
   }
   void linear(const void* X, int M, int K, const void* W, int N, const float* b, const void* R, void* Y,
-              const void* X2 = nullptr, int K1 = 0, const float2* gtab = nullptr, int gsilu = 0, int ghw = 0) {
+              const void* X2 = nullptr, int K1 = 0, const float2* gtab = nullptr, int gsilu = 0, int ghw = 0,
+              const GnStatSlot* st = nullptr, int st_hw = 0) {
     Ctx* cc = c;
+    void* sk = splitk;
     record([=] {
       const GnFuse f{gtab, gsilu};
-      return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1, splitk,
-                         gtab ? &f : nullptr, ghw);
+      return with_stats(cc, st, st_hw, [&] {
+        return gemm_linear(cc, DI_F16, X, X2 ? K1 : K, X2, M, K, W, N, b, R, 0, Y, 0, 0, nullptr, 1, sk,
+                           gtab ? &f : nullptr, ghw);
+      });
     },
            0, 2.0 * M * N * K, 2.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1)), gemm_kernel_count(c, M, N, K, 0));
   }
@@ -820,25 +896,32 @@ struct Plan {
     Act h;
     h.N = x1.N; h.H = x1.H; h.W = x1.W; h.C = Co;
     h.p = tmp(h.bytes());
+    h.st = new_stat_slot();
     Ctx* cc = c;
     const int N = x1.N, H = x1.H, W = x1.W;
     Plan* self = this;
+    void* sk = splitk;
     record([=] {
       const GnFuse f{g1.tab, g1.silu};
-      return gemm_conv3x3(cc, DI_F16, g1.x1, g1.C1, g1.x2, g1.C2, N, H, W, 1, w1, Co, b1,
-                          temb ? self->temb_all + toff : nullptr, nullptr, 0, h.p, 0, self->tproj_ld, splitk,
-                          g1.tab ? &f : nullptr);
+      return with_stats(cc, h.st, H * W, [&] {
+        return gemm_conv3x3(cc, DI_F16, g1.x1, g1.C1, g1.x2, g1.C2, N, H, W, 1, w1, Co, b1,
+                            temb ? self->temb_all + toff : nullptr, nullptr, 0, h.p, 0, self->tproj_ld, sk,
+                            g1.tab ? &f : nullptr);
+      });
     },
            0, 2.0 * N * H * W * Co * 9 * Ci, 2.0 * ((double)N * H * W * (Ci + Co) + 9.0 * Co * Ci), gemm_kernel_count(c, N * H * W, Co, 9 * Ci, 0));
     const GnOp g2 = gn_op(pre + ".norm2", h, nullptr, eps, 1);
     const void* w2 = conv_weight(pre + ".conv2.weight", Co, Co, Co, Co);
     const float* b2 = bias_padded(pre + ".conv2.bias", Co, Co, Co * 9);
     Act y = new_act(N, H, W, Co);
+    y.st = new_stat_slot();
     record([=] {
       self->join(fork);
       const GnFuse f{g2.tab, g2.silu};
-      return gemm_conv3x3(cc, DI_F16, g2.x1, g2.C1, g2.x2, g2.C2, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0, Co,
-                          splitk, g2.tab ? &f : nullptr);
+      return with_stats(cc, y.st, H * W, [&] {
+        return gemm_conv3x3(cc, DI_F16, g2.x1, g2.C1, g2.x2, g2.C2, N, H, W, 1, w2, Co, b2, nullptr, res, 0, y.p, 0,
+                            Co, sk, g2.tab ? &f : nullptr);
+      });
     },
            0, 2.0 * N * H * W * Co * 9 * Co, 2.0 * ((double)N * H * W * 3 * Co + 9.0 * Co * Co), gemm_kernel_count(c, N * H * W, Co, 9 * Co, 0));
     return y;
@@ -949,7 +1032,8 @@ struct Plan {
     const void* wpo = lin_weight(pre + ".proj_out.weight", C, C);
     const float* bpo = vec(pre + ".proj_out.bias", C, 0, C);
     Act y = new_act(N, x.H, x.W, C);
-    linear(h3, M, C, wpo, C, bpo, x.p, y.p);
+    y.st = new_stat_slot();
+    linear(h3, M, C, wpo, C, bpo, x.p, y.p, nullptr, 0, nullptr, 0, 0, y.st, HW);
     return y;
   }
 
@@ -1184,10 +1268,15 @@ static int build_unet(UNetPlan* u) {
     const void* w = P.conv_weight("conv_in.weight", 320, 4, 64, 320);
     const float* b = P.bias_padded("conv_in.bias", 320, 320, 36);
     h = P.new_act(B, H, W, 320);
+    h.st = P.new_stat_slot();
     const Act x = lat;
     const Act y = h;
-    P.record([=] { return gemm_conv3x3(cc, DI_F16, x.p, 64, nullptr, 0, B, H, W, 1, w, 320, b, nullptr, nullptr, 0,
-                                       y.p, 0, 320, sk); },
+    P.record([=] {
+      return Plan::with_stats(cc, y.st, H * W, [&] {
+        return gemm_conv3x3(cc, DI_F16, x.p, 64, nullptr, 0, B, H, W, 1, w, 320, b, nullptr, nullptr, 0, y.p, 0, 320,
+                            sk);
+      });
+    },
              0, 2.0 * B * H * W * 320 * 9 * 4, (double)B * H * W * (128 + 640), gemm_kernel_count(cc, B * H * W, 320, 9 * 64, 0));
   }
   const int ch[4] = {320, 640, 1280, 1280};
@@ -1404,9 +1493,14 @@ static int build_vae(VaePlan* v) {
     const void* wt = P.conv_weight("decoder.conv_in.weight", 512, 4, 64, 512);
     const float* bt = P.bias_padded("decoder.conv_in.bias", 512, 512, 4 * 9);
     x = P.new_act(B, h, w, 512);
+    x.st = P.new_stat_slot();
     const Act zz = z, xx = x;
-    P.record([=] { return gemm_conv3x3(cc, DI_F16, zz.p, 64, nullptr, 0, B, h, w, 1, wt, 512, bt, nullptr, nullptr, 0,
-                                       xx.p, 0, 512, sk); },
+    P.record([=] {
+      return Plan::with_stats(cc, xx.st, h * w, [&] {
+        return gemm_conv3x3(cc, DI_F16, zz.p, 64, nullptr, 0, B, h, w, 1, wt, 512, bt, nullptr, nullptr, 0, xx.p, 0,
+                            512, sk);
+      });
+    },
              0, 2.0 * B * h * w * 512 * 9 * 4, (double)B * h * w * (128 + 1024), gemm_kernel_count(cc, B * h * w, 512, 9 * 64, 0));
   }
   // mid block
