@@ -948,6 +948,10 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
     const char* e = getenv("DI_GEMM_PAIR");
     return (e && e[0] == '0') ? 0 : 1;
   }();
+  static const double split_cost = [] {  // the reduce launch, in K-block units; DI_SPLIT_COST overrides
+    const char* e = getenv("DI_SPLIT_COST");
+    return e ? atof(e) : 9.0;
+  }();
   double best = 1e30;
   *bn = 128;
   *splits = 1;
@@ -968,7 +972,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
         const long long units = (long long)mtiles * nt * s;
         const long long rounds = (units + slots - 1) / slots;
         double cost = (double)rounds * (per * kb_cost + 8.0) + 4.0;
-        if (s > 1) cost += 9.0 + (double)M * N * s * 8.0 / 6.4e12 / 290e-9;
+        if (s > 1) cost += split_cost + (double)M * N * s * 8.0 / 6.4e12 / 290e-9;
         if (cost < best - 1e-9 || (cost < best + 1e-9 && bc > *bn)) {
           best = cost;
           *bn = bc;
