@@ -84,6 +84,7 @@ SIGNATURES = {
     "di_tembed": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _I, _P]),
     "di_synth_uniform": (None, [ctypes.c_uint64, ctypes.c_char_p, _SZ, _F, _P]),
     "di_synth_normal": (None, [ctypes.c_uint64, ctypes.c_char_p, _SZ, _F, _F, _P]),
+    "di_euler_sigmas": (_I, [_I, _P, _P]),
     "di_unet_create": (_I, [_P, _I, _I, _I, _I, ctypes.c_uint64, _P, _P, ctypes.POINTER(_P)]),
     "di_unet_io": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)]),
     "di_unet_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),

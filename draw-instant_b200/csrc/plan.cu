@@ -1690,6 +1690,11 @@ extern "C" {
 DI_API void di_synth_uniform(uint64_t seed, const char* name, size_t n, float bound, float* out) {
   synth_uniform(seed, name, n, bound, out);
 }
+DI_API int di_euler_sigmas(int n, float* sigmas, float* timesteps) {
+  if (n <= 0 || !sigmas || !timesteps) return DI_EINVAL;
+  euler_sigmas(n, sigmas, timesteps);
+  return DI_OK;
+}
 DI_API void di_synth_normal(uint64_t seed, const char* name, size_t n, float mean, float stdv, float* out) {
   synth_normal(seed, name, n, mean, stdv, out);
 }

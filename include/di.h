@@ -221,6 +221,9 @@ typedef int (*di_weight_fn)(const char* name, size_t n, float* dst, void* user);
  * normal = Box-Muller (double) on (u_2j, u_2j+1).  Host-only; no GPU needed. */
 DI_API void di_synth_uniform(uint64_t seed, const char* name, size_t n, float bound, float* out);
 DI_API void di_synth_normal(uint64_t seed, const char* name, size_t n, float mean, float stdv, float* out);
+/* The Euler-discrete schedule the one-step pipeline uses (scheduler.js:27-89: scaled-linear betas,
+ * trailing timesteps, sigmas rounded to float, last sigma 0): sigmas[n + 1], timesteps[n].  Host-only. */
+DI_API int di_euler_sigmas(int n, float* sigmas, float* timesteps);
 
 /* SD-Turbo (SD2.1) U-Net, fp16 weights / activations, fp32 accumulation: replaces unetForwardWGSL
  * (unet-wgsl.js:145-195) and the Executor.run walk it drives (wgsl-executor.js:1248-1466).

@@ -50,3 +50,17 @@ def test_scale_and_step_bit_exact(sch, oracle):
         z = np.empty_like(x)
         oracle.lib().o_sched_step(x, e, z, x.size, float(s.sigmas[i]), float(s.sigmas[i + 1]))
         np.testing.assert_array_equal(s.step(x, e, i), z)
+
+
+@pytest.mark.parametrize("n", [1, 2, 4, 7, 50])
+def test_libdi_euler_sigmas_match_host_scheduler(dib, oracle, n):
+    """The C++ schedule the text-to-image pipeline bakes into the U-Net plan (host-only entry point,
+    no GPU) equals the Python mirror and the oracle bit for bit."""
+    import ctypes
+    sig = np.empty(n + 1, np.float32)
+    ts = np.empty(n, np.float32)
+    assert dib.lib().di_euler_sigmas(n, sig.ctypes.data_as(ctypes.c_void_p), ts.ctypes.data_as(ctypes.c_void_p)) == 0
+    sched = importlib.import_module("draw_instant_b200.scheduler")
+    s = sched.make_euler_scheduler(n)
+    assert np.array_equal(sig, s.sigmas) and np.array_equal(ts, s.timesteps)
+    assert np.array_equal(sig, oracle.sched_sigmas(n)) and np.array_equal(ts, oracle.sched_timesteps(n))
