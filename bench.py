@@ -225,35 +225,63 @@ def vae_result(ctx, pk, src):
     return out
 
 
-def t2i_result(ctx, pk, src, B=64, reps=3):
-    """Config 5: batched one-step text-to-image (text encoder -> U-Net B=64 -> VAE), images/s on one GPU,
-    with each stage's device time and its tensor-pipe fraction."""
+def t2i_result(ctx, pk, src, R, rank, world, B=64, reps=3):
+    """Config 5: batched one-step text-to-image (text encoder -> U-Net -> VAE) with the global batch of 64
+    sharded across the ranks (strong scaling); every iteration ends with the NCCL all-gather of the decoded
+    images (the path's one exchange).  images/s = 64 / (max over ranks of the per-iteration time).  At
+    N = 1 also each stage's device time and tensor-pipe fraction.  Every rank reaches every collective:
+    a local failure is agreed on first, then all ranks skip the measurement together."""
     import torch
+    import torch.distributed as dist
     t2i = importlib.import_module("draw_instant_b200.t2i")
+    _, Bl = R.shard(B, rank, world)
+    err, p = None, None
     t0 = time.perf_counter()
-    p = t2i.Text2Image(ctx, B=B, h=64, w=64, text_layers=24, seed=4)
+    try:
+        p = t2i.Text2Image(ctx, B=Bl, h=64, w=64, text_layers=24, seed=4)
+        g = torch.Generator(device="cuda").manual_seed(4 + rank)
+        p.ids.copy_(torch.randint(0, 49408, (Bl, 77), device="cuda", generator=g, dtype=torch.int32))
+        p.latent.copy_(torch.randn(Bl, 4, 64, 64, device="cuda", generator=g) * p.sigma0)
+        for _ in range(2):
+            p.forward()
+        torch.cuda.synchronize()
+    except Exception as e:  # reported, never fatal
+        err = str(e)
     build_s = time.perf_counter() - t0
-    g = torch.Generator(device="cuda").manual_seed(4)
-    p.ids.copy_(torch.randint(0, 49408, (B, 77), device="cuda", generator=g, dtype=torch.int32))
-    p.latent.copy_(torch.randn(B, 4, 64, 64, device="cuda", generator=g) * p.sigma0)
-    for _ in range(2):
-        p.forward()
-    torch.cuda.synchronize()
+    if world > 1:
+        flag = torch.tensor([0.0 if err is None else 1.0], device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        if flag.item() > 0 and err is None:
+            err = "another rank failed"
+    if err is not None:
+        return {"error": err}
+    if B % world:
+        return {"error": "global batch not divisible by the ranks"}
     stream = torch.cuda.current_stream()
-    ms = time_events(lambda: p.forward(), reps, stream)
-    stage_ms = [time_events(lambda k=k: p.forward(k), reps, stream) for k in range(3)]
+    R.barrier()
+    torch.cuda.synchronize()
+
+    def step():
+        p.forward()
+        R.gather(p.image)
+
+    ms = R.max_over_ranks(time_events(step, reps, stream), "cuda")
     fl = p.flops()
-    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
-    stages = {}
-    for i, n in enumerate(["text", "unet", "vae"]):
-        tf = fl[n] / (stage_ms[i] / 1e3) / 1e12
-        stages[n] = {"ms": stage_ms[i], "tflops": tf, "frac": tf / peak}
-    total = sum(fl.values())
-    out = {"batch": B, "ms": ms, "images_per_s": B / (ms / 1e3), "tflops": total / (ms / 1e3) / 1e12,
-           "gflop": total / 1e9, "stages": stages, "launches": p.launches, "build_s": build_s,
-           "finite": bool(torch.isfinite(p.image).all().item()),
-           "peak_source": f"{src} bf16_tflops_sustained (a step of a second or more)",
+    total = sum(fl.values()) * world
+    out = {"global_batch": B, "batch_per_gpu": Bl, "n_gpus": world, "ms": ms, "images_per_s": B / (ms / 1e3),
+           "tflops": total / (ms / 1e3) / 1e12, "gflop": total / 1e9, "launches_per_gpu": p.launches,
+           "build_s": build_s, "scaling": "strong", "finite": bool(torch.isfinite(p.image).all().item()),
+           "exchange": "NCCL all-gather of the decoded images every iteration" if world > 1 else None,
            "data": "random token ids U[0,49408) x 77, latents N(0,1) x sigma0, seeded random-init weights"}
+    if world == 1:
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        stages = {}
+        for k, n in enumerate(["text", "unet", "vae"]):
+            sm = time_events(lambda k=k: p.forward(k), reps, stream)
+            tf = fl[n] / (sm / 1e3) / 1e12
+            stages[n] = {"ms": sm, "tflops": tf, "frac": tf / peak}
+        out["stages"] = stages
+        out["peak_source"] = f"{src} bf16_tflops_sustained (a step of a second or more)"
     del p
     torch.cuda.empty_cache()
     return out
@@ -440,16 +468,13 @@ def main():
             "timing": "the step's GEMM/conv launches replayed alone as one graph, CUDA events, 20 replays",
             "share_of_step": gemm_ms / ms_step,
             "time_by_kind_ms": {names[k]: v for k, v in kind_ms.items()}}
+        line["t2i_config5"] = t2i_result(ctx, pk, src, R, rank, world)
         if rank == 0 and world == 1:
             line["blocks"] = block_results(dib, ctx, pk, src)
             try:
                 line["blocks"]["vae_decode_512"] = vae_result(ctx, pk, src)
             except Exception as e:  # a reported extra; never fail the bench line on it
                 line["blocks"]["vae_decode_512"] = {"error": str(e)}
-            try:
-                line["blocks"]["t2i_config5"] = t2i_result(ctx, pk, src)
-            except Exception as e:  # a reported extra; never fail the bench line on it
-                line["blocks"]["t2i_config5"] = {"error": str(e)}
             try:
                 v, sample, cores = cpu_baseline(unet_mod)
                 line["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": cores, "kind": "port",
