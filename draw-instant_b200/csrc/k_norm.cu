@@ -1,6 +1,6 @@
 // k_norm.cu — GroupNorm / InstanceNorm / LayerNorm (+SiLU) for sm_100a.
 //
-// Bandwidth-bound: each kernel is judged by achieved HBM GB/s.  The reference runs one 256-thread
+// Bandwidth-bound: each kernel is measured by achieved HBM GB/s.  The reference runs one 256-thread
 // workgroup per (n, group) with a shared-memory tree (wgsl-ops.js:390-458, fused-groupnorm.js:145-227),
 // i.e. 32 workgroups for a whole feature map.  Here statistics are split over many CTAs (per-chunk
 // partial sum / sum-of-squares written to a small scratch buffer, reduced in a fixed order so results

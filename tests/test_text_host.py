@@ -18,7 +18,7 @@ def test_sd_pad_ids(dib):
     assert np.all(out[1] == np.arange(77)) and np.all(out[0, 4:] == 0)
 
 
-def test_text_flops_matches_survey(dib):
+def test_text_flops_per_batch_of_64(dib):
     te = importlib.import_module("draw_instant_b200.text_encoder")
     # about 3.0 TFLOP per batch of 64 prompts (24 layers, width 1024, MLP 4096)
     assert abs(te.text_flops(64) / 1e12 - 2.98) < 0.05
