@@ -715,6 +715,9 @@ for _op in ("Sigmoid", "Sqrt", "Erf", "Abs", "Neg", "Sin", "Cos"):
 METADATA_OPS = {"Reshape", "Shape", "Unsqueeze", "Squeeze", "Gather", "Slice", "Concat", "Constant",
                 "ConstantOfShape", "Cast", "Expand", "Equal", "Where", "Identity", "Transpose"}
 BINARY_SHAPE_AWARE = {"Add", "Sub", "Mul", "Div"}
+# ops with a host path for 1-element host constants; every other device op gets them promoted (the
+# reference keeps such scalars unpromoted for all ops, so e.g. a MatMul on one would fail there)
+HOST_SCALAR_OPS = BINARY_SHAPE_AWARE | {"Pow", "Sigmoid", "Sqrt", "Erf", "Abs", "Neg"}
 
 
 def plan_execution(graph) -> dict:
@@ -868,7 +871,8 @@ class Executor:
                         fixed.append(t)
                     elif keep_int and t.cpu_data is not None and np.asarray(t.cpu_data).dtype in (np.int64, np.int32):
                         fixed.append(t)
-                    elif t.cpu_data is not None and np.asarray(t.cpu_data).size == 1:
+                    elif t.cpu_data is not None and np.asarray(t.cpu_data).size == 1 and \
+                            node["op_type"] in HOST_SCALAR_OPS:
                         fixed.append(t)  # scalar host constants feed the Pow / shape fast paths
                     else:
                         fixed.append(ctx.promote(t))

@@ -142,3 +142,26 @@ def test_unsupported_op_and_missing_tensor(E, backend, dib):
     ex = E.Executor(backend, graph, E.WeightCache(backend, {}))
     with pytest.raises(dib.DIError, match="tensor not found"):
         ex.run({"x": np.zeros(4, np.float32)})
+
+
+def test_timestep_expand_lowering_stays_on_host(E, backend):
+    """torch.onnx lowers `timesteps.expand(sample.shape[0])` to Shape -> Gather -> Unsqueeze ->
+    ConstantOfShape(int64) -> Mul -> Equal -> Where -> Expand; all of it must stay host metadata
+    (wgsl-executor.js:249-287, 542-573), and the float timestep then promotes into a device op."""
+    from executor_cases import _n, _t
+    one = _t("one", np.array([1]), "int64")
+    T = {"i0": _t("i0", np.array(0), "int64"), "neg1": _t("neg1", np.array([-1]), "int64"),
+         "w": _t("w", np.ones((1, 3), np.float32))}
+    nodes = [_n("Shape", ["sample"], ["s"]), _n("Gather", ["s", "i0"], ["b"], axis=0),
+             _n("Unsqueeze", ["b"], ["bu"], axes=[0]),
+             _n("ConstantOfShape", ["bu"], ["c"], value=one),
+             _n("Mul", ["c", "neg1"], ["m"]), _n("Equal", ["bu", "m"], ["e"]),
+             _n("Where", ["e", "c", "bu"], ["shape"]), _n("Expand", ["t", "shape"], ["te"]),
+             _n("Cast", ["te"], ["tf"], to=1), _n("Unsqueeze", ["tf"], ["tf2"], axes=[1]),
+             _n("MatMul", ["tf2", "w"], ["y"])]
+    graph = {"nodes": nodes, "inputs": [{"name": "sample"}, {"name": "t"}], "outputs": [{"name": "y"}]}
+    ex = E.Executor(backend, graph, E.WeightCache(backend, T))
+    t = E.Tensor(None, [1], "int64", np.array([999], np.int64), True)
+    out = ex.run({"sample": np.zeros((1, 4, 8, 8), np.float32), "t": t})
+    y = backend.read(out["y"].buf, 12)
+    assert out["y"].dims == [1, 3] and np.allclose(y, 999.0)
