@@ -53,6 +53,9 @@ struct Ctx {
   // fp16 output into gn_stats[image][group][3] (exact fixed point, see gn_fixed), images of gn_stats_hw rows.
   long long* gn_stats = nullptr;
   int gn_stats_hw = 0;
+  // Grid-barrier word pair {arrivals, generation} of the single-launch GroupNorm (gn_nhwc_grid) when it is
+  // called through the public entry point; zeroed at allocation, left at {0, g} by every completed launch.
+  unsigned* gn_bar = nullptr;
 };
 
 Ctx* ctx_of(di_ctx_t h);
@@ -109,7 +112,7 @@ inline cudaError_t launch_k_cluster(void (*kern)(KArgs...), dim3 grid, dim3 bloc
 // device error codes (OR-ed into Ctx::d_err)
 enum : int {
   DEVERR_WAIT_TMA = 1, DEVERR_WAIT_MMA = 2, DEVERR_WAIT_EPI = 4, DEVERR_WAIT_SOFTMAX = 8,
-  DEVERR_BOUNDS = 16,
+  DEVERR_BOUNDS = 16, DEVERR_GRID_BARRIER = 32,
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -192,6 +195,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       return false;
     }
   }
+}
+
+// ---- untiled bulk copy global -> this CTA's shared memory (no multicast) ----
+// Both addresses 16-byte aligned, bytes a multiple of 16; completion is counted on `bar`'s tx bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // ---- TMA (tiled tensor loads into this CTA's shared memory; never multicast) ----

@@ -119,6 +119,7 @@ void di_destroy(di_ctx_t ctx) {
   cudaSetDevice(ctx->c.device);
   cudaStreamSynchronize(ctx->c.stream);
   if (ctx->c.d_err) cudaFree(ctx->c.d_err);
+  if (ctx->c.gn_bar) cudaFree(ctx->c.gn_bar);
   for (auto& w : ctx->c.ws)
     if (w.ptr) cudaFree(w.ptr);
   if (ctx->c.own_stream) cudaStreamDestroy(ctx->c.stream);

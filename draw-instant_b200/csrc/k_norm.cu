@@ -10,6 +10,7 @@
 // Numerics follow the reference: mean = sum/n, var = sumsq/n - mean^2 clamped at 0,
 // y = (x - mean) * (1/sqrt(var + eps)) * gamma + beta, optional SiLU x/(1+exp(-x)).
 #include <algorithm>
+#include <cstdlib>
 
 #include "di_common.cuh"
 
@@ -321,6 +322,157 @@ __global__ void gn_apply_table(const Tin* __restrict__ x1, int C1, const Tin* __
   }
 }
 
+// Single-launch GroupNorm(+SiLU) of concat(x1, x2) for maps that fit in the shared memory of at most one
+// CTA per SM.  Grid (cpi, N): CTA (k, n) owns pixels [k * per, min(HW, (k + 1) * per)) of image n.
+//   1. one bulk copy per input brings the CTA's slice (contiguous in NHWC) into shared memory;
+//   2. per-channel sums and sums of squares (fp32, one 8-channel vector per thread) fold to per-group
+//      sums, written to partial[n][k][g];
+//   3. a grid barrier (every CTA is resident: the grid is at most one CTA per SM), then every CTA folds
+//      its image's cpi partials in a fixed order (deterministic, identical in every CTA) to mean / rstd;
+//   4. the slice is normalised from shared memory and written once.
+// Global traffic is the minimum, one read and one write of the map, in one launch instead of the
+// statistics + normalise pair.  The barrier is a {arrivals, generation} word pair: the last CTA to arrive
+// resets the arrivals and bumps the generation; the others wait for the bump, bounded by kWaitTimeoutNs
+// (then DEVERR_GRID_BARRIER is recorded and the kernel still finishes).  The next kernel is released
+// (pdl_trigger) at once: a dependent grid launches only after every CTA of this one has executed the
+// trigger, i.e. once the whole grid is resident, so its CTAs can never hold an SM this grid still needs.
+constexpr int kGridSub = 8;  // fixed partition of the partial fold (deterministic order)
+
+template <typename T>
+__global__ void __launch_bounds__(512) gn_nhwc_grid(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2, int HW, int per,
+                             int G, float eps, const float* __restrict__ gamma, const float* __restrict__ beta,
+                             int silu, T* __restrict__ y, float2* __restrict__ partial, unsigned* bar, int* err) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ float s_fold[2 * kGridSub * 128];
+  __shared__ float s_mean[128], s_rstd[128];
+  const int C = C1 + C2, V = blockDim.x, R = blockDim.y;
+  const int n = blockIdx.y, k = blockIdx.x, cpi = gridDim.x;
+  const int v = threadIdx.x, r = threadIdx.y, tid = r * V + v, nthr = V * R;
+  const int p0 = k * per, cnt = max(0, min(HW, p0 + per) - p0);
+  uint8_t* s1 = gsm;                                   // [cnt][C1]
+  uint8_t* s2 = gsm + (size_t)per * C1 * sizeof(T);    // [cnt][C2]
+  float* ssum = reinterpret_cast<float*>(gsm + (size_t)per * C * sizeof(T));  // [R][C]
+  float* ssq = ssum + R * C;                                                  // [R][C]
+  if (tid == 0) {
+    mbar_init(&mbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // x1 / x2 are written by the previous kernel
+  if (tid == 0) {
+    const uint32_t b1 = (uint32_t)((size_t)cnt * C1 * sizeof(T)), b2 = (uint32_t)((size_t)cnt * C2 * sizeof(T));
+    mbar_arrive_expect_tx(&mbar, b1 + b2);
+    if (b1) bulk_load(s1, x1 + ((size_t)n * HW + p0) * C1, b1, &mbar);
+    if (b2) bulk_load(s2, x2 + ((size_t)n * HW + p0) * C2, b2, &mbar);
+  }
+  mbar_wait(&mbar, 0, err, DEVERR_WAIT_EPI);
+  const int c = v * 8;
+  const uint8_t* src = c < C1 ? s1 + (size_t)c * sizeof(T) : s2 + (size_t)(c - C1) * sizeof(T);
+  const size_t row_bytes = (c < C1 ? C1 : C2) * sizeof(T);
+  {
+    float s[8], q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { s[j] = 0.f; q[j] = 0.f; }
+    for (int p = r; p < cnt; p += R) {
+      float f[8];
+      load8<T>(reinterpret_cast<const T*>(src + p * row_bytes), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { s[j] += f[j]; q[j] += f[j] * f[j]; }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { ssum[r * C + c + j] = s[j]; ssq[r * C + c + j] = q[j]; }
+  }
+  __syncthreads();
+  for (int cc = tid; cc < C; cc += nthr) {
+    float s = 0.f, q = 0.f;
+    for (int rr = 0; rr < R; ++rr) { s += ssum[rr * C + cc]; q += ssq[rr * C + cc]; }
+    ssum[cc] = s;
+    ssq[cc] = q;
+  }
+  __syncthreads();
+  const int cpg = C / G;
+  for (int g = tid; g < G; g += nthr) {
+    float s = 0.f, q = 0.f;
+    for (int cc = g * cpg; cc < (g + 1) * cpg; ++cc) { s += ssum[cc]; q += ssq[cc]; }
+    partial[((size_t)n * cpi + k) * G + g] = make_float2(s, q);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned total = gridDim.x * gridDim.y;
+    const unsigned gen = ld_acquire_gpu(bar + 1);  // cannot move before every CTA of this launch arrives
+    __threadfence();                               // this CTA's partials before its arrival
+    const unsigned old = atomicAdd(bar, 1u);
+    if (old == total - 1) {
+      atomicExch(bar, 0u);  // arrivals reset for the next launch, before anyone is released
+      __threadfence();
+      atomicAdd(bar + 1, 1u);
+    } else {
+      const unsigned long long t0 = globaltimer();
+      while (ld_acquire_gpu(bar + 1) == gen) {
+        if (globaltimer() - t0 > kWaitTimeoutNs) {
+          atomicOr(err, DEVERR_GRID_BARRIER);
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  // fold the image's cpi partials: (group g, subset u) sums partials u, u + kGridSub, ... in order, then
+  // the kGridSub subset sums are added in order (the same arithmetic in every CTA of the image)
+  for (int idx = tid; idx < G * kGridSub; idx += nthr) {
+    const int g = idx % G, u = idx / G;
+    float s = 0.f, q = 0.f;
+    const float2* pp = partial + (size_t)n * cpi * G + g;
+    int kk = u;
+    for (; kk + 7 * kGridSub < cpi; kk += 8 * kGridSub) {  // eight loads in flight, added in order
+      float2 t[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[i] = __ldcg(pp + (size_t)(kk + i * kGridSub) * G);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { s += t[i].x; q += t[i].y; }
+    }
+    for (; kk < cpi; kk += kGridSub) {
+      const float2 t = __ldcg(pp + (size_t)kk * G);
+      s += t.x;
+      q += t.y;
+    }
+    s_fold[2 * (u * G + g)] = s;
+    s_fold[2 * (u * G + g) + 1] = q;
+  }
+  __syncthreads();
+  for (int g = tid; g < G; g += nthr) {
+    float s = 0.f, q = 0.f;
+    for (int u = 0; u < kGridSub; ++u) { s += s_fold[2 * (u * G + g)]; q += s_fold[2 * (u * G + g) + 1]; }
+    const float cntf = (float)cpg * (float)HW;
+    const float mean = s / cntf;
+    const float var = fmaxf(q / cntf - mean * mean, 0.0f);
+    s_mean[g] = mean;
+    s_rstd[g] = 1.0f / sqrtf(var + eps);
+  }
+  __syncthreads();
+  float sc[8], sh[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int g = (c + j) / cpg;
+    sc[j] = s_rstd[g] * __ldg(gamma + c + j);
+    sh[j] = __ldg(beta + c + j) - s_mean[g] * sc[j];
+  }
+  T* yo = y + ((size_t)n * HW + p0) * C + c;
+  for (int p = r; p < cnt; p += R) {
+    float f[8];
+    load8<T>(reinterpret_cast<const T*>(src + p * row_bytes), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a = fmaf(f[j], sc[j], sh[j]);
+      f[j] = silu ? __fdividef(a, 1.0f + __expf(-a)) : a;
+    }
+    store8<T>(yo + (size_t)p * C, f);
+  }
+}
+
 // Normalise pass.  Block = V threads (one 8-channel vector each) x R pixel rows, so every thread keeps
 // the same 8 channels for the whole grid and applies them as one FMA per element with per-thread
 // scale / shift (gamma * rstd, beta - mean * gamma * rstd); two pixels per thread per round.
@@ -604,6 +756,111 @@ int gn_nhwc_via_table(Ctx* c, int dtype, const void* x1, int C1, const void* x2,
   return check_launch(c, "gn_apply_table");
 }
 
+// ---- single-launch GroupNorm (gn_nhwc_grid) ----
+// Largest per-CTA slice of the map kept in shared memory; larger maps use the two-launch paths.
+constexpr size_t kGridSliceMax = 160u << 10;
+
+// Geometry of gn_nhwc_grid: cpi CTAs per image (cpi * N <= SMs, so the whole grid is resident at once),
+// `per` pixels each (at least 4 where the map allows), a V x R thread block.  False when the map does not
+// fit (slice beyond kGridSliceMax, too many images for one CTA each, channel count unsupported).
+bool gn_grid_geometry(int num_sms, int N, int HW, int C, int G, int* cpi, int* per, int* R, size_t* smem) {
+  if (N <= 0 || HW <= 0 || C % 8 || G <= 0 || G > 128 || C % G) return false;
+  const int V = C / 8;
+  if (V > 512) return false;
+  int k = std::min(num_sms / N, (HW + 3) / 4);
+  if (k < 1) return false;
+  const int pp = (HW + k - 1) / k;
+  k = (HW + pp - 1) / pp;  // no empty CTAs
+  const size_t slice = (size_t)pp * C * 2;
+  if (slice > kGridSliceMax) return false;
+  const int r = std::max(1, (256 + V - 1) / V);
+  *cpi = k;
+  *per = pp;
+  *R = r;
+  *smem = slice + sizeof(float) * 2 * (size_t)r * C;
+  return true;
+}
+
+// DI_GN_GRID=1 turns the single-launch path on (read once per process).  Off by default: inside the
+// U-Net step on B200 it measured slower than the statistics-table + normalise pair (225.5 vs 232.7
+// steps/s at batch 1).  The grid barrier across ~148 SMs (fence, same-address atomics, polling) and the
+// fold of every CTA's partials cost about as much as the kernel boundary they replace, and the
+// statistics pass gains little from more CTAs on maps of a few MB.
+bool gn_grid_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("DI_GN_GRID");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+size_t gn_grid_ws_bytes(Ctx* c, int N, int HW, int C, int G) {
+  int cpi, per, R;
+  size_t smem;
+  if (!gn_grid_geometry(c->num_sms, N, HW, C, G, &cpi, &per, &R, &smem)) return 0;
+  return sizeof(float2) * (size_t)N * cpi * G;
+}
+
+// GroupNorm(+SiLU) of concat(x1, x2) (16-bit in and out) in one launch.  Returns 1 when the map does not
+// fit this path or a pointer is not 16-byte aligned (nothing launched; the caller takes a two-launch
+// path), 0 when launched, a negative DI_E* code on error.  `partial` holds gn_grid_ws_bytes bytes; `bar`
+// is a zero-initialised {arrivals, generation} pair not used by any concurrently running launch.
+// Whether gn_nhwc_grid takes this shape on this device: geometry accepted and at least one CTA per SM
+// resident for every CTA of the grid (the barrier needs the whole grid at once).
+bool gn_grid_usable(Ctx* c, int dtype, int N, int HW, int C1, int C2, int G) {
+  const int C = C1 + C2;
+  int cpi, per, R;
+  size_t smem;
+  if (!gn_grid_enabled() || (dtype != DI_F16 && dtype != DI_BF16) || C1 % 8 || C2 % 8 ||
+      !gn_grid_geometry(c->num_sms, N, HW, C, G, &cpi, &per, &R, &smem))
+    return false;
+  static unsigned attr_done = 0;  // per-device bit
+  if (!(attr_done & (1u << (c->device & 31)))) {
+    // R * C <= 4096 for every geometry gn_grid_geometry accepts (R = ceil(256 / V), C = 8 V, V <= 512)
+    const int maxdyn = (int)(kGridSliceMax + sizeof(float) * 2 * 4096);
+    if (cudaFuncSetAttribute(gn_nhwc_grid<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxdyn) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(gn_nhwc_grid<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, maxdyn) !=
+            cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    attr_done |= 1u << (c->device & 31);
+  }
+  int occ = 0;
+  const cudaError_t e =
+      dtype == DI_BF16 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gn_nhwc_grid<__nv_bfloat16>, (C / 8) * R, smem)
+                       : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gn_nhwc_grid<__half>, (C / 8) * R, smem);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return occ >= 1 && (long long)cpi * N <= (long long)occ * c->num_sms;
+}
+
+int gn_nhwc_grid_launch(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                        float eps, const float* gamma, const float* beta, int silu, void* y, float2* partial,
+                        unsigned* bar) {
+  const int C = C1 + C2;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al(x1) || (C2 && !al(x2)) || !al(y) || !partial || !bar) return 1;
+  if (!gn_grid_usable(c, dtype, N, HW, C1, C2, G)) return 1;
+  int cpi, per, R;
+  size_t smem;
+  gn_grid_geometry(c->num_sms, N, HW, C, G, &cpi, &per, &R, &smem);
+  const dim3 grid(cpi, N), block(C / 8, R);
+  if (dtype == DI_BF16)
+    launch_k(gn_nhwc_grid<__nv_bfloat16>, grid, block, smem, c->stream, static_cast<const __nv_bfloat16*>(x1), C1,
+             static_cast<const __nv_bfloat16*>(x2), C2, HW, per, G, eps, gamma, beta, silu,
+             static_cast<__nv_bfloat16*>(y), partial, bar, c->d_err);
+  else
+    launch_k(gn_nhwc_grid<__half>, grid, block, smem, c->stream, static_cast<const __half*>(x1), C1,
+             static_cast<const __half*>(x2), C2, HW, per, G, eps, gamma, beta, silu, static_cast<__half*>(y),
+             partial, bar, c->d_err);
+  const int rc = check_launch(c, "gn_nhwc_grid");
+  return rc ? rc : 0;
+}
+
 size_t gn_nhwc_ws_bytes(int N, int HW, int G) {
   int chunks, cl;
   gn_geometry(HW, &chunks, &cl);
@@ -673,7 +930,26 @@ int di_group_norm_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void
                        float eps, const float* gamma, const float* beta, int fuse_silu, void* y) {
   Ctx* c = ctx_of(h);
   if (!c) return DI_EINVAL;
-  return group_norm_nhwc(c, dtype, dtype, x1, C1, x2, x2 ? C2 : 0, N, HW, G, eps, gamma, beta, fuse_silu, y, nullptr);
+  if (!x2) C2 = 0;
+  // With DI_GN_GRID=1, maps small enough for one CTA per SM take the single-launch kernel (16-bit data).
+  const size_t ws = (dtype == DI_F16 || dtype == DI_BF16) && gn_grid_enabled() ? gn_grid_ws_bytes(c, N, HW, C1 + C2, G)
+                                                                             : 0;
+  if (ws) {
+    if (!c->gn_bar) {
+      if (cudaMalloc(&c->gn_bar, 2 * sizeof(unsigned)) != cudaSuccess) {
+        cudaGetLastError();
+        c->gn_bar = nullptr;
+        return set_error(c, DI_ENOMEM, "group_norm_nhwc: barrier word");
+      }
+      cudaMemset(c->gn_bar, 0, 2 * sizeof(unsigned));
+    }
+    float2* part = static_cast<float2*>(workspace(c, ws, 0));
+    if (!part) return set_error(c, DI_ENOMEM, "group_norm_nhwc: workspace");
+    const int r = gn_nhwc_grid_launch(c, dtype, x1, C1, x2, C2, N, HW, G, eps, gamma, beta, fuse_silu, y, part,
+                                      c->gn_bar);
+    if (r <= 0) return r;  // launched (0) or failed; 1: not applicable, two-launch path below
+  }
+  return group_norm_nhwc(c, dtype, dtype, x1, C1, x2, C2, N, HW, G, eps, gamma, beta, fuse_silu, y, nullptr);
 }
 
 int di_gn_table_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,

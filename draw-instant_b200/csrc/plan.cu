@@ -43,6 +43,11 @@ int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1,
                     int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
                     void* partial_ws);
 size_t gn_nhwc_ws_bytes(int N, int HW, int G);
+bool gn_grid_usable(Ctx* c, int dtype, int N, int HW, int C1, int C2, int G);
+size_t gn_grid_ws_bytes(Ctx* c, int N, int HW, int C, int G);
+int gn_nhwc_grid_launch(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                        float eps, const float* gamma, const float* beta, int silu, void* y, float2* partial,
+                        unsigned* bar);
 int gn_apply_with_stats(Ctx* c, const void* x, int C, int N, int HW, const long long* stats, float eps,
                         const float* gamma, const float* beta, int silu, void* y);
 int gn_table_nhwc(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G, float eps,
@@ -415,6 +420,20 @@ struct Plan {
   GnStatSlot* new_stat_slot() {
     stat_slots.emplace_back();
     return &stat_slots.back();
+  }
+  // A zeroed {arrivals, generation} barrier pair for one single-launch GroupNorm site (gn_nhwc_grid).
+  // Each site has its own pair, so launches on the plan's side stream could never share one.
+  unsigned* gn_bars = nullptr;
+  int gn_bar_used = 0, gn_bar_cap = 0;
+  unsigned* gn_bar_alloc() {
+    if (gn_bar_used == gn_bar_cap) {
+      gn_bar_cap = 256;
+      gn_bar_used = 0;
+      gn_bars = static_cast<unsigned*>(dalloc(sizeof(unsigned) * 2 * gn_bar_cap));
+      if (!gn_bars) return nullptr;
+      cudaMemset(gn_bars, 0, sizeof(unsigned) * 2 * gn_bar_cap);
+    }
+    return gn_bars ? gn_bars + 2 * gn_bar_used++ : nullptr;
   }
   long long* stats_alloc(int N) {
     const size_t need = (size_t)N * 32 * 3;
@@ -793,6 +812,20 @@ struct Plan {
     const float* g = vec(pre + ".weight", C, 1, 1);
     const float* b = vec(pre + ".bias", C, 2, 1);
     void* y = tmp((size_t)x1.N * HW * C * 2);
+    if (gn_grid_usable(c, DI_F16, x1.N, HW, x1.C, x2 ? x2->C : 0, 32)) {
+      // one launch: statistics, grid barrier and normalise (gn_nhwc_grid; opt-in, DI_GN_GRID=1)
+      float2* part = static_cast<float2*>(tmp(gn_grid_ws_bytes(c, x1.N, HW, C, 32)));
+      unsigned* bar = gn_bar_alloc();
+      Ctx* cc = c;
+      const Act a = x1;
+      const void* p2 = x2 ? x2->p : nullptr;
+      const int C2 = x2 ? x2->C : 0;
+      record([=] {
+        const int r = gn_nhwc_grid_launch(cc, DI_F16, a.p, a.C, p2, C2, a.N, HW, 32, eps, g, b, silu, y, part, bar);
+        return r == 1 ? set_error(cc, DI_EUNSUPPORTED, "gn_nhwc_grid: shape or alignment no longer accepted") : r;
+      }, 2, 0, 2.0 * x1.N * HW * C * 2, 1);
+      return GnOp{y, C, nullptr, 0, nullptr, 0};
+    }
     float2* tab = static_cast<float2*>(tmp(sizeof(float2) * (size_t)x1.N * C));
     Ctx* cc = c;
     const Act a = x1;

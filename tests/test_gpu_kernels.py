@@ -158,7 +158,9 @@ def test_attention(ctx, dib, oracle, B, H, Sq, Skv, layout, dtype):
 
 @pytest.mark.parametrize("N,HW,C1,C2,G,silu", [(1, 4096, 320, 0, 32, 1), (2, 256, 1280, 1280, 32, 1),
                                                (1, 64, 640, 320, 32, 0), (1, 1024, 1920, 0, 32, 1),
-                                               (1, 262144, 128, 0, 32, 1), (2, 65536, 256, 256, 32, 1)])
+                                               (1, 262144, 128, 0, 32, 1), (2, 65536, 256, 256, 32, 1),
+                                               (1, 1000, 640, 0, 32, 1), (3, 4096, 320, 320, 32, 0),
+                                               (16, 64, 1280, 0, 32, 1)])
 def test_group_norm_nhwc(ctx, dib, oracle, N, HW, C1, C2, G, silu):
     import torch
     rng = np.random.default_rng(HW + C1)
@@ -177,6 +179,13 @@ def test_group_norm_nhwc(ctx, dib, oracle, N, HW, C1, C2, G, silu):
     ref = oracle.group_norm(xn, g, b, N, C, HW, G, 1e-5, silu=bool(silu))
     ref = np.transpose(ref, (0, 2, 1))
     assert rel_err(_np(Y), ref) < TOL
+    # a second call (the single-launch path reuses its grid-barrier word) gives the same bits
+    Y2 = torch.empty_like(Y)
+    ctx.check(dib.lib().di_group_norm_nhwc(ctx.h, 1, X1.data_ptr(), C1, X2.data_ptr() if C2 else None, C2, N, HW, G,
+                                           1e-5, Gt.data_ptr(), Bt.data_ptr(), silu, Y2.data_ptr()), "gn")
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
+    assert ctx.fault() == 0
 
 
 def test_tembed(ctx, dib, oracle):
