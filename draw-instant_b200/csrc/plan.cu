@@ -465,7 +465,16 @@ struct Plan {
   cudaStream_t side = nullptr;
   void* splitk_side = nullptr;
   std::vector<cudaEvent_t> fork_ev;  // [2j] fork, [2j + 1] join
+  // fork_live[j]: branch j was enqueued in the current pass and not joined yet.  A consumer joins only a
+  // live branch, and every pass ends by joining the rest (join_all), so a pass over a subset of the ops
+  // (profile_kind) that runs a branch without its consumer, or a consumer without its branch, still
+  // captures a well-formed graph.
+  mutable std::vector<char> fork_live;
   int record_fork(std::function<int()> f, int kind, double flops, double bytes, int kernels) {
+    return insert_fork(ops.size(), std::move(f), kind, flops, bytes, kernels);
+  }
+  // The same, inserted as op `at` (a branch built after the ops that follow it, e.g. the time MLP).
+  int insert_fork(size_t at, std::function<int()> f, int kind, double flops, double bytes, int kernels) {
     if (!side) {
       if (cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking) != cudaSuccess) {
         fail(DI_ECUDA, "plan: side stream");
@@ -475,11 +484,12 @@ struct Plan {
     }
     const int j = (int)fork_ev.size() / 2;
     fork_ev.resize(fork_ev.size() + 2);
+    fork_live.push_back(0);
     cudaEventCreateWithFlags(&fork_ev[2 * j], cudaEventDisableTiming);
     cudaEventCreateWithFlags(&fork_ev[2 * j + 1], cudaEventDisableTiming);
     Ctx* cc = c;
     Plan* self = this;
-    ops.push_back([cc, self, j, f = std::move(f)] {
+    ops.insert(ops.begin() + at, [cc, self, j, f = std::move(f)] {
       cudaEventRecord(self->fork_ev[2 * j], cc->stream);
       cudaStreamWaitEvent(self->side, self->fork_ev[2 * j], 0);
       cudaStream_t main_stream = cc->stream;
@@ -489,14 +499,21 @@ struct Plan {
       cc->weights_const = false;
       cc->stream = main_stream;
       cudaEventRecord(self->fork_ev[2 * j + 1], self->side);
+      self->fork_live[j] = 1;
       return r;
     });
-    info.push_back({kind, flops, bytes, kernels});
+    info.insert(info.begin() + at, OpInfo{kind, flops, bytes, kernels});
     launches += kernels;
     return j;
   }
   void join(int j) const {
-    if (j >= 0) cudaStreamWaitEvent(c->stream, fork_ev[2 * j + 1], 0);
+    if (j >= 0 && fork_live[j]) {
+      cudaStreamWaitEvent(c->stream, fork_ev[2 * j + 1], 0);
+      fork_live[j] = 0;
+    }
+  }
+  void join_all() const {
+    for (int j = 0; j < (int)fork_live.size(); ++j) join(j);
   }
 
   // Device time of the ops of one kind alone: a graph holding only those launches (same buffers, same
@@ -522,6 +539,7 @@ struct Plan {
       }
       for (size_t i = 0; i < ops.size() && r == DI_OK; ++i)
         if (info[i].kind == kind) r = ops[i]();
+      join_all();
       cudaError_t e = cudaStreamEndCapture(stream, &g);
       if (r != DI_OK || e != cudaSuccess || cudaGraphInstantiate(&kexec[kind], g, 0) != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
@@ -578,6 +596,7 @@ struct Plan {
         r = ops[i]();
         cudaEventRecordWithFlags(pev[i + 1], stream, cudaEventRecordExternal);
       }
+      join_all();
       cudaError_t e = cudaStreamEndCapture(stream, &g);
       if (r != DI_OK || e != cudaSuccess || cudaGraphInstantiate(&pexec, g, 0) != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
@@ -607,8 +626,12 @@ struct Plan {
     if (stats_off) cudaMemsetAsync(stats_base, 0, stats_off * sizeof(long long), c->stream);
     for (auto& f : ops) {
       int r = f();
-      if (r) return r;
+      if (r) {
+        join_all();
+        return r;
+      }
     }
+    join_all();
     return DI_OK;
   }
 
@@ -617,10 +640,10 @@ struct Plan {
     if (err) return err;
     if (const char* e = getenv("DI_PLAN_LIMIT")) {  // diagnostics: run only the first k ops, eagerly
       const size_t k = std::min<size_t>(ops.size(), (size_t)std::max(0, atoi(e)));
-      for (size_t i = 0; i < k; ++i) {
-        const int r = ops[i]();
-        if (r) return r;
-      }
+      int r = DI_OK;
+      for (size_t i = 0; i < k && r == DI_OK; ++i) r = ops[i]();
+      join_all();
+      if (r) return r;
       return cudaStreamSynchronize(c->stream) == cudaSuccess ? DI_OK : DI_ECUDA;
     }
     cudaEventRecord(ev_in, c->stream);
@@ -924,6 +947,8 @@ struct Plan {
     }
     const int toff = tproj_rows;
     if (temb) tproj_rows += Co;
+    const bool join_temb = temb && !temb_seen;  // the first reader of the time projections
+    if (temb) temb_seen = true;
     const void* w1 = conv_weight(pre + ".conv1.weight", Co, Ci, Ci, Co);
     const float* b1 = bias_padded(pre + ".conv1.bias", Co, Co, Ci * 9);
     Act h;
@@ -935,6 +960,7 @@ struct Plan {
     Plan* self = this;
     void* sk = splitk;
     record([=] {
+      if (join_temb) self->join(self->temb_fork);
       const GnFuse f{g1.tab, g1.silu};
       return with_stats(cc, h.st, H * W, [&] {
         return gemm_conv3x3(cc, DI_F16, g1.x1, g1.C1, g1.x2, g1.C2, N, H, W, 1, w1, Co, b1,
@@ -1015,7 +1041,10 @@ struct Plan {
       ctxkv_w.insert(ctxkv_w.end(), wkv.begin(), wkv.end());
       ctxkv_rows += 2 * C;
       Plan* self = this;
+      const bool join_ctx = !ctx_seen;  // the first reader of the context projection
+      ctx_seen = true;
       record([=] {
+        if (join_ctx) self->join(self->ctx_fork);
         const __half* base = self->ctxkv + off;
         const long long ld = self->ctxkv_rows;
         return attention(cc, DI_F16, q2, base, base + C, o2, N, heads, HW, Sk, 0, C, ld, ld, C);
@@ -1164,28 +1193,56 @@ struct Plan {
   std::vector<float> ctxkv_w;
   int ctxkv_rows = 0;
   __half* ctxkv = nullptr;
+  // The step's prologue work whose results are needed only later (the time MLP and the ResNets' time
+  // projections, first read by the first conv1 epilogue; the context K / V projection, first read by the
+  // first cross-attention) runs on the side branch beside conv_in and the first GroupNorms / convs.
+  // DI_PLAN_PREFORK=0 keeps it on the main chain (diagnostics).
+  static bool prefork_ok() {
+    static const bool on = [] {
+      const char* e = getenv("DI_PLAN_PREFORK");
+      return !(e && e[0] == '0');
+    }();
+    return on;
+  }
+  int temb_fork = -1, ctx_fork = -1;  // side branches joined by the first consumer (resnet / transformer)
+  bool temb_seen = false, ctx_seen = false;
+
+  // Inserts op `at`: the context K / V projection of every transformer block, one GEMM.
   void finish_ctx_kv(size_t at, const void* ctx16, int rows, int Cctx) {
     const void* W = upload_f16(ctxkv_w);
     ctxkv = static_cast<__half*>(act_alloc(sizeof(__half) * (size_t)rows * ctxkv_rows));
     Ctx* cc = c;
     const int N = ctxkv_rows;
     __half* out = ctxkv;
-    void* sk = splitk;
-    info.insert(info.begin() + at, OpInfo{0, 2.0 * rows * N * Cctx, 2.0 * ((double)rows * Cctx + (double)N * Cctx +
-                                          (double)rows * N), gemm_kernel_count(c, rows, N, Cctx, 0)});
-    launches += gemm_kernel_count(c, rows, N, Cctx, 0);
-    ops.insert(ops.begin() + at, [=] {
-      cc->weights_const = true;
-      const int r = gemm_linear(cc, DI_F16, ctx16, Cctx, nullptr, rows, Cctx, W, N, nullptr, nullptr, 0, out, 0, 0,
-                                nullptr, 1, sk);
-      cc->weights_const = false;
-      return r;
-    });
+    const double flops = 2.0 * rows * N * Cctx;
+    const double bytes = 2.0 * ((double)rows * Cctx + (double)N * Cctx + (double)rows * N);
+    const int kern = gemm_kernel_count(c, rows, N, Cctx, 0);
+    if (prefork_ok()) {
+      Plan* self = this;
+      ctx_fork = insert_fork(at, [=] {
+        return gemm_linear(cc, DI_F16, ctx16, Cctx, nullptr, rows, Cctx, W, N, nullptr, nullptr, 0, out, 0, 0,
+                           nullptr, 1, self->splitk_side);
+      }, 0, flops, bytes, kern);
+    } else {
+      void* sk = splitk;
+      info.insert(info.begin() + at, OpInfo{0, flops, bytes, kern});
+      launches += kern;
+      ops.insert(ops.begin() + at, [=] {
+        cc->weights_const = true;
+        const int r = gemm_linear(cc, DI_F16, ctx16, Cctx, nullptr, rows, Cctx, W, N, nullptr, nullptr, 0, out, 0, 0,
+                                  nullptr, 1, sk);
+        cc->weights_const = false;
+        return r;
+      });
+    }
     ctxkv_w.clear();
     ctxkv_w.shrink_to_fit();
   }
 
-  void finish_time_proj(size_t at, const float* temb, int B) {
+  // Inserts op `at`: `pre` (the time MLP writing `temb`, `pre_kernels` launches) followed by one GEMV
+  // computing every ResNet's time projection from it.
+  void finish_time_proj(size_t at, const float* temb, int B, std::function<int()> pre, double pre_flops,
+                        double pre_bytes, int pre_kernels) {
     const void* W = upload_f16(tproj_w);
     const float* b = upload_f32(tproj_b);
     temb_all = static_cast<float*>(act_alloc(sizeof(float) * (size_t)B * tproj_rows));
@@ -1193,16 +1250,23 @@ struct Plan {
     Ctx* cc = c;
     const int rows = tproj_rows;
     float* out = temb_all;
-    info.insert(info.begin() + at, OpInfo{3, 2.0 * B * rows * 1280, 2.0 * rows * 1280, (B + 7) / 8});
-    ops.insert(ops.begin() + at, [=] {
-      for (int b0 = 0; b0 < B; b0 += 8) {
+    auto f = [=] {
+      int r = pre();
+      for (int b0 = 0; b0 < B && r == DI_OK; b0 += 8) {
         const int nb = std::min(8, B - b0);
-        int r = gemv(cc, temb + (size_t)b0 * 1280, nb, 1280, W, 1, b, rows, 1, out + (size_t)b0 * rows, rows);
-        if (r) return r;
+        r = gemv(cc, temb + (size_t)b0 * 1280, nb, 1280, W, 1, b, rows, 1, out + (size_t)b0 * rows, rows);
       }
-      return DI_OK;
-    });
-    launches += (B + 7) / 8;
+      return r;
+    };
+    const double flops = pre_flops + 2.0 * B * rows * 1280, bytes = pre_bytes + 2.0 * rows * 1280;
+    const int kern = pre_kernels + (B + 7) / 8;
+    if (prefork_ok()) {
+      temb_fork = insert_fork(at, f, 3, flops, bytes, kern);
+    } else {
+      info.insert(info.begin() + at, OpInfo{3, flops, bytes, kern});
+      ops.insert(ops.begin() + at, f);
+      launches += kern;
+    }
     tproj_w.clear();
     tproj_w.shrink_to_fit();
   }
@@ -1273,6 +1337,7 @@ static int build_unet(UNetPlan* u) {
   // timestep embedding (fp32 weights, fp16-rounded values)
   float* temb = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 1280));
   float* thid = static_cast<float*>(P.act_alloc(sizeof(float) * (size_t)B * 1280));
+  std::function<int()> temb_fn;
   {
     auto w1 = P.host_param("time_embedding.linear_1.weight", (size_t)1280 * 320, 0, 320, 1280);
     Plan::round_f16(w1);
@@ -1283,14 +1348,15 @@ static int build_unet(UNetPlan* u) {
     const float* W2 = P.upload_f32(w2);
     const float* b2 = P.vec("time_embedding.linear_2.bias", 1280, 0, 1280);
     const float* tv = u->tvals;
-    P.record([=] {
+    // run, with the time projections, as one op (finish_time_proj) on the plan's side branch
+    temb_fn = [=] {
       for (int b0 = 0; b0 < B; b0 += 8) {
         const int nb = std::min(8, B - b0);
         int r = tembed(cc, tv + b0, nb, W1, b1, W2, b2, 320, 1280, thid + (size_t)b0 * 1280, temb + (size_t)b0 * 1280);
         if (r) return r;
       }
       return DI_OK;
-    }, 3, 2.0 * B * 1280 * (320 + 1280), 4.0 * 1280 * (320 + 1280), 2 * ((B + 7) / 8));
+    };
   }
   const size_t tproj_at = P.ops.size();
   P.batch_ctx_kv = true;
@@ -1367,8 +1433,9 @@ static int build_unet(UNetPlan* u) {
       return check_launch(cc, "latent_out");
     }, 3, 0, (double)B * H * W * (32 + 16 + 32));
   }
-  P.finish_time_proj(tproj_at, temb, B);
-  P.finish_ctx_kv(tproj_at, ctx16, B * Sk, 1024);
+  P.finish_time_proj(tproj_at, temb, B, temb_fn, 2.0 * B * 1280 * (320 + 1280), 4.0 * 1280 * (320 + 1280),
+                     2 * ((B + 7) / 8));
+  P.finish_ctx_kv(tproj_at + 1, ctx16, B * Sk, 1024);  // after the time MLP on the side branch
   cudaDeviceSynchronize();
   return P.err;
 }

@@ -95,6 +95,24 @@ def test_unet_full_size_properties(ctx, dib, oracle):
     assert u.launches > 100
 
 
+def test_unet_profiles_keep_branches_joined(ctx, dib, oracle):
+    """The plan's side branches (time MLP, context K/V projection, ResNet shortcuts) are joined in every
+    captured pass: the per-kind replays (a branch without its consumer or the reverse) and the per-op
+    profile capture succeed, and the forward after them is unchanged."""
+    import importlib
+    unet = importlib.import_module("draw_instant_b200.unet")
+    u = unet.UNet(ctx, B=2, H=16, W=16, seed=3)
+    lat = oracle.gen_normal(3, "latent", 2 * 4 * 16 * 16).reshape(2, 4, 16, 16)
+    cx = oracle.gen_normal(3, "context", 2 * 77 * 1024).reshape(2, 77, 1024)
+    a = u.forward_host(lat, 999.0, cx)
+    for kind in range(4):
+        assert u.profile_kind(kind, reps=2) >= 0.0
+    assert np.all(u.profile(reps=2) >= 0.0)
+    b = u.forward_host(lat, 999.0, cx)
+    assert np.array_equal(a, b)
+    assert ctx.fault() == 0
+
+
 @pytest.mark.parametrize("B,h,w", [(1, 8, 8), (2, 8, 16), (1, 64, 64)])
 def test_vae_decoder_vs_oracle(ctx, dib, oracle, B, h, w):
     """SD VAE decoder (config 5's decode) at small latents: cosine >= 0.999 and max-rel <= 1e-2 against the
