@@ -43,9 +43,10 @@ METRIC = "SD-Turbo 512² U-Net steps/s at 1/2/4/8 B200; per-block ms vs roofline
 WORKLOAD = ("config 4: SD-Turbo (SD2.1) U-Net single denoising step, 64x64 latent (512x512 image), t=999, "
             "context 77x1024")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes per launch of the dominant kernel from the committed ncu capture
-# (profiles/gemm_tc_kernel_unet_conv.md); None until that capture exists.
+# DRAM bytes (read + write) per launch of the dominant kernel, the mean over the GEMM launches of one
+# forward in the committed ncu capture (profiles/gemm_tc_unet64_dram.md); None until that capture exists.
 GEMM_TRAFFIC = None
+GEMM_TRAFFIC_SOURCE = "not captured"
 
 
 def load_package():
@@ -187,14 +188,22 @@ def run_reference(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-            "config": {"workload": WORKLOAD, "global_batch": 1, "latent": [1, 4, 64, 64], "parallelism": "cpu",
-                       "reference_runtime": "unavailable on this box: the reference path is WGSL on WebGPU "
-                                            "(Deno/wgpu lavapipe); no JS runtime and no graphics stack here"},
+            "config": run_config(1, world, unet_mod.unet_flops(1, 64, 64), per_step * 1e3,
+                                 "none: one CPU process on rank 0 (all host threads)"),
+            "reference_runtime": "unavailable on this box: the reference path is WGSL on WebGPU "
+                                 "(Deno/wgpu lavapipe); no JS runtime and no graphics stack here",
             "cpu_baseline": {"value": value, "unit": "steps/s", "cores": oracle.num_threads(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     oracle.clear_cache()
     print(json.dumps(line), flush=True)
+
+
+def run_config(B, world, step_flops, ms_step, parallelism):
+    """The `config` object of both arms (same keys, same workload)."""
+    return {"workload": WORKLOAD, "global_batch": B * world, "batch_per_gpu": B, "latent": [B, 4, 64, 64],
+            "parallelism": parallelism, "l2": "inputs larger than L2: 1.73 GB of fp16 weights streamed per step",
+            "step_gflop": step_flops / 1e9, "step_tflops": step_flops / (ms_step / 1e3) / 1e12}
 
 
 def vae_result(ctx, pk, src):
@@ -417,10 +426,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic: seeded N(0,1) latent and context, seeded random-init SD2.1 U-Net weights",
-            "config": {"workload": WORKLOAD, "global_batch": B * world, "batch_per_gpu": B, "latent": [B, 4, 64, 64],
-                       "parallelism": f"replicas x{world} (batch sharded, NCCL all-gather of outputs)",
-                       "l2": "inputs larger than L2: 1.73 GB of fp16 weights streamed per step",
-                       "step_gflop": step_flops / 1e9, "step_tflops": step_flops / (ms_step / 1e3) / 1e12},
+            "config": run_config(B, world, step_flops, ms_step,
+                                 f"replicas x{world} (batch sharded, NCCL all-gather of outputs)"),
             "clocks": sampler.summary(), "gpu_launches": int(u.launches * args.steps), "device_fault": ctx.fault()}
 
     if not args.no_extras:
@@ -455,19 +462,30 @@ def main():
         gemm_ms = kind_ms[0]
         n_gemm = int(ops["kernels"][gemm].sum())
         pk, src = peaks()
-        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        # 20 replays of a ~3 ms graph is a burst, not a seconds-long loop: the burst peak applies
+        peak = pk["bf16_tflops"]
         achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
         names = ["gemm", "attention", "norm", "other"]
+        norm = kinds == 2
+        norm_bytes = float(ops["bytes"][norm].sum())
+        norm_gbs = norm_bytes / (kind_ms[2] / 1e3) / 1e9 if kind_ms[2] > 0 else None
         line["roofline"] = {
             "bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05 implicit-GEMM conv3x3 + linear)",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
             "frac": achieved / peak if achieved else None,
-            "peak_source": f"{src} bf16_tflops_sustained (fp16 runs at the bf16 tensor rate; timed inside the step)",
-            "traffic": GEMM_TRAFFIC, "launches_per_step": n_gemm,
+            "peak_source": f"{src} bf16_tflops (burst: the GEMM subset is timed as 20 replays of a ~3 ms graph; "
+                           "fp16 runs at the bf16 tensor rate)",
+            "traffic": GEMM_TRAFFIC, "algorithmic_bytes_per_launch": float(ops["bytes"][gemm].sum()) / max(1, n_gemm),
+            "traffic_source": GEMM_TRAFFIC_SOURCE, "launches_per_step": n_gemm,
             "flops_per_launch": gemm_flops / max(1, n_gemm), "ms_per_launch": gemm_ms / max(1, n_gemm),
             "timing": "the step's GEMM/conv launches replayed alone as one graph, CUDA events, 20 replays",
             "share_of_step": gemm_ms / ms_step,
-            "time_by_kind_ms": {names[k]: v for k, v in kind_ms.items()}}
+            "time_by_kind_ms": {names[k]: v for k, v in kind_ms.items()},
+            "norm": {"bound": "hbm", "kernels": "GroupNorm statistics + apply, LayerNorm",
+                     "algorithmic_bytes_per_step": norm_bytes, "ms_per_step": kind_ms[2], "achieved": norm_gbs,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": norm_gbs / pk["hbm_gbs"] if norm_gbs else None,
+                     "launches_per_step": int(ops["kernels"][norm].sum())}}
         line["t2i_config5"] = t2i_result(ctx, pk, src, R, rank, world)
         if rank == 0 and world == 1:
             line["blocks"] = block_results(dib, ctx, pk, src)

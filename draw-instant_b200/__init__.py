@@ -53,6 +53,7 @@ SIGNATURES = {
     "di_device_fault": (_I, [_P]),
     "di_clear_fault": (_I, [_P]),
     "di_debug_gemm_trace": (_I, [_P, _I]),
+    "di_debug_wait_timeout": (_I, [_P, _I]),
     "di_f16_bytes_to_f32": (_I, [_P, _P, _P, _SZ]),
     "di_unary": (_I, [_P, _I, _P, _P, _U]),
     "di_binary": (_I, [_P, _I, _P, _U, _P, _U, _P, _U]),

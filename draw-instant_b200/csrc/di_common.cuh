@@ -112,7 +112,7 @@ inline cudaError_t launch_k_cluster(void (*kern)(KArgs...), dim3 grid, dim3 bloc
 // device error codes (OR-ed into Ctx::d_err)
 enum : int {
   DEVERR_WAIT_TMA = 1, DEVERR_WAIT_MMA = 2, DEVERR_WAIT_EPI = 4, DEVERR_WAIT_SOFTMAX = 8,
-  DEVERR_BOUNDS = 16, DEVERR_GRID_BARRIER = 32,
+  DEVERR_BOUNDS = 16, DEVERR_GRID_BARRIER = 32, DEVERR_WAIT_PROBE = 64,
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -181,7 +181,8 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t pa
 }
 // Bounded wait: returns false (and records `code`) if the phase did not complete in time.
 template <bool CLUSTER = false>
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_u32(bar);
   auto probe = [&] { return CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity); };
   if (probe()) return true;
@@ -190,7 +191,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 #pragma unroll 1
     for (int i = 0; i < 256; ++i)
       if (probe()) return true;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > timeout_ns) {
       if (err) atomicOr(err, code);
       return false;
     }

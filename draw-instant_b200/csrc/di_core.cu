@@ -21,6 +21,8 @@ struct di_buf_s {
 
 namespace di {
 
+void noalloc_forget(int device);  // k_noalloc.cu
+
 int set_error(Ctx* c, int code, const std::string& msg) {
   if (c) c->last_error = msg;
   return code;
@@ -123,6 +125,7 @@ void di_destroy(di_ctx_t ctx) {
   for (auto& w : ctx->c.ws)
     if (w.ptr) cudaFree(w.ptr);
   if (ctx->c.own_stream) cudaStreamDestroy(ctx->c.stream);
+  di::noalloc_forget(ctx->c.device);
   delete ctx;
 }
 
@@ -217,6 +220,26 @@ int di_clear_fault(di_ctx_t ctx) {
 }
 
 }  // extern "C"
+
+namespace {
+// One thread waits, through the same bounded mbarrier wait every pipeline kernel uses, on a barrier phase
+// that nothing completes; after `timeout_ns` it records DEVERR_WAIT_PROBE in the error word and returns.
+__global__ void wait_probe_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  di::mbar_init(&bar, 1);
+  di::fence_mbar_init();
+  di::mbar_wait(&bar, 0, err, di::DEVERR_WAIT_PROBE, timeout_ns);
+}
+}  // namespace
+
+extern "C" int di_debug_wait_timeout(di_ctx_t ctx, int timeout_us) {
+  if (!ctx) return DI_EINVAL;
+  if (timeout_us <= 0 || timeout_us > 1000000)
+    return set_error(&ctx->c, DI_EINVAL, "di_debug_wait_timeout: timeout_us must be in 1 .. 1000000");
+  wait_probe_kernel<<<1, 32, 0, ctx->c.stream>>>(ctx->c.d_err, 1000ull * (unsigned long long)timeout_us);
+  return di::check_launch(&ctx->c, "wait_probe_kernel");
+}
 
 // Internal accessors used by the other translation units.
 namespace di {

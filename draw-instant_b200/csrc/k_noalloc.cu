@@ -10,6 +10,8 @@
 //
 // Host code cannot use the array's name as a device address (on the host it is only a stand-in), so
 // the device address is looked up once per device with cudaGetSymbolAddress and passed to the kernels.
+// Under CUDA's lazy module loading that first lookup (and the kernels' first launch) may load the
+// library's device code, which allocates: callers make one call per device at start-up.
 #include <mutex>
 
 #include "di_common.cuh"
@@ -51,6 +53,15 @@ int scratch_address(Ctx* c, void** out) {
 }
 
 }  // namespace
+
+// Called by di_destroy: the next call on `device` looks the address up again, so a module reloaded after
+// the context is re-created (for example after a device reset) is never addressed through a stale pointer.
+void noalloc_forget(int device) {
+  if (device < 0 || device >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_scratch_addr[device] = nullptr;
+}
+
 }  // namespace di
 
 using namespace di;

@@ -63,6 +63,12 @@ DI_API int di_clear_fault(di_ctx_t ctx);
  * done, dependency wait passed, first stage landed, last MMA issued, accumulator ready, epilogue done,
  * exit, then epilogue detail (TMEM load issue / done for chunks 0 and 1, store issued for chunks 0, 1).  ctas = 0 switches it off.  Launches in flight keep the pointer they were given. */
 DI_API int di_debug_gemm_trace(unsigned long long* buf, int ctas);
+/* Fault-path probe (test support for the sticky fault of unet-wgsl.js:32-38): enqueues one kernel whose
+ * bounded mbarrier wait (the helper every pipeline kernel uses) waits on a phase nothing completes, gives
+ * up after timeout_us (1 .. 1e6) microseconds, sets flag 64 in the device error word and returns: the
+ * context stays usable, di_device_fault reports the flag and di_clear_fault clears it.  No trap, no
+ * unbounded wait. */
+DI_API int di_debug_wait_timeout(di_ctx_t ctx, int timeout_us);
 
 /* ---------------------------------------------------------------------------------------------
  * wgsl-ops.js op families: fp32 tensors in the reference's layouts, cfg blocks exactly as the
@@ -141,7 +147,12 @@ DI_API int di_group_norm_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, c
  * reference.  Its scratch is a fixed 1 MiB array inside the library (kept on every GPU that loads the
  * library until the process exits): sizes needing more than N * max(1, min(16, HW/256)) * G * 8 =
  * 1 MiB are rejected with DI_EINVAL.  The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress), so make that first call before any stream capture.  All calls share the one
+ * (cudaGetSymbolAddress); under CUDA's lazy module loading that lookup, and the first launch of the
+ * GroupNorm kernels, may load the library's device code, which allocates.  So make one call per device
+ * at start-up, before any stream capture and before the no-allocation period begins; later calls
+ * allocate nothing.  The looked-up address is forgotten when a context on that device is destroyed
+ * (di_destroy) and looked up again by the next call; do not call it across a device reset without
+ * destroying the contexts first.  All calls share the one
  * array: calls that may overlap on the GPU (different streams or contexts on the same device) race and
  * must be serialised by the caller. */
 DI_API int di_group_norm_nhwc_noalloc(di_ctx_t ctx, int dtype, const void* x1, int C1, const void* x2, int C2, int N,

@@ -156,6 +156,54 @@ def test_attention(ctx, dib, oracle, B, H, Sq, Skv, layout, dtype):
     assert cosine(got, ref) > 0.9999
 
 
+def _cfg3_inputs(scale, dtype, skv_cross=False):
+    """Config 3's inputs as bench.py draws them: seed-2 torch generator on the GPU, ~N(0,1) * scale."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(2)
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    mk = lambda *s: (torch.randn(*s, device="cuda", generator=g) * scale).to(tdt)
+    q, k, v = mk(8, 5, 4096, 64), mk(8, 5, 4096, 64), mk(8, 5, 4096, 64)
+    kc, vc = mk(8, 5, 77, 64), mk(8, 5, 77, 64)
+    return q, k, v, kc, vc
+
+
+@pytest.mark.parametrize("dtype,scale", [("bf16", 0.125), ("f16", 3.0), ("bf16", 3.0)])
+def test_attention_config3_self(ctx, dib, oracle, dtype, scale):
+    """Config 3 self-attention at its own shape, Q/K/V [8,5,4096,64] head-major, seed 2, ~N(0,1)/sqrt(64)
+    (fused-attn.js:199-307); sampled query rows of every head against the oracle.  The x3 cases make the
+    score spread large (std ~9 in natural-log units), so the running row maximum rises by more than the
+    kernel's lazy-rescale threshold (8 in log2 units) after the first key tiles."""
+    import torch
+    q, k, v, _, _ = _cfg3_inputs(scale, dtype)
+    o = torch.zeros_like(q)
+    ctx.check(dib.lib().di_attention(ctx.h, _code(dtype), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 8, 5,
+                                     4096, 4096, 1), "attention")
+    torch.cuda.synchronize()
+    rows = np.arange(0, 4096, 37)
+    ref = oracle.attention(_np(q), _np(k), _np(v), 8, 5, 4096, 4096, 1, rows)[:, :, rows]
+    got = _np(o)[:, :, rows]
+    assert np.all(np.isfinite(got))
+    assert rel_err(got, ref) < TOL
+    assert cosine(got, ref) > 0.999
+    assert ctx.fault() == 0
+
+
+@pytest.mark.parametrize("dtype,scale", [("bf16", 0.125), ("f16", 3.0)])
+def test_attention_config3_cross(ctx, dib, oracle, dtype, scale):
+    """Config 3 cross-attention: Q [8,5,4096,64], K/V [8,5,77,64] (fused-cross-attn.js:112-173), every row."""
+    import torch
+    q, _, _, kc, vc = _cfg3_inputs(scale, dtype)
+    o = torch.zeros_like(q)
+    ctx.check(dib.lib().di_attention(ctx.h, _code(dtype), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), 8,
+                                     5, 4096, 77, 1), "attention")
+    torch.cuda.synchronize()
+    ref = oracle.attention(_np(q), _np(kc), _np(vc), 8, 5, 4096, 77, 1)
+    got = _np(o)
+    assert rel_err(got, ref) < TOL
+    assert cosine(got, ref) > 0.999
+    assert ctx.fault() == 0
+
+
 @pytest.mark.parametrize("N,HW,C1,C2,G,silu", [(1, 4096, 320, 0, 32, 1), (2, 256, 1280, 1280, 32, 1),
                                                (1, 64, 640, 320, 32, 0), (1, 1024, 1920, 0, 32, 1),
                                                (1, 262144, 128, 0, 32, 1), (2, 65536, 256, 256, 32, 1),

@@ -137,3 +137,37 @@ def test_text_to_image_vs_oracle(ctx, dib, oracle, B, h):
     assert cosine(p.context.cpu().numpy(), cx) >= 0.999
     assert cosine(p.eps.cpu().numpy(), eps) >= 0.999
     assert ctx.fault() == 0
+
+
+def test_text_to_image_config5_batch64(ctx, dib, oracle):
+    """Config 5 as bench.py times it: B = 64 prompts, 24 text layers, 64x64 latents, 512x512 images.
+    Every image must equal the same prompt and latent run through a batch-1 pipeline (batch invariance:
+    the GEMM tilings, split-K and the VAE chunking differ between the two), and images 0 and 63 must
+    match the oracle composition text_encode -> unet_forward(scaleModelInput) -> Euler step -> vae_decode
+    (unet-wgsl-test.html:174-193's whole-output check: cosine and max error)."""
+    import torch
+    t2i = importlib.import_module("draw_instant_b200.t2i")
+    seed, B, h, layers = 4, 64, 64, 24
+    sig = oracle.sched_sigmas(1)
+    ids = np.random.default_rng(64).integers(0, 49408, (B, 77)).astype(np.int32)
+    lat = oracle.noise_latent(B, h, h, 13, float(sig[0]))
+    p = t2i.Text2Image(ctx, B=B, h=h, w=h, text_layers=layers, seed=seed)
+    img = p.forward_host(ids, lat)
+    p.close()
+    del p
+    torch.cuda.empty_cache()
+    assert img.shape == (B, 3, 512, 512) and np.all(np.isfinite(img))
+    one = t2i.Text2Image(ctx, B=1, h=h, w=h, text_layers=layers, seed=seed)
+    for i in range(B):
+        s = one.forward_host(ids[i:i + 1], lat[i:i + 1])
+        assert rel_err(img[i], s[0]) <= 2e-3, f"image {i}: batch-64 vs batch-1 {rel_err(img[i], s[0])}"
+    one.close()
+    for i in (0, B - 1):
+        cx = oracle.text_encode(ids[i:i + 1], layers, seed)
+        eps = oracle.unet_forward(oracle.sched_scale_input(lat[i:i + 1], float(sig[0])), 999.0,
+                                  cx.astype(np.float16).astype(np.float32), seed)
+        x0 = oracle.sched_step(lat[i:i + 1], eps, float(sig[0]), float(sig[1]))
+        ref = oracle.vae_decode(x0, seed)[0]
+        assert cosine(img[i], ref) >= 0.999, f"image {i}"
+        assert rel_err(img[i], ref) <= 1e-2, f"image {i}"
+    assert ctx.fault() == 0
