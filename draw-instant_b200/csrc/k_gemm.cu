@@ -53,6 +53,10 @@ struct GemmParams {
   int vec_ok;  // 16-byte aligned rows for out / residual: vectorised epilogue
   int b_early;     // weights are constant data: fetch the first B stages before the dependency wait
   int splits;      // K splits; > 1 writes raw fp32 partials, the reduce kernel applies the epilogue
+  // Cluster split-K (splits > 1, launched as clusters of `splits` CTAs): CTA rank r of a cluster takes K
+  // split r of the cluster's tiles, and the cluster sums its partials through distributed shared memory in
+  // the epilogue (fixed rank order), so no fp32 partials reach global memory and no reduce kernel runs.
+  int cs;
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
   long long* gstats;  // GroupNorm(32) statistics of the fp16 output (Ctx::gn_stats), or null
@@ -217,17 +221,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   uint64_t* tempty = tfull + 2;      // [2] accumulator drained by the epilogue
   uint64_t* afull = tempty + 2;       // [STAGES] this CTA's A tile landed (operand-fused GroupNorm only)
   uint64_t* aready = afull + STAGES;  // [STAGES] A tiles transformed (on the pair leader: both CTAs')
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aready + STAGES);
+  uint64_t* xfull = aready + STAGES;   // [kEpiWarps] cluster split-K: every rank's slab of this warp written
+  uint64_t* xempty = xfull + kEpiWarps;  // [kEpiWarps] cluster split-K: every rank done reading this warp's slab
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0 = leader
-  const int cta0 = PAIR ? blockIdx.x >> 1 : blockIdx.x;  // first unit of this CTA (pair)
-  const int cstride = PAIR ? gridDim.x >> 1 : gridDim.x;
+  // Cluster split-K: rank csr runs split csr of tiles cluster, cluster + clusters, ... (units
+  // csr * per_split + tile), so every CTA of a cluster walks the same tiles in the same order.
+  const int CS = PAIR ? 0 : p.cs;  // cluster size of the split-K cluster, 0 = off
+  const int csr = CS ? (int)cluster_ctarank() : 0;
+  const int cta0 = PAIR ? blockIdx.x >> 1 : (CS ? csr * p.m_tiles * p.n_tiles + (int)blockIdx.x / CS : blockIdx.x);
+  const int cstride = PAIR ? gridDim.x >> 1 : (CS ? (int)gridDim.x / CS : gridDim.x);
   unsigned long long* tr = p.trace ? p.trace + (size_t)blockIdx.x * kTracePoints : nullptr;
   if (tr && threadIdx.x == 0) tr[0] = globaltimer();
   const int nt = p.n_tiles, per_split = p.m_tiles * p.n_tiles;
-  const int units = per_split * p.splits;
+  const int units = CS ? (csr + 1) * per_split : per_split * p.splits;  // loop bound of this CTA's units
   const int kper = (p.num_k + p.splits - 1) / p.splits;
 
   if (threadIdx.x == 0) {
@@ -239,6 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     }
     // tempty: one arrival per epilogue warp (of both CTAs of a pair, on the leader's barrier)
     for (int s = 0; s < 2; ++s) { mbar_init(&tfull[s], 1); mbar_init(&tempty[s], (PAIR ? 2 : 1) * kEpiWarps); }
+    for (int w = 0; w < kEpiWarps; ++w) { mbar_init(&xfull[w], CS ? CS : 1); mbar_init(&xempty[w], CS ? CS : 1); }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -247,7 +258,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     else { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
   }
   tc_fence_before();
-  if (PAIR) cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
+  if (PAIR || CS) cluster_sync();  // every CTA's barriers initialised before any cross-CTA signal
   else __syncthreads();
   tc_fence_after();
   const uint32_t full0_leader = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
@@ -543,6 +554,72 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         }
       }
     };
+    // Cluster split-K epilogue of one 32 x 32 chunk (this warp's rows m0 + 32q .., columns nb ..): the raw
+    // partial goes to this warp's slab; once every rank's slab of this warp holds the same chunk, rank r
+    // sums rows r, r + CS, ... over the ranks' slabs in rank order (distributed shared memory reads),
+    // applies the epilogue and stores them.  Rounds alternate on xfull / xempty (one arrival per rank).
+    int xr = 0;
+    const int ew = warp - 2;
+    auto cs_reduce = [&](const float (&v)[32], int nb, int m0, int n_out) -> bool {
+      if (xr > 0 && !mbar_wait<true>(&xempty[ew], (xr - 1) & 1, p.err, DEVERR_WAIT_EPI)) return false;
+      float4* rp = reinterpret_cast<float4*>(stg + lane * 128);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) rp[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      __syncwarp();
+      if (lane < CS) mbar_arrive_cluster(mapa_shared(smem_u32(&xfull[ew]), lane));
+      if (!mbar_wait<true>(&xfull[ew], xr & 1, p.err, DEVERR_WAIT_EPI)) return false;
+      const int sub = lane >> 3, quad = lane & 7;
+      const uint32_t sl = smem_u32(stg);
+      const int nown = (32 - csr + CS - 1) / CS;  // rows csr, csr + CS, ... below 32
+      for (int k0 = 0; k0 < nown; k0 += 4) {
+        const int k = k0 + sub, r = csr + CS * k;
+        if (k < nown) {
+          const uint32_t off = sl + r * 128 + ((quad ^ (r & 7)) << 4);
+          float4 a = ld_cluster_f4(mapa_shared(off, 0));
+          for (int pr = 1; pr < CS; ++pr) {
+            const float4 b = ld_cluster_f4(mapa_shared(off, pr));
+            a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+          }
+          const int mm = m0 + q * 32 + r, col = nb + quad * 4;
+          if (mm < p.M && col < n_out) {
+            float f[4] = {a.x, a.y, a.z, a.w};
+            const int nc = min(4, n_out - col);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (j < nc) {
+                if (p.bias) f[j] += __ldg(p.bias + col + j);
+                if (p.rowvec) f[j] += __ldg(p.rowvec + (size_t)(mm / p.rowvec_div) * p.rowvec_ld + col + j);
+                if (p.act == 1) f[j] = silu_f(f[j]);
+                else if (p.act == 2) f[j] = gelu_erf(f[j]);
+                if (p.residual) f[j] += load_one(p.residual, (size_t)mm * p.ldr + col + j, p.res_f32, BF16);
+              }
+            }
+            const size_t o = (size_t)mm * p.ldo + col;
+            if (nc == 4 && p.vec_ok) {
+              if (p.out_f32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + o) = make_float4(f[0], f[1], f[2], f[3]);
+              } else {
+                uint32_t w0, w1;
+                if (BF16) {
+                  __nv_bfloat162 h0 = __floats2bfloat162_rn(f[0], f[1]), h1 = __floats2bfloat162_rn(f[2], f[3]);
+                  w0 = *reinterpret_cast<uint32_t*>(&h0); w1 = *reinterpret_cast<uint32_t*>(&h1);
+                } else {
+                  __half2 h0 = __floats2half2_rn(f[0], f[1]), h1 = __floats2half2_rn(f[2], f[3]);
+                  w0 = *reinterpret_cast<uint32_t*>(&h0); w1 = *reinterpret_cast<uint32_t*>(&h1);
+                }
+                *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + o) = make_uint2(w0, w1);
+              }
+            } else {
+              for (int j = 0; j < nc; ++j) store_one(p.out, o + j, f[j], p.out_f32, BF16);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane < CS) mbar_arrive_cluster(mapa_shared(smem_u32(&xempty[ew]), lane));
+      ++xr;
+      return true;
+    };
     int lt = 0, xit = 0;
     for (int u = cta0; u < units; u += cstride, ++lt) {
       int m0, n0, sp, kb0, kb1;
@@ -677,6 +754,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       const uint32_t trow = tmem + ab * BN + (static_cast<uint32_t>(q * 32) << 16);
       const bool split = p.splits > 1;
       const bool gg = p.geglu && !split;  // split-K stores raw packed partials; the reduce applies GEGLU
+      bool xok = true;  // cluster split-K exchange still in step with the peers
       const int nchunks = gg ? BN / 64 : BN / 32;
       const int n_out = gg ? p.N / 2 : p.N;
 #pragma unroll 1
@@ -719,17 +797,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           store_chunk(v, nb, m0, m, sp, false, p.staged);
           continue;
         }
+        if (CS) {
+          if (xok) xok = cs_reduce(v, nb, m0, n_out);
+          continue;
+        }
         store_chunk(v, nb, m0, m, sp, true, p.staged);  // fp32 partials: the reduce kernel finishes them
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + ab * 8);
       if (tr && lt == 0 && threadIdx.x == 64) tr[6] = globaltimer();
-      if (!ok) break;
+      if (!ok || !xok) break;
     }
   }
   tc_fence_before();
-  if (PAIR) cluster_sync();  // no CTA leaves while its pair partner may still signal its barriers
+  if (PAIR || CS) cluster_sync();  // no CTA leaves while a cluster peer may still read its slabs or signal it
   else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -741,6 +823,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
 
 // Pairs of CTAs that can be resident at once (clusters of 2 need both SMs in one GPC), per device.
 static int g_max_pairs[32] = {0};
+// Cluster split-K: clusters of n = 2 .. kMaxClusterSplit CTAs that can be resident at once, per device.
+constexpr int kMaxClusterSplit = 8;
+static int g_max_clusters[32][kMaxClusterSplit + 1] = {};
+
+static int max_clusters(Ctx* c, int n) {
+  int& mc = g_max_clusters[c->device & 31][n];
+  if (mc) return mc;
+  using S = GemmSmem<128, 6, false>;
+  auto kern = gemm_tc_kernel<128, 6, false, false, false>;
+  mc = std::max(1, c->num_sms / (2 * n));  // conservative if the query fails
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n * (c->num_sms / n));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = S::TOTAL;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = n;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int k = 0;
+    if (cudaOccupancyMaxActiveClusters(&k, kern, &cfg) == cudaSuccess && k > 0) mc = std::min(k, c->num_sms / n);
+  }
+  cudaGetLastError();
+  return mc;
+}
 
 template <int BN, int STAGES, bool BF16, bool PAIR, bool XF>
 int launch_variant(Ctx* c, const GemmParams& p) {
@@ -760,9 +870,14 @@ int launch_variant(Ctx* c, const GemmParams& p) {
   } else {
     grid = std::min(units, c->num_sms);
   }
+  if (!PAIR && p.cs) {  // clusters of p.cs CTAs, one cluster per tile at a time
+    const int per_split = p.m_tiles * p.n_tiles;
+    grid = p.cs * std::min(per_split, max_clusters(c, p.cs));
+  }
   GemmParams q = p;
   q.trace = (g_trace && grid <= g_trace_ctas) ? g_trace : nullptr;
   if (PAIR) launch_k_cluster(kern, grid, kGemmThreads, S::TOTAL, c->stream, 2, q);
+  else if (p.cs) launch_k_cluster(kern, grid, kGemmThreads, S::TOTAL, c->stream, p.cs, q);
   else launch_k(kern, grid, kGemmThreads, S::TOTAL, c->stream, q);
   return check_launch(c, "gemm_tc_kernel");
 }
@@ -911,10 +1026,23 @@ __global__ void splitk_reduce_gn(const float* __restrict__ part, int splits, int
 // K block of MMA work per SM: units = M tiles x N tiles x splits run on min(units, SMs) persistent CTAs;
 // cost = rounds x (K blocks per unit x (128 + BN)/256 + per-unit overhead) + split-K reduce (partial-sum
 // traffic and one launch).  GEGLU needs BN in {128, 256} (value/gate rows packed per 128 columns).
-void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits, int* pair) {
+void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* splits, int* pair, int* cs) {
   static const int cands[4] = {128, 160, 192, 256};
   const int mt = (M + BM - 1) / BM;
   *pair = 0;
+  *cs = 0;
+  // Cluster split-K (partials summed through distributed shared memory, no reduce launch): not for GEGLU
+  // (value and gate columns sit in different chunks) nor with epilogue GroupNorm statistics.
+  // DI_CLUSTER_SPLIT=0 switches it off (diagnostics).
+  static const int cs_ok = [] {
+    const char* e = getenv("DI_CLUSTER_SPLIT");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  static const double cs_cost = [] {  // exchange cost per 32-column chunk round, in K-block units
+    const char* e = getenv("DI_CLUSTER_SPLIT_COST");
+    return e ? atof(e) : 1.0;
+  }();
+  const bool allow_cs = cs_ok && !geglu && !c->gn_stats;
   // Tuning / diagnostics override: DI_GEMM_TILING="bn,splits[,pair]" forces the tiling of every GEMM.
   static int forced_bn = -1, forced_s = 1, forced_pair = 0;
   if (forced_bn < 0) {
@@ -924,17 +1052,21 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
       if (sscanf(e, "%d,%d,%d", &b, &s, &pr) >= 1 && (b == 128 || b == 160 || b == 192 || b == 256)) {
         forced_bn = b;
         forced_s = std::max(1, s);
-        forced_pair = pr ? 1 : 0;
+        forced_pair = pr == 2 ? 2 : (pr ? 1 : 0);
       }
     }
   }
   if (forced_bn && (!geglu || forced_bn % 128 == 0)) {
     *bn = forced_bn;
     int fs = forced_s;
-    while (fs > 1 && (size_t)M * N * fs * 4 > kSplitKWsBytes) --fs;
+    // forced pair value 2 = cluster split-K instead of paired tiles
+    const bool fcs = forced_pair == 2 && allow_cs;
+    if (fcs) fs = std::min(fs, kMaxClusterSplit);
+    while (!fcs && fs > 1 && (size_t)M * N * fs * 4 > kSplitKWsBytes) --fs;
     const int per = (num_k + fs - 1) / fs;
     *splits = (num_k + per - 1) / per;
-    *pair = forced_pair && M > BM;
+    *pair = forced_pair == 1 && M > BM;
+    *cs = (fcs && *splits > 1) ? *splits : 0;
     return;
   }
   // Model in units of one BN=128 K block on one CTA (~0.3 us, measured with the per-CTA trace).  A K
@@ -968,16 +1100,34 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
         const int per = (num_k + s - 1) / s;
         const int seff = (num_k + per - 1) / per;
         if (seff != s) continue;
-        if (s > 1 && (size_t)M * N * s * 4 > kSplitKWsBytes) break;  // partials must fit the buffer
+        // global partials must fit the buffer (a cluster split needs none)
+        const bool fits = s == 1 || (size_t)M * N * s * 4 <= kSplitKWsBytes;
+        if (!fits && !(allow_cs && !pr && s <= kMaxClusterSplit)) break;
         const long long units = (long long)mtiles * nt * s;
         const long long rounds = (units + slots - 1) / slots;
         double cost = (double)rounds * (per * kb_cost + 8.0) + 4.0;
         if (s > 1) cost += split_cost + (double)M * N * s * 8.0 / 6.4e12 / 290e-9;
+        if (!fits) cost = 1e30;
         if (cost < best - 1e-9 || (cost < best + 1e-9 && bc > *bn)) {
           best = cost;
           *bn = bc;
           *splits = s;
           *pair = pr;
+          *cs = 0;
+        }
+        // the same split as a cluster split-K: one tile per cluster at a time, partials exchanged on chip
+        if (!pr && s > 1 && s <= kMaxClusterSplit && allow_cs) {
+          const int ncl = max_clusters(c, s);
+          const long long tiles = (long long)mtiles * nt;
+          const long long crounds = (tiles + ncl - 1) / ncl;
+          const double ccost = (double)crounds * (per * kb_cost + 8.0 + cs_cost * (bc / 64.0)) + 4.0;
+          if (ccost < best - 1e-9 || (ccost < best + 1e-9 && bc > *bn)) {
+            best = ccost;
+            *bn = bc;
+            *splits = s;
+            *pair = 0;
+            *cs = s;
+          }
         }
       }
     }
@@ -985,9 +1135,9 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
 }
 
 int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
-  int bn, s, pr;
-  choose_tiling(c, M, N, K / 64, geglu, &bn, &s, &pr);
-  return s > 1 ? 2 : 1;
+  int bn, s, pr, cs;
+  choose_tiling(c, M, N, K / 64, geglu, &bn, &s, &pr, &cs);
+  return (s > 1 && !cs) ? 2 : 1;
 }
 
 template <bool XF>
@@ -1012,7 +1162,7 @@ static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool
   return p.gn_tab ? dispatch_xf<true>(c, p, bn, bf16, pair) : dispatch_xf<false>(c, p, bn, bf16, pair);
 }
 
-int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, void* splitk_ws) {
+int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, int cs, void* splitk_ws) {
   p.err = c->d_err;
   p.gstats = nullptr;
   if (c->gn_stats) {
@@ -1028,6 +1178,12 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
   p.splits = std::max(1, splits);
   p.m_tiles = pair ? (p.M + 2 * BM - 1) / (2 * BM) : (p.M + BM - 1) / BM;
   p.n_tiles = p.geglu ? p.N / bn : (p.N + bn - 1) / bn;
+  p.cs = 0;
+  if (p.splits > 1 && cs && !pair && !p.geglu && !p.gstats && !p.gn_tab && p.splits <= kMaxClusterSplit) {
+    p.cs = p.splits;  // partials summed on chip by the cluster, epilogue in the same kernel
+    p.staged = 0;
+    return dispatch_variant(c, p, bn, bf16, false);
+  }
   if (p.splits > 1) {
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
     if (need > kSplitKWsBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
@@ -1160,10 +1316,10 @@ int gemm_linear(Ctx* c, int dtype, const void* X1, int K1, const void* X2, int M
     p.gn_HW = gnf_hw;
   }
   int chosen, splits;
-  int pair;
-  choose_tiling(c, M, N, p.num_k, geglu, &chosen, &splits, &pair);
+  int pair, cs;
+  choose_tiling(c, M, N, p.num_k, geglu, &chosen, &splits, &pair, &cs);
   if (!tmap_kmajor(&p.tmB, dtype, W, N, K, K, pair ? chosen / 2 : chosen, &err)) return set_error(c, DI_EINVAL, err);
-  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, pair, splitk_ws);
+  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, pair, cs, splitk_ws);
 }
 
 int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int H, int W, int stride,
@@ -1222,11 +1378,12 @@ int gemm_conv3x3(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int 
     p.conv_bh = (int)bh;
   }
   int chosen, splits;
-  int pair;
-  choose_tiling(c, p.M, Co, p.num_k, 0, &chosen, &splits, &pair);
+  int pair, cs;
+  choose_tiling(c, p.M, Co, p.num_k, 0, &chosen, &splits, &pair, &cs);
   if (!tmap_kmajor(&p.tmB, dtype, Wt, Co, 9 * Cin, 9 * Cin, pair ? chosen / 2 : chosen, &err))
     return set_error(c, DI_EINVAL, err);
-  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, pair, splitk_ws);
+  if (p.gn_tab) cs = 0;  // the fused-GroupNorm transform keeps its table in the epilogue slabs
+  return launch_gemm(c, p, dtype == DI_BF16, chosen, splits, pair, cs, splitk_ws);
 }
 
 // Weight repack: [Co][Ci][3][3] fp32 -> [Co][3][3][Ci] fp16/bf16.

@@ -10,8 +10,9 @@
 //
 // Host code cannot use the array's name as a device address (on the host it is only a stand-in), so
 // the device address is looked up once per device with cudaGetSymbolAddress and passed to the kernels.
-// Under CUDA's lazy module loading that first lookup (and the kernels' first launch) may load the
-// library's device code, which allocates: callers make one call per device at start-up.
+// Under CUDA's lazy module loading that first lookup may load the library's device code, which
+// allocates; the same set-up also loads the GroupNorm kernels, so only the first call on a device can
+// allocate: callers make it at start-up.
 #include <mutex>
 
 #include "di_common.cuh"
@@ -22,6 +23,7 @@ int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1,
                     int HW, int G, float eps, const float* gamma, const float* beta, int silu, void* y,
                     void* partial_ws);
 size_t gn_nhwc_ws_bytes(int N, int HW, int G);
+int gn_nhwc_preload(Ctx* c);
 
 namespace {
 
@@ -43,9 +45,12 @@ int scratch_address(Ctx* c, void** out) {
     cudaSetDevice(c->device);
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_gn_scratch);
+    // load the GroupNorm kernels now too, so that no later call loads code (and allocates) on this device
+    const int pl = e == cudaSuccess ? gn_nhwc_preload(c) : DI_OK;
     cudaSetDevice(prev);
     if (e != cudaSuccess || !p)
       return set_error(c, DI_ECUDA, std::string("noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    if (pl) return pl;
     g_scratch_addr[c->device] = p;
   }
   *out = g_scratch_addr[c->device];

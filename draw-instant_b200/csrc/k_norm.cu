@@ -707,6 +707,18 @@ int group_norm_nhwc(Ctx* c, int in_dtype, int out_dtype, const void* x1, int C1,
   return set_error(c, DI_EINVAL, "group_norm_nhwc: dtype combination");
 }
 
+// Loads the device code of the kernels group_norm_nhwc runs for fp16 and bf16 (under CUDA's lazy module
+// loading a kernel is otherwise loaded, and its memory allocated, at its first launch).
+int gn_nhwc_preload(Ctx* c) {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, gn_nhwc_partial<__half>) != cudaSuccess ||
+      cudaFuncGetAttributes(&a, gn_nhwc_partial<__nv_bfloat16>) != cudaSuccess ||
+      cudaFuncGetAttributes(&a, gn_nhwc_apply<__half, __half>) != cudaSuccess ||
+      cudaFuncGetAttributes(&a, gn_nhwc_apply<__nv_bfloat16, __nv_bfloat16>) != cudaSuccess)
+    return set_error(c, DI_ECUDA, "group_norm_nhwc: loading the kernels failed");
+  return DI_OK;
+}
+
 // Statistics of concat(x1, x2) -> table[N][C] of (scale, shift) for an operand-fused GroupNorm.
 int gn_table_nhwc(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G, float eps,
                   const float* gamma, const float* beta, float2* table) {

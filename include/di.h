@@ -147,8 +147,8 @@ DI_API int di_group_norm_nhwc(di_ctx_t ctx, int dtype, const void* x1, int C1, c
  * reference.  Its scratch is a fixed 1 MiB array inside the library (kept on every GPU that loads the
  * library until the process exits): sizes needing more than N * max(1, min(16, HW/256)) * G * 8 =
  * 1 MiB are rejected with DI_EINVAL.  The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress); under CUDA's lazy module loading that lookup, and the first launch of the
- * GroupNorm kernels, may load the library's device code, which allocates.  So make one call per device
+ * (cudaGetSymbolAddress) and loads the GroupNorm kernels' device code; under CUDA's lazy module loading
+ * that may allocate.  So make one call per device
  * at start-up, before any stream capture and before the no-allocation period begins; later calls
  * allocate nothing.  The looked-up address is forgotten when a context on that device is destroyed
  * (di_destroy) and looked up again by the next call; do not call it across a device reset without
