@@ -57,6 +57,7 @@ struct GemmParams {
   // split r of the cluster's tiles, and the cluster sums its partials through distributed shared memory in
   // the epilogue (fixed rank order), so no fp32 partials reach global memory and no reduce kernel runs.
   int cs;
+  int dbg;  // diagnostics (DI_GEMM_DEBUG): 1 skip output / partial stores, 2 skip the bias/residual epilogue
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
   long long* gstats;  // GroupNorm(32) statistics of the fp16 output (Ctx::gn_stats), or null
@@ -781,27 +782,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
               }
             }
           } else {
-            if (tr && lt == 0 && threadIdx.x == 64 && c < 2) tr[8 + 2 * c] = globaltimer();
+            if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[8] = globaltimer();
             tmem_ld32(trow + c * 32, r);
             tmem_wait_ld();
-            if (tr && lt == 0 && threadIdx.x == 64 && c < 2) tr[9 + 2 * c] = globaltimer();
+            if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[9] = globaltimer();
             nb = n0 + c * 32;
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            if (!split && nb < n_out && m < p.M) epi(v, nb, m);
+            if (!split && nb < n_out && m < p.M && !(p.dbg & 2)) epi(v, nb, m);
+            if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[10] = globaltimer();
           }
         }
         if (p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
         if (!ok || nb >= n_out) continue;  // warp-uniform
         if (!split) {
-          store_chunk(v, nb, m0, m, sp, false, p.staged);
+          if (!(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, false, p.staged);
+          if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[11] = globaltimer();
+          if (tr && lt == 0 && threadIdx.x == 64 && c == half + 2) tr[12] = globaltimer();
           continue;
         }
         if (CS) {
+          if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[13] = globaltimer();
           if (xok) xok = cs_reduce(v, nb, m0, n_out);
+          if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[14] = globaltimer();
           continue;
         }
-        store_chunk(v, nb, m0, m, sp, true, p.staged);  // fp32 partials: the reduce kernel finishes them
+        if (!(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, true, p.staged);  // fp32 partials: the reduce kernel finishes them
+        if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[11] = globaltimer();
+        if (tr && lt == 0 && threadIdx.x == 64 && c == half + 2) tr[12] = globaltimer();
       }
       tc_fence_before();
       __syncwarp();
@@ -1033,10 +1041,10 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
   *cs = 0;
   // Cluster split-K (partials summed through distributed shared memory, no reduce launch): not for GEGLU
   // (value and gate columns sit in different chunks) nor with epilogue GroupNorm statistics.
-  // DI_CLUSTER_SPLIT=0 switches it off (diagnostics).
+  // Opt-in (DI_CLUSTER_SPLIT=1): measured slower than the reduce kernel in the U-Net step so far.
   static const int cs_ok = [] {
     const char* e = getenv("DI_CLUSTER_SPLIT");
-    return (e && e[0] == '0') ? 0 : 1;
+    return (e && e[0] == '1') ? 1 : 0;
   }();
   static const double cs_cost = [] {  // exchange cost per 32-column chunk round, in K-block units
     const char* e = getenv("DI_CLUSTER_SPLIT_COST");
@@ -1175,6 +1183,12 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
   }
   p.staged = (p.vec_ok && splits <= 1) ? 1 : 0;
   p.b_early = c->weights_const ? 1 : 0;
+  static const int dbg = [] {
+    const char* e = getenv("DI_GEMM_DEBUG");
+    return e ? atoi(e) : 0;
+  }();
+  p.dbg = dbg;
+  if (dbg & 4) p.staged = 0;
   p.splits = std::max(1, splits);
   p.m_tiles = pair ? (p.M + 2 * BM - 1) / (2 * BM) : (p.M + BM - 1) / BM;
   p.n_tiles = p.geglu ? p.N / bn : (p.N + bn - 1) / bn;
