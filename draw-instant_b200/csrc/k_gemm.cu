@@ -75,6 +75,10 @@ struct GemmParams {
 constexpr int kTracePoints = 16;
 static unsigned long long* g_trace = nullptr;
 static int g_trace_ctas = 0;
+static const bool g_gemm_generic = [] {  // diagnostics: DI_GEMM_GENERIC=1 never uses the plain epilogue
+  const char* e = getenv("DI_GEMM_GENERIC");
+  return e && e[0] == '1';
+}();
 
 namespace {
 
@@ -206,7 +210,9 @@ __device__ __forceinline__ void gn_stats_chunk(const float (&v)[32], int nb, int
   }
 }
 
-template <int BN, int STAGES, bool BF16, bool PAIR = false, bool XF = false>
+// MODE: 0 generic epilogue (every runtime variant), 1 operand-fused GroupNorm (XF), 2 plain epilogue: 16-bit
+// output through the staging slab, no split-K, GEGLU, statistics or fp32 operands (compiled without them).
+template <int BN, int STAGES, bool BF16, bool PAIR = false, int MODE = 0>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmSmem<BN, STAGES, PAIR>;
   constexpr uint32_t STAGE_TX = S::A_BYTES + S::B_BYTES;
@@ -231,7 +237,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0 = leader
   // Cluster split-K: rank csr runs split csr of tiles cluster, cluster + clusters, ... (units
   // csr * per_split + tile), so every CTA of a cluster walks the same tiles in the same order.
-  const int CS = PAIR ? 0 : p.cs;  // cluster size of the split-K cluster, 0 = off
+  const int CS = (PAIR || MODE == 2) ? 0 : p.cs;  // cluster size of the split-K cluster, 0 = off
   const int csr = CS ? (int)cluster_ctarank() : 0;
   const int cta0 = PAIR ? blockIdx.x >> 1 : (CS ? csr * p.m_tiles * p.n_tiles + (int)blockIdx.x / CS : blockIdx.x);
   const int cstride = PAIR ? gridDim.x >> 1 : (CS ? (int)gridDim.x / CS : gridDim.x);
@@ -265,7 +271,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   const uint32_t full0_leader = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
   const uint32_t tempty_leader = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
   const uint32_t aready_leader = PAIR ? mapa_shared(smem_u32(aready), 0) : smem_u32(aready);
-  constexpr bool xform = XF;  // operand-fused GroupNorm (p.gn_tab): a separate instantiation
+  constexpr bool xform = MODE == 1;  // operand-fused GroupNorm (p.gn_tab): a separate instantiation
+  constexpr bool PLAIN = MODE == 2;
+  const int out_f32 = PLAIN ? 0 : p.out_f32, res_f32 = PLAIN ? 0 : p.res_f32, vec_ok = PLAIN ? 1 : p.vec_ok;
+  const int staged = PLAIN ? 1 : p.staged;
   const uint32_t tmem = *tmem_slot;
   if (tr && threadIdx.x == 0) tr[1] = globaltimer();
   // Programmatic dependent launch: let the next kernel be scheduled right away.  Everything before
@@ -427,7 +436,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       const int n_out = p.N;
       const bool full = nb + 32 <= n_out;
       if (p.bias) {
-        if (full) {
+        if (PLAIN && full) {  // one coalesced load, broadcast by shuffles
+          const float bl = __ldg(p.bias + nb + lane);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
+        } else if (full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
         } else {
@@ -455,15 +468,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
       }
       if (p.residual) {
-        if (full && p.vec_ok) {
+        if (full && vec_ok) {
           float rr[32];
-          load_row32(p.residual, (size_t)m * p.ldr + nb, rr, p.res_f32, BF16);
+          load_row32(p.residual, (size_t)m * p.ldr + nb, rr, res_f32, BF16);
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += rr[j];
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (nb + j < n_out) v[j] += load_one(p.residual, (size_t)m * p.ldr + nb + j, p.res_f32, BF16);
+            if (nb + j < n_out) v[j] += load_one(p.residual, (size_t)m * p.ldr + nb + j, res_f32, BF16);
         }
       }
     };
@@ -476,7 +489,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         // per lane), then is read back so that each store instruction writes whole 64/128-byte row
         // segments of 8 or 4 rows (coalesced), instead of 32 rows 16 bytes at a time.
         __syncwarp();  // the previous chunk's read-back is done
-        if (to_partial || p.out_f32) {
+        if (to_partial || out_f32) {
           // 32 fp32 per row = 128 B; 16-byte chunk j of row r at j ^ (r & 7)
           float4* rp = reinterpret_cast<float4*>(stg + lane * 128);
 #pragma unroll
@@ -504,7 +517,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         }
         __syncwarp();
         const int mrow0 = m0 + q * 32;
-        if (to_partial || p.out_f32) {
+        if (to_partial || out_f32) {
           float* base = to_partial ? p.partial + (size_t)sp * p.M * p.N : static_cast<float*>(p.out);
           const int ld = to_partial ? p.N : p.ldo;
 #pragma unroll
@@ -546,12 +559,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (nb + j < p.N) dst[j] = v[j];
-        } else if (p.vec_ok && nb + 32 <= n_out) {
-          store_row32(p.out, (size_t)m * p.ldo + nb, v, p.out_f32, BF16);
+        } else if (vec_ok && nb + 32 <= n_out) {
+          store_row32(p.out, (size_t)m * p.ldo + nb, v, out_f32, BF16);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (nb + j < n_out) store_one(p.out, (size_t)m * p.ldo + nb + j, v[j], p.out_f32, BF16);
+            if (nb + j < n_out) store_one(p.out, (size_t)m * p.ldo + nb + j, v[j], out_f32, BF16);
         }
       }
     };
@@ -753,8 +766,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       if (tr && lt == 0 && threadIdx.x == 64) tr[5] = globaltimer();
       tc_fence_after();
       const uint32_t trow = tmem + ab * BN + (static_cast<uint32_t>(q * 32) << 16);
-      const bool split = p.splits > 1;
-      const bool gg = p.geglu && !split;  // split-K stores raw packed partials; the reduce applies GEGLU
+      const bool split = !PLAIN && p.splits > 1;
+      const bool gg = !PLAIN && p.geglu && !split;  // split-K stores raw packed partials; the reduce applies GEGLU
       bool xok = true;  // cluster split-K exchange still in step with the peers
       const int nchunks = gg ? BN / 64 : BN / 32;
       const int n_out = gg ? p.N / 2 : p.N;
@@ -789,14 +802,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             nb = n0 + c * 32;
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            if (!split && nb < n_out && m < p.M && !(p.dbg & 2)) epi(v, nb, m);
+            if (!split && nb < n_out && m < p.M && (PLAIN || !(p.dbg & 2))) epi(v, nb, m);
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[10] = globaltimer();
           }
         }
-        if (p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
+        if (!PLAIN && p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
         if (!ok || nb >= n_out) continue;  // warp-uniform
         if (!split) {
-          if (!(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, false, p.staged);
+          if (PLAIN || !(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, false, staged);
           if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[11] = globaltimer();
           if (tr && lt == 0 && threadIdx.x == 64 && c == half + 2) tr[12] = globaltimer();
           continue;
@@ -813,7 +826,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader + ab * 8);
+      if (lane == 0) {  // CTA-scope arrive unless the pair leader's barrier is remote
+        if (PAIR) mbar_arrive_cluster(tempty_leader + ab * 8);
+        else mbar_arrive(&tempty[ab]);
+      }
       if (tr && lt == 0 && threadIdx.x == 64) tr[6] = globaltimer();
       if (!ok || !xok) break;
     }
@@ -839,7 +855,7 @@ static int max_clusters(Ctx* c, int n) {
   int& mc = g_max_clusters[c->device & 31][n];
   if (mc) return mc;
   using S = GemmSmem<128, 6, false>;
-  auto kern = gemm_tc_kernel<128, 6, false, false, false>;
+  auto kern = gemm_tc_kernel<128, 6, false, false, 0>;
   mc = std::max(1, c->num_sms / (2 * n));  // conservative if the query fails
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
@@ -860,7 +876,7 @@ static int max_clusters(Ctx* c, int n) {
   return mc;
 }
 
-template <int BN, int STAGES, bool BF16, bool PAIR, bool XF>
+template <int BN, int STAGES, bool BF16, bool PAIR, int XF>
 int launch_variant(Ctx* c, const GemmParams& p) {
   using S = GemmSmem<BN, STAGES, PAIR>;
   auto kern = gemm_tc_kernel<BN, STAGES, BF16, PAIR, XF>;
@@ -895,7 +911,7 @@ static int max_pairs(Ctx* c) {
   int& mp = g_max_pairs[c->device & 31];
   if (mp) return mp;
   using S = GemmSmem<256, 6, true>;
-  auto kern = gemm_tc_kernel<256, 6, false, true, false>;
+  auto kern = gemm_tc_kernel<256, 6, false, true, 0>;
   mp = c->num_sms / 2;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
@@ -1148,7 +1164,7 @@ int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
   return (s > 1 && !cs) ? 2 : 1;
 }
 
-template <bool XF>
+template <int XF>
 static int dispatch_xf(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
   if (pair) {
     switch (bn) {
@@ -1167,7 +1183,10 @@ static int dispatch_xf(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair
 }
 
 static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
-  return p.gn_tab ? dispatch_xf<true>(c, p, bn, bf16, pair) : dispatch_xf<false>(c, p, bn, bf16, pair);
+  if (p.gn_tab) return dispatch_xf<1>(c, p, bn, bf16, pair);
+  const bool plain = !p.geglu && p.splits <= 1 && !p.gstats && !p.out_f32 && !p.res_f32 && p.staged && !p.cs &&
+                     !p.dbg && !g_gemm_generic;
+  return plain ? dispatch_xf<2>(c, p, bn, bf16, pair) : dispatch_xf<0>(c, p, bn, bf16, pair);
 }
 
 int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, int cs, void* splitk_ws) {

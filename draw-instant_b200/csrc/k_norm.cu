@@ -473,6 +473,119 @@ __global__ void __launch_bounds__(512) gn_nhwc_grid(const T* __restrict__ x1, in
   }
 }
 
+// Single-launch GroupNorm(+SiLU) of concat(x1, x2) for maps whose per-image slice fits one cluster:
+// grid (kGnCluster, N), clusters of kGnCluster CTAs, one cluster per image.  CTA rank k owns pixels
+// [k * per, min(HW, (k + 1) * per)):
+//   1. one bulk copy per input brings the slice (contiguous in NHWC) into shared memory;
+//   2. per-channel sums and sums of squares (fp32, one 8-channel vector per thread) fold to per-group
+//      sums in this CTA's shared memory;
+//   3. after a cluster barrier every CTA reads all ranks' group sums through distributed shared memory,
+//      in rank order (the same arithmetic in every CTA: deterministic), to mean / rstd; a second cluster
+//      barrier lets the ranks' shared memory go;
+//   4. the slice is normalised from shared memory and written once.
+// One read and one write of the map in one launch, with no grid-wide barrier and no global scratch; only
+// kGnCluster SMs per image are held, so the consumer's CTAs start on the others.
+constexpr int kGnCluster = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(1024) gn_nhwc_cluster(const T* __restrict__ x1, int C1, const T* __restrict__ x2,
+                                                        int C2, int HW, int per, int G, float eps,
+                                                        const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, int silu, T* __restrict__ y,
+                                                        int* err) {
+  extern __shared__ __align__(16) uint8_t csm[];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ float s_grp[2 * 128];
+  __shared__ float s_mean[128], s_rstd[128];
+  const int C = C1 + C2, V = blockDim.x, R = blockDim.y;
+  const int n = blockIdx.y, k = (int)cluster_ctarank();
+  const int v = threadIdx.x, r = threadIdx.y, tid = r * V + v, nthr = V * R;
+  const int p0 = k * per, cnt = max(0, min(HW, p0 + per) - p0);
+  uint8_t* s1 = csm;                                                         // [cnt][C1]
+  uint8_t* s2 = csm + (size_t)per * C1 * sizeof(T);                          // [cnt][C2]
+  float* ssum = reinterpret_cast<float*>(csm + (size_t)per * C * sizeof(T));  // [R][C]
+  float* ssq = ssum + R * C;                                                  // [R][C]
+  if (tid == 0) {
+    mbar_init(&mbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // x1 / x2 are written by the previous kernel
+  if (tid == 0) {
+    const uint32_t b1 = (uint32_t)((size_t)cnt * C1 * sizeof(T)), b2 = (uint32_t)((size_t)cnt * C2 * sizeof(T));
+    mbar_arrive_expect_tx(&mbar, b1 + b2);
+    if (b1) bulk_load(s1, x1 + ((size_t)n * HW + p0) * C1, b1, &mbar);
+    if (b2) bulk_load(s2, x2 + ((size_t)n * HW + p0) * C2, b2, &mbar);
+  }
+  const bool landed = mbar_wait(&mbar, 0, err, DEVERR_WAIT_EPI);
+  const int c = v * 8;
+  const uint8_t* src = c < C1 ? s1 + (size_t)c * sizeof(T) : s2 + (size_t)(c - C1) * sizeof(T);
+  const size_t row_bytes = (c < C1 ? C1 : C2) * sizeof(T);
+  {
+    float s[8], q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { s[j] = 0.f; q[j] = 0.f; }
+    for (int p = r; landed && p < cnt; p += R) {
+      float f[8];
+      load8<T>(reinterpret_cast<const T*>(src + p * row_bytes), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { s[j] += f[j]; q[j] += f[j] * f[j]; }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { ssum[r * C + c + j] = s[j]; ssq[r * C + c + j] = q[j]; }
+  }
+  __syncthreads();
+  for (int cc = tid; cc < C; cc += nthr) {  // fold the R rows per channel (fixed order)
+    float s = 0.f, q = 0.f;
+    for (int rr = 0; rr < R; ++rr) { s += ssum[rr * C + cc]; q += ssq[rr * C + cc]; }
+    ssum[cc] = s;
+    ssq[cc] = q;
+  }
+  __syncthreads();
+  const int cpg = C / G;
+  for (int g = tid; g < G; g += nthr) {
+    float s = 0.f, q = 0.f;
+    for (int cc = g * cpg; cc < (g + 1) * cpg; ++cc) { s += ssum[cc]; q += ssq[cc]; }
+    s_grp[2 * g] = s;
+    s_grp[2 * g + 1] = q;
+  }
+  cluster_sync();  // every rank's group sums are in its shared memory
+  const uint32_t base_addr = smem_u32(s_grp);
+  for (int g = tid; g < G; g += nthr) {
+    float s = 0.f, q = 0.f;
+    for (int kk = 0; kk < kGnCluster; ++kk) {
+      const uint32_t a = mapa_shared(base_addr, (uint32_t)kk) + 8u * g;
+      s += ld_dsmem_f32(a);
+      q += ld_dsmem_f32(a + 4);
+    }
+    const float cntf = (float)cpg * (float)HW;
+    const float mean = s / cntf;
+    const float var = fmaxf(q / cntf - mean * mean, 0.0f);
+    s_mean[g] = mean;
+    s_rstd[g] = 1.0f / sqrtf(var + eps);
+  }
+  cluster_sync();  // all ranks have read every rank's sums (and s_mean / s_rstd are visible in the CTA)
+  float sc[8], sh[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int g = (c + j) / cpg;
+    sc[j] = s_rstd[g] * __ldg(gamma + c + j);
+    sh[j] = __ldg(beta + c + j) - s_mean[g] * sc[j];
+  }
+  T* yo = y + ((size_t)n * HW + p0) * C + c;
+  for (int p = r; landed && p < cnt; p += R) {
+    float f[8];
+    load8<T>(reinterpret_cast<const T*>(src + p * row_bytes), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a = fmaf(f[j], sc[j], sh[j]);
+      f[j] = silu ? __fdividef(a, 1.0f + __expf(-a)) : a;
+    }
+    store8<T>(yo + (size_t)p * C, f);
+  }
+}
+
 // Normalise pass.  Block = V threads (one 8-channel vector each) x R pixel rows, so every thread keeps
 // the same 8 channels for the whole grid and applies them as one FMA per element with per-thread
 // scale / shift (gamma * rstd, beta - mean * gamma * rstd); two pixels per thread per round.
@@ -873,6 +986,57 @@ int gn_nhwc_grid_launch(Ctx* c, int dtype, const void* x1, int C1, const void* x
   return rc ? rc : 0;
 }
 
+// The cluster GroupNorm's geometry: pixels per CTA, pixel rows per block and dynamic shared memory.
+static bool gn_cluster_geometry(int HW, int C1, int C2, int G, int* per, int* R, size_t* smem) {
+  const int C = C1 + C2;
+  if (HW <= 0 || C % 8 || C1 % 8 || C2 % 8 || G <= 0 || G > 128 || C % G || C / 8 > 1024) return false;
+  *per = (HW + kGnCluster - 1) / kGnCluster;
+  *R = std::max(1, 256 / (C / 8));
+  *smem = (size_t)*per * C * 2 + 2 * sizeof(float) * (size_t)*R * C;
+  // every per-CTA bulk copy starts on a 16-byte boundary: per * C1 * 2 and per * C2 * 2 are multiples of 16
+  return *smem <= (200u << 10);
+}
+
+bool gn_cluster_usable(int dtype, int HW, int C1, int C2, int G) {
+  if (dtype != DI_F16 && dtype != DI_BF16) return false;
+  static const bool off = [] {  // diagnostics: DI_GN_CLUSTER=0 keeps the two-launch path
+    const char* e = getenv("DI_GN_CLUSTER");
+    return e && e[0] == '0';
+  }();
+  int per, R;
+  size_t smem;
+  return !off && gn_cluster_geometry(HW, C1, C2, G, &per, &R, &smem);
+}
+
+// Returns 1 (nothing launched) when the shape does not fit the cluster path.
+int gn_nhwc_cluster_launch(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                           float eps, const float* gamma, const float* beta, int silu, void* y) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (N <= 0 || !al(x1) || (C2 && !al(x2)) || !al(y) || !gn_cluster_usable(dtype, HW, C1, C2, G)) return 1;
+  int per, R;
+  size_t smem;
+  gn_cluster_geometry(HW, C1, C2, G, &per, &R, &smem);
+  static unsigned attr_done[2] = {0, 0};  // per dtype, per-device bit
+  const int di = dtype == DI_BF16 ? 1 : 0;
+  if (!(attr_done[di] & (1u << (c->device & 31)))) {
+    const void* kern = dtype == DI_BF16 ? (const void*)gn_nhwc_cluster<__nv_bfloat16> : (const void*)gn_nhwc_cluster<__half>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 << 10) != cudaSuccess)
+      return set_error(c, DI_ECUDA, "gn_nhwc_cluster: kernel attributes");
+    attr_done[di] |= 1u << (c->device & 31);
+  }
+  const dim3 grid(kGnCluster, N), block((C1 + C2) / 8, R);
+  if (dtype == DI_BF16)
+    launch_k_cluster(gn_nhwc_cluster<__nv_bfloat16>, grid, block, smem, c->stream, kGnCluster,
+                     static_cast<const __nv_bfloat16*>(x1), C1, static_cast<const __nv_bfloat16*>(x2), C2, HW, per, G,
+                     eps, gamma, beta, silu, static_cast<__nv_bfloat16*>(y), c->d_err);
+  else
+    launch_k_cluster(gn_nhwc_cluster<__half>, grid, block, smem, c->stream, kGnCluster, static_cast<const __half*>(x1),
+                     C1, static_cast<const __half*>(x2), C2, HW, per, G, eps, gamma, beta, silu,
+                     static_cast<__half*>(y), c->d_err);
+  return check_launch(c, "gn_nhwc_cluster");
+}
+
 size_t gn_nhwc_ws_bytes(int N, int HW, int G) {
   int chunks, cl;
   gn_geometry(HW, &chunks, &cl);
@@ -960,6 +1124,11 @@ int di_group_norm_nhwc(di_ctx_t h, int dtype, const void* x1, int C1, const void
     const int r = gn_nhwc_grid_launch(c, dtype, x1, C1, x2, C2, N, HW, G, eps, gamma, beta, fuse_silu, y, part,
                                       c->gn_bar);
     if (r <= 0) return r;  // launched (0) or failed; 1: not applicable, two-launch path below
+  }
+  // Maps whose per-image slice fits one 16-CTA cluster's shared memory: one launch, one read, one write.
+  {
+    const int r = gn_nhwc_cluster_launch(c, dtype, x1, C1, x2, C2, N, HW, G, eps, gamma, beta, fuse_silu, y);
+    if (r <= 0) return r;
   }
   return group_norm_nhwc(c, dtype, dtype, x1, C1, x2, C2, N, HW, G, eps, gamma, beta, fuse_silu, y, nullptr);
 }

@@ -48,6 +48,9 @@ size_t gn_grid_ws_bytes(Ctx* c, int N, int HW, int C, int G);
 int gn_nhwc_grid_launch(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
                         float eps, const float* gamma, const float* beta, int silu, void* y, float2* partial,
                         unsigned* bar);
+bool gn_cluster_usable(int dtype, int HW, int C1, int C2, int G);
+int gn_nhwc_cluster_launch(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G,
+                           float eps, const float* gamma, const float* beta, int silu, void* y);
 int gn_apply_with_stats(Ctx* c, const void* x, int C, int N, int HW, const long long* stats, float eps,
                         const float* gamma, const float* beta, int silu, void* y);
 int gn_table_nhwc(Ctx* c, int dtype, const void* x1, int C1, const void* x2, int C2, int N, int HW, int G, float eps,
@@ -835,6 +838,18 @@ struct Plan {
     const float* g = vec(pre + ".weight", C, 1, 1);
     const float* b = vec(pre + ".bias", C, 2, 1);
     void* y = tmp((size_t)x1.N * HW * C * 2);
+    if (gn_cluster_usable(DI_F16, HW, x1.C, x2 ? x2->C : 0, 32)) {
+      // one launch per image cluster: slice in shared memory, statistics folded through DSMEM
+      Ctx* cc = c;
+      const Act a = x1;
+      const void* p2 = x2 ? x2->p : nullptr;
+      const int C2 = x2 ? x2->C : 0;
+      record([=] {
+        const int r = gn_nhwc_cluster_launch(cc, DI_F16, a.p, a.C, p2, C2, a.N, HW, 32, eps, g, b, silu, y);
+        return r == 1 ? set_error(cc, DI_EUNSUPPORTED, "gn_nhwc_cluster: shape or alignment no longer accepted") : r;
+      }, 2, 0, 2.0 * x1.N * HW * C * 2, 1);
+      return GnOp{y, C, nullptr, 0, nullptr, 0};
+    }
     if (gn_grid_usable(c, DI_F16, x1.N, HW, x1.C, x2 ? x2->C : 0, 32)) {
       // one launch: statistics, grid barrier and normalise (gn_nhwc_grid; opt-in, DI_GN_GRID=1)
       float2* part = static_cast<float2*>(tmp(gn_grid_ws_bytes(c, x1.N, HW, C, 32)));
