@@ -436,10 +436,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       const int n_out = p.N;
       const bool full = nb + 32 <= n_out;
       if (p.bias) {
-        if (PLAIN && full) {  // one coalesced load, broadcast by shuffles
-          const float bl = __ldg(p.bias + nb + lane);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
+        if (PLAIN && full) {
+          // added by the caller on all 32 lanes (a full-warp shuffle; rows past M skip this function)
         } else if (full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
@@ -802,6 +800,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             nb = n0 + c * 32;
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (PLAIN && p.bias && nb + 32 <= n_out) {  // one coalesced load, broadcast by full-warp shuffles
+              const float bl = __ldg(p.bias + nb + lane);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
+            }
             if (!split && nb < n_out && m < p.M && (PLAIN || !(p.dbg & 2))) epi(v, nb, m);
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[10] = globaltimer();
           }
