@@ -436,9 +436,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       const int n_out = p.N;
       const bool full = nb + 32 <= n_out;
       if (p.bias) {
-        if (PLAIN && full) {
-          // added by the caller on all 32 lanes (a full-warp shuffle; rows past M skip this function)
-        } else if (full) {
+        if (full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + nb + j);
         } else {
@@ -759,6 +757,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           if (tr && lt == 0 && threadIdx.x == 64 && kb == kb1 - 1) tr[11] = globaltimer();
         }
       }
+      // Plain epilogue: the operands that do not depend on the accumulator are fetched one chunk ahead on all
+      // 32 lanes (the first chunk's before the accumulator wait, i.e. during the main loop): lane j holds
+      // column j's bias and row-vector values (broadcast later by full-warp shuffles), each lane its own
+      // row's 32 residual values.  A chunk takes this path when it is whole and its 32 rows share one image.
+      float pf_b = 0.f, pf_r = 0.f;
+      uint4 pf_res[4] = {};
+      auto pf_fast = [&](int c) {
+        return PLAIN && n0 + c * 32 + 32 <= p.N && (!p.rowvec || p.rowvec_div % 32 == 0);
+      };
+      auto pf_fetch = [&](int c) {
+        const int nbc = n0 + c * 32;
+        if (p.bias) pf_b = __ldg(p.bias + nbc + lane);
+        if (p.rowvec && m0 + q * 32 < p.M)
+          pf_r = __ldg(p.rowvec + (size_t)((m0 + q * 32) / p.rowvec_div) * p.rowvec_ld + nbc + lane);
+        if (p.residual && m < p.M) {
+          const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.residual) + (size_t)m * p.ldr + nbc);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) pf_res[j] = __ldg(src + j);
+        }
+      };
+      if (PLAIN && pf_fast(half)) pf_fetch(half);
       const bool okw = mbar_wait<PAIR>(&tfull[ab], (lt >> 1) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
       const bool ok = __all_sync(0xffffffffu, okw);
       if (tr && lt == 0 && threadIdx.x == 64) tr[5] = globaltimer();
@@ -794,18 +813,52 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             }
           } else {
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[8] = globaltimer();
+            const bool fastc = pf_fast(c);
+            const float cb = pf_b, cr = pf_r;
+            uint4 cres[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) cres[j] = pf_res[j];
+            if (PLAIN && c + kEpiWarps / 4 < nchunks && pf_fast(c + kEpiWarps / 4)) pf_fetch(c + kEpiWarps / 4);
             tmem_ld32(trow + c * 32, r);
             tmem_wait_ld();
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[9] = globaltimer();
             nb = n0 + c * 32;
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            if (PLAIN && p.bias && nb + 32 <= n_out) {  // one coalesced load, broadcast by full-warp shuffles
-              const float bl = __ldg(p.bias + nb + lane);
+            if (PLAIN && fastc) {  // warp-uniform: the shuffles run on all 32 lanes
+              if (p.bias) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, bl, j);
+                for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, cb, j);
+              }
+              if (p.rowvec) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, cr, j);
+              }
+              if (p.act == 1) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+              } else if (p.act == 2) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+              }
+              if (p.residual) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t w[4] = {cres[j].x, cres[j].y, cres[j].z, cres[j].w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    uint32_t we = w[e];
+                    float2 f;
+                    if (BF16) f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&we));
+                    else f = __half22float2(*reinterpret_cast<__half2*>(&we));
+                    v[8 * j + 2 * e] += f.x;
+                    v[8 * j + 2 * e + 1] += f.y;
+                  }
+                }
+              }
+            } else if (!split && nb < n_out && m < p.M && (PLAIN || !(p.dbg & 2))) {
+              epi(v, nb, m);
             }
-            if (!split && nb < n_out && m < p.M && (PLAIN || !(p.dbg & 2))) epi(v, nb, m);
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[10] = globaltimer();
           }
         }
