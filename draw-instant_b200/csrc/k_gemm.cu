@@ -211,7 +211,8 @@ __device__ __forceinline__ void gn_stats_chunk(const float (&v)[32], int nb, int
 }
 
 // MODE: 0 generic epilogue (every runtime variant), 1 operand-fused GroupNorm (XF), 2 plain epilogue: 16-bit
-// output through the staging slab, no split-K, GEGLU, statistics or fp32 operands (compiled without them).
+// output through the staging slab, no split-K, GEGLU, statistics or fp32 operands (compiled without them);
+// 3 split-K partials: raw fp32 partial stores only (no epilogue arithmetic, no GEGLU / statistics / cluster).
 template <int BN, int STAGES, bool BF16, bool PAIR = false, int MODE = 0>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmSmem<BN, STAGES, PAIR>;
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0 = leader
   // Cluster split-K: rank csr runs split csr of tiles cluster, cluster + clusters, ... (units
   // csr * per_split + tile), so every CTA of a cluster walks the same tiles in the same order.
-  const int CS = (PAIR || MODE == 2) ? 0 : p.cs;  // cluster size of the split-K cluster, 0 = off
+  const int CS = (PAIR || MODE >= 2) ? 0 : p.cs;  // cluster size of the split-K cluster, 0 = off
   const int csr = CS ? (int)cluster_ctarank() : 0;
   const int cta0 = PAIR ? blockIdx.x >> 1 : (CS ? csr * p.m_tiles * p.n_tiles + (int)blockIdx.x / CS : blockIdx.x);
   const int cstride = PAIR ? gridDim.x >> 1 : (CS ? (int)gridDim.x / CS : gridDim.x);
@@ -272,7 +273,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   const uint32_t tempty_leader = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
   const uint32_t aready_leader = PAIR ? mapa_shared(smem_u32(aready), 0) : smem_u32(aready);
   constexpr bool xform = MODE == 1;  // operand-fused GroupNorm (p.gn_tab): a separate instantiation
-  constexpr bool PLAIN = MODE == 2;
+  constexpr bool PLAIN = MODE == 2, PARTIAL = MODE == 3;
   const int out_f32 = PLAIN ? 0 : p.out_f32, res_f32 = PLAIN ? 0 : p.res_f32, vec_ok = PLAIN ? 1 : p.vec_ok;
   const int staged = PLAIN ? 1 : p.staged;
   const uint32_t tmem = *tmem_slot;
@@ -783,8 +784,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       if (tr && lt == 0 && threadIdx.x == 64) tr[5] = globaltimer();
       tc_fence_after();
       const uint32_t trow = tmem + ab * BN + (static_cast<uint32_t>(q * 32) << 16);
-      const bool split = !PLAIN && p.splits > 1;
-      const bool gg = !PLAIN && p.geglu && !split;  // split-K stores raw packed partials; the reduce applies GEGLU
+      const bool split = PARTIAL || (!PLAIN && p.splits > 1);
+      const bool gg = !PLAIN && !PARTIAL && p.geglu && !split;  // split-K stores raw packed partials; the reduce applies GEGLU
       bool xok = true;  // cluster split-K exchange still in step with the peers
       const int nchunks = gg ? BN / 64 : BN / 32;
       const int n_out = gg ? p.N / 2 : p.N;
@@ -862,7 +863,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[10] = globaltimer();
           }
         }
-        if (!PLAIN && p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
+        if (!PLAIN && !PARTIAL && p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
         if (!ok || nb >= n_out) continue;  // warp-uniform
         if (!split) {
           if (PLAIN || !(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, false, staged);
@@ -876,7 +877,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[14] = globaltimer();
           continue;
         }
-        if (!(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, true, p.staged);  // fp32 partials: the reduce kernel finishes them
+        if (PARTIAL || !(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, true, staged);  // fp32 partials: the reduce kernel finishes them
         if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[11] = globaltimer();
         if (tr && lt == 0 && threadIdx.x == 64 && c == half + 2) tr[12] = globaltimer();
       }
@@ -1242,6 +1243,8 @@ static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool
   if (p.gn_tab) return dispatch_xf<1>(c, p, bn, bf16, pair);
   const bool plain = !p.geglu && p.splits <= 1 && !p.gstats && !p.out_f32 && !p.res_f32 && p.staged && !p.cs &&
                      !p.dbg && !g_gemm_generic;
+  const bool partial = p.splits > 1 && !p.cs && !p.gstats && !p.dbg && !g_gemm_generic;  // GEGLU packs raw partials too
+  if (partial) return dispatch_xf<3>(c, p, bn, bf16, pair);
   return plain ? dispatch_xf<2>(c, p, bn, bf16, pair) : dispatch_xf<0>(c, p, bn, bf16, pair);
 }
 
