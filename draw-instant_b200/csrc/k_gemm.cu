@@ -212,7 +212,8 @@ __device__ __forceinline__ void gn_stats_chunk(const float (&v)[32], int nb, int
 
 // MODE: 0 generic epilogue (every runtime variant), 1 operand-fused GroupNorm (XF), 2 plain epilogue: 16-bit
 // output through the staging slab, no split-K, GEGLU, statistics or fp32 operands (compiled without them);
-// 3 split-K partials: raw fp32 partial stores only (no epilogue arithmetic, no GEGLU / statistics / cluster).
+// 3 split-K partials: raw fp32 partial stores only (no epilogue arithmetic, no GEGLU / statistics / cluster);
+// 4 GEGLU without split: value * GELU(gate) to a 16-bit output.
 template <int BN, int STAGES, bool BF16, bool PAIR = false, int MODE = 0>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using S = GemmSmem<BN, STAGES, PAIR>;
@@ -273,8 +274,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   const uint32_t tempty_leader = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
   const uint32_t aready_leader = PAIR ? mapa_shared(smem_u32(aready), 0) : smem_u32(aready);
   constexpr bool xform = MODE == 1;  // operand-fused GroupNorm (p.gn_tab): a separate instantiation
-  constexpr bool PLAIN = MODE == 2, PARTIAL = MODE == 3;
-  const int out_f32 = PLAIN ? 0 : p.out_f32, res_f32 = PLAIN ? 0 : p.res_f32, vec_ok = PLAIN ? 1 : p.vec_ok;
+  constexpr bool PLAIN = MODE == 2, PARTIAL = MODE == 3, GEGLU = MODE == 4;
+  const int out_f32 = (PLAIN || GEGLU) ? 0 : p.out_f32, res_f32 = PLAIN ? 0 : p.res_f32, vec_ok = PLAIN ? 1 : p.vec_ok;
   const int staged = PLAIN ? 1 : p.staged;
   const uint32_t tmem = *tmem_slot;
   if (tr && threadIdx.x == 0) tr[1] = globaltimer();
@@ -784,8 +785,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       if (tr && lt == 0 && threadIdx.x == 64) tr[5] = globaltimer();
       tc_fence_after();
       const uint32_t trow = tmem + ab * BN + (static_cast<uint32_t>(q * 32) << 16);
-      const bool split = PARTIAL || (!PLAIN && p.splits > 1);
-      const bool gg = !PLAIN && !PARTIAL && p.geglu && !split;  // split-K stores raw packed partials; the reduce applies GEGLU
+      const bool split = PARTIAL || (!PLAIN && !GEGLU && p.splits > 1);
+      const bool gg = GEGLU || (!PLAIN && !PARTIAL && p.geglu && !split);  // split-K stores raw packed partials; the reduce applies GEGLU
       bool xok = true;  // cluster split-K exchange still in step with the peers
       const int nchunks = gg ? BN / 64 : BN / 32;
       const int n_out = gg ? p.N / 2 : p.N;
@@ -863,7 +864,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[10] = globaltimer();
           }
         }
-        if (!PLAIN && !PARTIAL && p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
+        if (MODE == 0 && p.gstats && !split && ok && nb < n_out) gn_stats_chunk(v, nb, m0 + q * 32, m, lane, p);
         if (!ok || nb >= n_out) continue;  // warp-uniform
         if (!split) {
           if (PLAIN || !(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, false, staged);
@@ -1245,6 +1246,7 @@ static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool
                      !p.dbg && !g_gemm_generic;
   const bool partial = p.splits > 1 && !p.cs && !p.gstats && !p.dbg && !g_gemm_generic;  // GEGLU packs raw partials too
   if (partial) return dispatch_xf<3>(c, p, bn, bf16, pair);
+  if (p.geglu && p.splits <= 1 && !p.out_f32 && !p.dbg && !g_gemm_generic) return dispatch_xf<4>(c, p, bn, bf16, pair);
   return plain ? dispatch_xf<2>(c, p, bn, bf16, pair) : dispatch_xf<0>(c, p, bn, bf16, pair);
 }
 
