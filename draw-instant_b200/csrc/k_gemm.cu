@@ -57,6 +57,9 @@ struct GemmParams {
   // split r of the cluster's tiles, and the cluster sums its partials through distributed shared memory in
   // the epilogue (fixed rank order), so no fp32 partials reach global memory and no reduce kernel runs.
   int cs;
+  // 16-bit output stored by TMA from the 64-byte-swizzled staging slab (box 32 x 32): set by launch_gemm
+  CUtensorMap tmO;
+  int tma_out;
   int dbg;  // diagnostics (DI_GEMM_DEBUG): 1 skip output / partial stores, 2 skip the bias/residual epilogue
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
@@ -486,6 +489,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
         // The warp's 32 x 32 tile goes through a swizzled staging slab (conflict-free writes of one row
         // per lane), then is read back so that each store instruction writes whole 64/128-byte row
         // segments of 8 or 4 rows (coalesced), instead of 32 rows 16 bytes at a time.
+        if (p.tma_out && lane == 0) bulk_wait_read0();  // the previous chunk's TMA store has read the slab
         __syncwarp();  // the previous chunk's read-back is done
         if (to_partial || out_f32) {
           // 32 fp32 per row = 128 B; 16-byte chunk j of row r at j ^ (r & 7)
@@ -532,6 +536,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                 for (int k = 0; k < 4 && col + k < n_out; ++k) d[k] = t[k];
               }
             }
+          }
+        } else if (p.tma_out) {
+          // the slab's 16-byte chunk j of row r sits at j ^ ((r >> 1) & 3): the TMA 64-byte swizzle
+          fence_async_smem();  // this lane's slab writes, visible to the TMA unit
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&p.tmO, stg, nb, mrow0);
+            bulk_commit();
           }
         } else {
           uint16_t* base = static_cast<uint16_t*>(p.out);
@@ -891,6 +903,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       if (tr && lt == 0 && threadIdx.x == 64) tr[6] = globaltimer();
       if (!ok || !xok) break;
     }
+    if (p.tma_out && lane == 0) bulk_wait0();  // every output store of this warp has completed
   }
   tc_fence_before();
   if (PAIR || CS) cluster_sync();  // no CTA leaves while a cluster peer may still read its slabs or signal it
@@ -1242,6 +1255,16 @@ static int dispatch_xf(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair
 
 static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
   if (p.gn_tab) return dispatch_xf<1>(c, p, bn, bf16, pair);
+  // 16-bit output rows 16-byte aligned: the epilogue stores its 32 x 32 chunks with TMA
+  p.tma_out = 0;
+  if (!p.out_f32 && p.staged && p.splits <= 1 && !p.cs && !p.gstats && !p.dbg && !g_gemm_generic) {
+    const uint64_t dims[2] = {(uint64_t)(p.geglu ? p.N / 2 : p.N), (uint64_t)p.M};
+    const uint64_t strides[1] = {(uint64_t)p.ldo * 2};
+    const uint32_t box[2] = {32, 32};
+    std::string err;
+    p.tma_out = make_tmap(&p.tmO, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.out,
+                          dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B, &err) ? 1 : 0;
+  }
   const bool plain = !p.geglu && p.splits <= 1 && !p.gstats && !p.out_f32 && !p.res_f32 && p.staged && !p.cs &&
                      !p.dbg && !g_gemm_generic;
   const bool partial = p.splits > 1 && !p.cs && !p.gstats && !p.dbg && !g_gemm_generic;  // GEGLU packs raw partials too
