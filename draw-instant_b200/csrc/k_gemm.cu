@@ -1255,16 +1255,6 @@ static int dispatch_xf(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair
 
 static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool pair) {
   if (p.gn_tab) return dispatch_xf<1>(c, p, bn, bf16, pair);
-  // 16-bit output rows 16-byte aligned: the epilogue stores its 32 x 32 chunks with TMA
-  p.tma_out = 0;
-  if (!p.out_f32 && p.staged && p.splits <= 1 && !p.cs && !p.gstats && !p.dbg && !g_gemm_generic) {
-    const uint64_t dims[2] = {(uint64_t)(p.geglu ? p.N / 2 : p.N), (uint64_t)p.M};
-    const uint64_t strides[1] = {(uint64_t)p.ldo * 2};
-    const uint32_t box[2] = {32, 32};
-    std::string err;
-    p.tma_out = make_tmap(&p.tmO, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.out,
-                          dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B, &err) ? 1 : 0;
-  }
   const bool plain = !p.geglu && p.splits <= 1 && !p.gstats && !p.out_f32 && !p.res_f32 && p.staged && !p.cs &&
                      !p.dbg && !g_gemm_generic;
   const bool partial = p.splits > 1 && !p.cs && !p.gstats && !p.dbg && !g_gemm_generic;  // GEGLU packs raw partials too
@@ -1323,6 +1313,16 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
     launch_k(splitk_reduce, blocks, 256, 0, c->stream, p.partial, p.splits, p.M, p.N, p.bias, p.rowvec, p.rowvec_div,
              p.rowvec_ld, p.residual, p.ldr, p.res_f32, p.out, p.ldo, p.out_f32, p.geglu, bf16, p.act);
     return check_launch(c, "splitk_reduce");
+  }
+  // 16-bit output rows 16-byte aligned: the epilogue stores its 32 x 32 chunks with TMA
+  p.tma_out = 0;
+  if (!p.out_f32 && p.staged && p.splits <= 1 && !p.cs && !p.gstats && !p.dbg && !p.gn_tab && !g_gemm_generic) {
+    const uint64_t dims[2] = {(uint64_t)(p.geglu ? p.N / 2 : p.N), (uint64_t)p.M};
+    const uint64_t strides[1] = {(uint64_t)p.ldo * 2};
+    const uint32_t box[2] = {32, 32};
+    std::string err;
+    p.tma_out = make_tmap(&p.tmO, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.out,
+                          dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B, &err) ? 1 : 0;
   }
   return dispatch_variant(c, p, bn, bf16, pair);
 }
