@@ -53,6 +53,10 @@ struct Ctx {
   // fp16 output into gn_stats[image][group][3] (exact fixed point, see gn_fixed), images of gn_stats_hw rows.
   long long* gn_stats = nullptr;
   int gn_stats_hw = 0;
+  // When set (by a plan, around one GEMM call): the GEMM folds a LayerNorm of its A rows (eps ln_eps);
+  // its weights are gamma-scaled, ln_c1[n] their row sums, its bias includes the beta term.
+  const float* ln_c1 = nullptr;
+  float ln_eps = 1e-5f;
   // Grid-barrier word pair {arrivals, generation} of the single-launch GroupNorm (gn_nhwc_grid) when it is
   // called through the public entry point; zeroed at allocation, left at {0, g} by every completed launch.
   unsigned* gn_bar = nullptr;

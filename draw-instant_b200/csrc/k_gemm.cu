@@ -60,6 +60,13 @@ struct GemmParams {
   // 16-bit output stored by TMA from the 64-byte-swizzled staging slab (box 32 x 32): set by launch_gemm
   CUtensorMap tmO;
   int tma_out;
+  // LayerNorm of the A rows folded in (plain and GEGLU instantiations, no split, single CTAs): the B rows
+  // hold W[n][k] * gamma[k], ln_c1[n] = sum_k of those, and the bias holds b[n] + sum_k W[n][k] * beta[k];
+  // the epilogue warps take each row's mean / rstd from the A tiles in shared memory during the main loop
+  // and the epilogue computes rstd * (acc - mean * ln_c1[n]) + bias[n].
+  int ln;
+  float ln_eps;
+  const float* ln_c1;
   int dbg;  // diagnostics (DI_GEMM_DEBUG): 1 skip output / partial stores, 2 skip the bias/residual epilogue
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
@@ -255,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], (!PAIR && p.ln) ? 1 + kEpiWarps : 1);  // + the LayerNorm statistics readers
       mbar_init(&afull[s], 1);
       mbar_init(&aready[s], (PAIR ? 2 : 1) * kEpiWarps);  // one arrival per transforming warp
     }
@@ -436,10 +443,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
     const int row = q * 32 + lane;
     const int half = (warp - 2) / 4;  // which alternate column chunks this warp handles
     uint8_t* stg = sEpi + (warp - 2) * 4096;
+    const bool LN = (PLAIN || GEGLU) && !PAIR && p.ln;
+    float ln_rs = 1.f, ln_rm = 0.f;  // this row's rstd and rstd * mean (LayerNorm fold)
+    int lit = 0;                     // ring position of the statistics readers (same sequence as the producer)
     // Epilogue on one row's 32 columns: bias, per-image row vector, activation, residual (not GEGLU).
     auto epi = [&](float (&v)[32], int nb, int m) {
       const int n_out = p.N;
       const bool full = nb + 32 <= n_out;
+      if (LN) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (nb + j < n_out) v[j] = fmaf(ln_rs, v[j], -ln_rm * p.ln_c1[nb + j]);
+      }
       if (p.bias) {
         if (full) {
 #pragma unroll
@@ -775,7 +790,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       // 32 lanes (the first chunk's before the accumulator wait, i.e. during the main loop): lane j holds
       // column j's bias and row-vector values (broadcast later by full-warp shuffles), each lane its own
       // row's 32 residual values.  A chunk takes this path when it is whole and its 32 rows share one image.
-      float pf_b = 0.f, pf_r = 0.f;
+      if (LN) {
+        // LayerNorm statistics of this warp's 32 rows (one row per lane, all 64 columns of every K block)
+        float sum = 0.f, sq = 0.f;
+        for (int kb = kb0; kb < kb1; ++kb, ++lit) {
+          const int s = lit % STAGES;
+          const bool okl = mbar_wait(&full[s], (lit / STAGES) & 1, p.err, DEVERR_WAIT_EPI) && !*abort_flag;
+          if (okl) {
+            const uint4* rowp = reinterpret_cast<const uint4*>(sA + s * S::A_BYTES + row * 128);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint4 u = rowp[j];
+              const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                uint32_t we = w[e];
+                float2 f;
+                if (BF16) f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&we));
+                else f = __half22float2(*reinterpret_cast<__half2*>(&we));
+                sum += f.x + f.y;
+                sq = fmaf(f.x, f.x, fmaf(f.y, f.y, sq));
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        const float kk = (float)(p.num_k * BK);
+        const float mean = sum / kk;
+        const float var = fmaxf(sq / kk - mean * mean, 0.0f);
+        ln_rs = 1.0f / sqrtf(var + p.ln_eps);
+        ln_rm = ln_rs * mean;
+      }
+      float pf_b = 0.f, pf_r = 0.f, pf_c = 0.f;
       uint4 pf_res[4] = {};
       auto pf_fast = [&](int c) {
         return PLAIN && n0 + c * 32 + 32 <= p.N && (!p.rowvec || p.rowvec_div % 32 == 0);
@@ -783,6 +830,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       auto pf_fetch = [&](int c) {
         const int nbc = n0 + c * 32;
         if (p.bias) pf_b = __ldg(p.bias + nbc + lane);
+        if (LN) pf_c = __ldg(p.ln_c1 + nbc + lane);
         if (p.rowvec && m0 + q * 32 < p.M)
           pf_r = __ldg(p.rowvec + (size_t)((m0 + q * 32) / p.rowvec_div) * p.rowvec_ld + nbc + lane);
         if (p.residual && m < p.M) {
@@ -821,6 +869,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 float a = __uint_as_float(r[j]), gt = __uint_as_float(rg[j]);
+                if (LN) {
+                  a = fmaf(ln_rs, a, -ln_rm * __ldg(p.ln_c1 + nv + j));
+                  gt = fmaf(ln_rs, gt, -ln_rm * __ldg(p.ln_c1 + nv + 64 + j));
+                }
                 if (p.bias) { a += __ldg(p.bias + nv + j); gt += __ldg(p.bias + nv + 64 + j); }
                 v[j] = a * gelu_erf(gt);
               }
@@ -828,7 +880,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           } else {
             if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[8] = globaltimer();
             const bool fastc = pf_fast(c);
-            const float cb = pf_b, cr = pf_r;
+            const float cb = pf_b, cr = pf_r, cc1 = pf_c;
             uint4 cres[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) cres[j] = pf_res[j];
@@ -840,6 +892,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
             if (PLAIN && fastc) {  // warp-uniform: the shuffles run on all 32 lanes
+              if (LN) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = fmaf(ln_rs, v[j], -ln_rm * __shfl_sync(0xffffffffu, cc1, j));
+              }
               if (p.bias) {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, cb, j);
@@ -1151,7 +1207,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
       }
     }
   }
-  if (forced_bn && (!geglu || forced_bn % 128 == 0)) {
+  if (forced_bn && !c->ln_c1 && (!geglu || forced_bn % 128 == 0)) {
     *bn = forced_bn;
     int fs = forced_s;
     // forced pair value 2 = cluster split-K instead of paired tiles
@@ -1182,14 +1238,15 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
   double best = 1e30;
   *bn = 128;
   *splits = 1;
+  const bool single = c->ln_c1 != nullptr;  // folded LayerNorm: whole K per CTA, no CTA pairs
   for (int pr = 0; pr < 2; ++pr) {
-    if (pr && (M <= BM || !pair_ok)) continue;
+    if (pr && (M <= BM || !pair_ok || single)) continue;
     const int mtiles = pr ? (M + 2 * BM - 1) / (2 * BM) : mt;
     const int slots = pr ? pairs : c->num_sms;  // concurrently running units
     for (int bc : cands) {
       if (geglu && (bc % 128 || N % bc)) continue;
       const int nt = geglu ? N / bc : (N + bc - 1) / bc;
-      const int smax = std::max(1, std::min(16, num_k / 4));
+      const int smax = single ? 1 : std::max(1, std::min(16, num_k / 4));
       const double kb_cost = 1.0 + (pr ? 0.05 : 0.2) * (bc - 128) / 128.0;
       for (int s = 1; s <= smax; ++s) {
         const int per = (num_k + s - 1) / s;
@@ -1260,6 +1317,7 @@ static int dispatch_variant(Ctx* c, const GemmParams& p, int bn, bool bf16, bool
   const bool partial = p.splits > 1 && !p.cs && !p.gstats && !p.dbg && !g_gemm_generic;  // GEGLU packs raw partials too
   if (partial) return dispatch_xf<3>(c, p, bn, bf16, pair);
   if (p.geglu && p.splits <= 1 && !p.out_f32 && !p.dbg && !g_gemm_generic) return dispatch_xf<4>(c, p, bn, bf16, pair);
+  if (p.ln && !plain) return set_error(c, DI_EINVAL, "gemm: a folded LayerNorm needs the plain or GEGLU epilogue");
   return plain ? dispatch_xf<2>(c, p, bn, bf16, pair) : dispatch_xf<0>(c, p, bn, bf16, pair);
 }
 
@@ -1275,6 +1333,14 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
     p.g_hw = c->gn_stats_hw;
   }
   p.staged = (p.vec_ok && splits <= 1) ? 1 : 0;
+  p.ln = 0;
+  if (c->ln_c1) {
+    if (splits > 1 || pair || p.out_f32 || !p.staged || p.gn_tab || p.gstats || !p.bias)
+      return set_error(c, DI_EINVAL, "gemm: a folded LayerNorm needs one unsplit single-CTA tile, 16-bit aligned output");
+    p.ln = 1;
+    p.ln_c1 = c->ln_c1;
+    p.ln_eps = c->ln_eps;
+  }
   p.b_early = c->weights_const ? 1 : 0;
   static const int dbg = [] {
     const char* e = getenv("DI_GEMM_DEBUG");

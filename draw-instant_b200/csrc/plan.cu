@@ -1002,6 +1002,52 @@ struct Plan {
   }
 
   // Transformer2DModel (linear proj_in/out) + BasicTransformerBlock; ctx16 = [N, Sk, Cctx] fp16.
+  // LayerNorm(x) . W^T + b as one GEMM on the raw rows x (the GEMM folds the normalisation, Ctx::ln_c1):
+  // W'[n][k] = f16(f16(W[n][k]) * gamma[k]), c1[n] = sum_k W'[n][k], b'[n] = b[n] + sum_k f16(W[n][k]) * beta[k].
+  // y = rstd * (x . W'^T - mean * c1) + b' is LayerNorm(x) . W^T + b with the LayerNorm output kept in fp32.
+  // DI_LN_FOLD=0 keeps the separate LayerNorm kernel (diagnostics).
+  bool ln_fold_on = [] {
+    const char* e = getenv("DI_LN_FOLD");
+    return !(e && e[0] == '0');
+  }();
+  struct LnFold { const void* W; const float* c1; const float* b; };
+  LnFold ln_fold(std::vector<float> W, const std::vector<float>* bias, int N, int K, const std::string& norm) {
+    auto g = host_param(norm + ".weight", K, 1, 1);
+    auto be = host_param(norm + ".bias", K, 2, 1);
+    round_f16(g);
+    round_f16(be);
+    round_f16(W);
+    std::vector<float> wp(W.size()), c1(N), b2(N);
+    for (int n = 0; n < N; ++n) {
+      double bs = bias ? (*bias)[n] : 0.0;
+      for (int k = 0; k < K; ++k) {
+        const float w = W[(size_t)n * K + k];
+        wp[(size_t)n * K + k] = w * g[k];
+        bs += (double)w * be[k];
+      }
+      b2[n] = (float)bs;
+    }
+    round_f16(wp);
+    for (int n = 0; n < N; ++n) {
+      double cs = 0.0;
+      for (int k = 0; k < K; ++k) cs += wp[(size_t)n * K + k];
+      c1[n] = (float)cs;
+    }
+    return LnFold{upload_f16(wp), upload_f32(c1), upload_f32(b2)};
+  }
+  void linear_ln(const void* X, int M, int K, const LnFold& f, int N, void* Y, int geglu) {
+    Ctx* cc = c;
+    void* sk = splitk;
+    record([=] {
+      cc->ln_c1 = f.c1;
+      cc->ln_eps = 1e-5f;
+      const int r = gemm_linear(cc, DI_F16, X, K, nullptr, M, K, f.W, N, f.b, nullptr, 0, Y, 0, geglu, nullptr, 1, sk,
+                                nullptr, 0, 0);
+      cc->ln_c1 = nullptr;
+      return r;
+    }, 0, 2.0 * M * N * K, 2.0 * ((double)M * K + (double)N * K + (double)M * (geglu ? N / 2 : N)), 1);
+  }
+
   Act transformer(const std::string& pre, const Act& x, const void* ctx16, int Sk, int Cctx) {
     tmp_reset();
     const int N = x.N, HW = x.H * x.W, C = x.C, M = N * HW, heads = C / 64;
@@ -1015,16 +1061,19 @@ struct Plan {
     // --- self attention ---
     const float* g1 = vec(tb + ".norm1.weight", C, 1, 1);
     const float* be1 = vec(tb + ".norm1.bias", C, 2, 1);
-    void* n1 = tmp((size_t)M * C * 2);
-    record([=] { return layer_norm(cc, DI_F16, DI_F16, h0, g1, be1, n1, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
     std::vector<float> wqkv;
     for (const char* nm : {".attn1.to_q.weight", ".attn1.to_k.weight", ".attn1.to_v.weight"}) {
       auto w = host_param(tb + nm, (size_t)C * C, 0, C, C);
       wqkv.insert(wqkv.end(), w.begin(), w.end());
     }
-    const void* Wqkv = upload_f16(wqkv);
     void* qkv = tmp((size_t)M * 3 * C * 2);
-    linear(n1, M, C, Wqkv, 3 * C, nullptr, nullptr, qkv);
+    if (ln_fold_on) {
+      linear_ln(h0, M, C, ln_fold(wqkv, nullptr, 3 * C, C, tb + ".norm1"), 3 * C, qkv, 0);
+    } else {
+      void* n1 = tmp((size_t)M * C * 2);
+      record([=] { return layer_norm(cc, DI_F16, DI_F16, h0, g1, be1, n1, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
+      linear(n1, M, C, upload_f16(wqkv), 3 * C, nullptr, nullptr, qkv);
+    }
     void* o1 = tmp((size_t)M * C * 2);
     record([=] {
       const char* base = static_cast<const char*>(qkv);
@@ -1038,11 +1087,16 @@ struct Plan {
     // --- cross attention ---
     const float* g2 = vec(tb + ".norm2.weight", C, 1, 1);
     const float* be2 = vec(tb + ".norm2.bias", C, 2, 1);
-    void* n2 = tmp((size_t)M * C * 2);
-    record([=] { return layer_norm(cc, DI_F16, DI_F16, h1, g2, be2, n2, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
-    const void* wq2 = lin_weight(tb + ".attn2.to_q.weight", C, C);
     void* q2 = tmp((size_t)M * C * 2);
-    linear(n2, M, C, wq2, C, nullptr, nullptr, q2);
+    if (ln_fold_on) {
+      linear_ln(h1, M, C, ln_fold(host_param(tb + ".attn2.to_q.weight", (size_t)C * C, 0, C, C), nullptr, C, C,
+                                  tb + ".norm2"), C, q2, 0);
+    } else {
+      void* n2 = tmp((size_t)M * C * 2);
+      record([=] { return layer_norm(cc, DI_F16, DI_F16, h1, g2, be2, n2, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
+      const void* wq2 = lin_weight(tb + ".attn2.to_q.weight", C, C);
+      linear(n2, M, C, wq2, C, nullptr, nullptr, q2);
+    }
     std::vector<float> wkv;
     for (const char* nm : {".attn2.to_k.weight", ".attn2.to_v.weight"}) {
       auto w = host_param(tb + nm, (size_t)C * Cctx, 0, Cctx, C);
@@ -1080,8 +1134,6 @@ struct Plan {
     // --- GEGLU feed-forward ---
     const float* g3 = vec(tb + ".norm3.weight", C, 1, 1);
     const float* be3 = vec(tb + ".norm3.bias", C, 2, 1);
-    void* n3 = tmp((size_t)M * C * 2);
-    record([=] { return layer_norm(cc, DI_F16, DI_F16, h2, g3, be3, n3, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
     const int F = 4 * C;
     auto wff = host_param(tb + ".ff.net.0.proj.weight", (size_t)2 * F * C, 0, C, 2 * F);
     auto bff = host_param(tb + ".ff.net.0.proj.bias", (size_t)2 * F, 0, C);
@@ -1095,12 +1147,18 @@ struct Plan {
         bp[128 * t + 64 + r] = bff[F + 64 * t + r];
       }
     }
-    const void* Wff = upload_f16(wp);
-    const float* Bff = upload_f32(bp);
     void* g = tmp((size_t)M * F * 2);
-    record([=] { return gemm_linear(cc, DI_F16, n3, C, nullptr, M, C, Wff, 2 * F, Bff, nullptr, 0, g, 0, 1, nullptr,
-                                    1, splitk); },
-           0, 2.0 * M * 2 * F * C, 2.0 * ((double)M * C + 2.0 * F * C + (double)M * F), gemm_kernel_count(c, M, 2 * F, C, 1));
+    if (ln_fold_on) {
+      linear_ln(h2, M, C, ln_fold(wp, &bp, 2 * F, C, tb + ".norm3"), 2 * F, g, 1);
+    } else {
+      void* n3 = tmp((size_t)M * C * 2);
+      record([=] { return layer_norm(cc, DI_F16, DI_F16, h2, g3, be3, n3, M, C, 1e-5f); }, 2, 0, 4.0 * M * C);
+      const void* Wff = upload_f16(wp);
+      const float* Bff = upload_f32(bp);
+      record([=] { return gemm_linear(cc, DI_F16, n3, C, nullptr, M, C, Wff, 2 * F, Bff, nullptr, 0, g, 0, 1, nullptr,
+                                      1, splitk); },
+             0, 2.0 * M * 2 * F * C, 2.0 * ((double)M * C + 2.0 * F * C + (double)M * F), gemm_kernel_count(c, M, 2 * F, C, 1));
+    }
     const void* wf2 = lin_weight(tb + ".ff.net.2.weight", C, F);
     const float* bf2 = vec(tb + ".ff.net.2.bias", C, 0, F);
     void* h3 = tmp((size_t)M * C * 2);
