@@ -1255,6 +1255,8 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
         // global partials must fit the buffer (a cluster split needs none)
         const bool fits = s == 1 || (size_t)M * N * s * 4 <= kSplitKWsBytes;
         if (!fits && !(allow_cs && !pr && s <= kMaxClusterSplit)) break;
+        // a folded LayerNorm keeps one tile per CTA (its statistics readers would hold the ring otherwise)
+        if (single && (long long)mtiles * (geglu ? N / bc : (N + bc - 1) / bc) > slots) continue;
         const long long units = (long long)mtiles * nt * s;
         const long long rounds = (units + slots - 1) / slots;
         double cost = (double)rounds * (per * kb_cost + 8.0) + 4.0;

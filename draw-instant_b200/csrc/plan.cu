@@ -1035,6 +1035,9 @@ struct Plan {
     }
     return LnFold{upload_f16(wp), upload_f32(c1), upload_f32(b2)};
   }
+  // The fold pays only when the GEMM runs as one tile per CTA (BN = 256 bound); otherwise the plan keeps the
+  // LayerNorm kernel.
+  bool ln_fits(int M, int N) const { return (long long)((M + 127) / 128) * ((N + 255) / 256) <= c->num_sms; }
   void linear_ln(const void* X, int M, int K, const LnFold& f, int N, void* Y, int geglu) {
     Ctx* cc = c;
     void* sk = splitk;
@@ -1067,7 +1070,7 @@ struct Plan {
       wqkv.insert(wqkv.end(), w.begin(), w.end());
     }
     void* qkv = tmp((size_t)M * 3 * C * 2);
-    if (ln_fold_on) {
+    if (ln_fold_on && ln_fits(M, 3 * C)) {
       linear_ln(h0, M, C, ln_fold(wqkv, nullptr, 3 * C, C, tb + ".norm1"), 3 * C, qkv, 0);
     } else {
       void* n1 = tmp((size_t)M * C * 2);
@@ -1088,7 +1091,7 @@ struct Plan {
     const float* g2 = vec(tb + ".norm2.weight", C, 1, 1);
     const float* be2 = vec(tb + ".norm2.bias", C, 2, 1);
     void* q2 = tmp((size_t)M * C * 2);
-    if (ln_fold_on) {
+    if (ln_fold_on && ln_fits(M, C)) {
       linear_ln(h1, M, C, ln_fold(host_param(tb + ".attn2.to_q.weight", (size_t)C * C, 0, C, C), nullptr, C, C,
                                   tb + ".norm2"), C, q2, 0);
     } else {
@@ -1148,7 +1151,7 @@ struct Plan {
       }
     }
     void* g = tmp((size_t)M * F * 2);
-    if (ln_fold_on) {
+    if (ln_fold_on && ln_fits(M, 2 * 4 * C)) {
       linear_ln(h2, M, C, ln_fold(wp, &bp, 2 * F, C, tb + ".norm3"), 2 * F, g, 1);
     } else {
       void* n3 = tmp((size_t)M * C * 2);
