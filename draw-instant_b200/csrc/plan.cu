@@ -1005,10 +1005,11 @@ struct Plan {
   // LayerNorm(x) . W^T + b as one GEMM on the raw rows x (the GEMM folds the normalisation, Ctx::ln_c1):
   // W'[n][k] = f16(f16(W[n][k]) * gamma[k]), c1[n] = sum_k W'[n][k], b'[n] = b[n] + sum_k f16(W[n][k]) * beta[k].
   // y = rstd * (x . W'^T - mean * c1) + b' is LayerNorm(x) . W^T + b with the LayerNorm output kept in fp32.
-  // DI_LN_FOLD=0 keeps the separate LayerNorm kernel (diagnostics).
+  // Opt-in (DI_LN_FOLD=1): parity-green, but measured slower in the step (236.8 vs 263.7 steps/s, one-wave
+  // GEMMs only; 227.3 when folded everywhere) than the separate LayerNorm kernel.
   bool ln_fold_on = [] {
     const char* e = getenv("DI_LN_FOLD");
-    return !(e && e[0] == '0');
+    return e && e[0] == '1';
   }();
   struct LnFold { const void* W; const float* c1; const float* b; };
   LnFold ln_fold(std::vector<float> W, const std::vector<float>* bias, int N, int K, const std::string& norm) {
