@@ -44,10 +44,10 @@ WORKLOAD = ("config 4: SD-Turbo (SD2.1) U-Net single denoising step, 64x64 laten
             "context 77x1024")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch of the dominant kernel, the mean over the GEMM launches of one
-# forward in the committed ncu capture (profiles/hbm_kernels_unet64.md); None until that capture exists.
+# forward in a committed ncu capture of the step (dram__bytes_read.sum + dram__bytes_write.sum).
 GEMM_TRAFFIC = 9.98e6
 GEMM_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over 60 gemm_tc_kernel launches of "
-                       "the batch-1 forward (profiles/hbm_kernels_unet64.md)")
+                       "the batch-1 forward (committed ncu summary of the step's HBM counters)")
 
 
 def load_package():

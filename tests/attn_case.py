@@ -1,7 +1,7 @@
 """Standalone driver for profiling the config-3 attention (not a test): runs di_attention three times on
 Q/K/V [8, 5, 4096, 64] head-major bf16 drawn like bench.py's (seed-2 generator, N(0,1)/8), self-attention
-by default or cross-attention (K/V [8, 5, 77, 64]) with --cross.  Used by the ncu command in
-profiles/attn_fwd_config3_ncu.md."""
+by default or cross-attention (K/V [8, 5, 77, 64]) with --cross: the command the committed ncu capture
+of the config-3 attention kernel profiles."""
 from __future__ import annotations
 
 import sys
