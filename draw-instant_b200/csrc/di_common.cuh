@@ -26,10 +26,6 @@ namespace di {
 // Largest split-K partial-sum buffer (fp32, splits x M x N) a GEMM may use: the size of a plan's
 // shared split-K buffer; the tiling model only picks splits that fit.
 constexpr size_t kSplitKWsBytes = 32u << 20;
-// Its last kSplitKCntBytes hold the per-chunk arrival counters of the in-kernel split-K reduction (zeroed
-// when the buffer is made; every reduction resets the counters it used), so partials use the rest.
-constexpr size_t kSplitKCntBytes = 256u << 10;
-constexpr size_t kSplitKPartBytes = kSplitKWsBytes - kSplitKCntBytes;
 
 // ---------------------------------------------------------------------------------------------
 // Host-side context

@@ -67,11 +67,6 @@ struct GemmParams {
   int ln;
   float ln_eps;
   const float* ln_c1;
-  // In-kernel split-K reduction (split-K partial instantiation): after storing a chunk's partial, each split
-  // bumps the chunk's arrival counter; the last arrival sums the splits' partials in split order (the
-  // reduce kernel's order: identical bits), applies the epilogue, stores and resets the counter.
-  int fused;
-  int* cnt;
   int dbg;  // diagnostics (DI_GEMM_DEBUG): 1 skip output / partial stores, 2 skip the bias/residual epilogue
   int m_tiles, n_tiles;  // 128-row M tiles and BN-column N tiles (set by launch_gemm)
   float* partial;  // [splits][M][N] fp32 when splits > 1
@@ -90,13 +85,6 @@ struct GemmParams {
 constexpr int kTracePoints = 16;
 static unsigned long long* g_trace = nullptr;
 static int g_trace_ctas = 0;
-static bool fused_reduce_on() {  // DI_FUSED_REDUCE=0 keeps the split-K reduce kernel (diagnostics)
-  static const bool on = [] {
-    const char* e = getenv("DI_FUSED_REDUCE");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
 static const bool g_gemm_generic = [] {  // diagnostics: DI_GEMM_GENERIC=1 never uses the plain epilogue
   const char* e = getenv("DI_GEMM_GENERIC");
   return e && e[0] == '1';
@@ -863,12 +851,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
       const int nchunks = gg ? BN / 64 : BN / 32;
       const int n_out = gg ? p.N / 2 : p.N;
 #pragma unroll 1
-      // With the in-kernel reduction each split walks its chunks from a different start, so the last
-      // arrivals (which reduce) are spread over the split CTAs instead of all falling on the slowest one.
-      const int cstep = kEpiWarps / 4, nper = (nchunks - half + cstep - 1) / cstep;
-      const bool rot = PARTIAL && p.fused;
-      for (int ci = 0; ci < nper; ++ci) {
-        const int c = half + cstep * (rot ? (ci + sp) % nper : ci);
+      for (int c = half; c < nchunks; c += kEpiWarps / 4) {
         float v[32];
         int nb;  // first output column of the chunk
         {
@@ -964,39 +947,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
           continue;
         }
         if (PARTIAL || !(p.dbg & 1)) store_chunk(v, nb, m0, m, sp, true, staged);  // fp32 partials: the reduce kernel finishes them
-        if (PARTIAL && p.fused) {
-          __threadfence();  // this lane's partial stores, before the arrival below
-          __syncwarp();
-          const int idx = (((m0 / BM) * p.n_tiles + n0 / BN) * 4 + q) * (BN / 32) + c;
-          int last = 0;
-          if (lane == 0) last = atomicAdd(p.cnt + idx, 1) == p.splits - 1;
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (last) {
-            __threadfence();
-            float acc[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-            if (m < p.M) {
-              for (int z = 0; z < p.splits; ++z) {
-                const float* src = p.partial + ((size_t)z * p.M + m) * p.N + nb;
-                if (nb + 32 <= p.N && (p.N & 3) == 0) {
-#pragma unroll
-                  for (int j = 0; j < 8; ++j) {
-                    const float4 t = __ldcg(reinterpret_cast<const float4*>(src) + j);
-                    acc[4 * j] += t.x; acc[4 * j + 1] += t.y; acc[4 * j + 2] += t.z; acc[4 * j + 3] += t.w;
-                  }
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j)
-                    if (nb + j < p.N) acc[j] += __ldcg(src + j);
-                }
-              }
-              epi(acc, nb, m);
-            }
-            store_chunk(acc, nb, m0, m, sp, false, p.vec_ok);
-            if (lane == 0) p.cnt[idx] = 0;  // ready for the next launch
-          }
-        }
         if (tr && lt == 0 && threadIdx.x == 64 && c == half) tr[11] = globaltimer();
         if (tr && lt == 0 && threadIdx.x == 64 && c == half + 2) tr[12] = globaltimer();
       }
@@ -1263,7 +1213,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
     // forced pair value 2 = cluster split-K instead of paired tiles
     const bool fcs = forced_pair == 2 && allow_cs;
     if (fcs) fs = std::min(fs, kMaxClusterSplit);
-    while (!fcs && fs > 1 && (size_t)M * N * fs * 4 > kSplitKPartBytes) --fs;
+    while (!fcs && fs > 1 && (size_t)M * N * fs * 4 > kSplitKWsBytes) --fs;
     const int per = (num_k + fs - 1) / fs;
     *splits = (num_k + per - 1) / per;
     *pair = forced_pair == 1 && M > BM;
@@ -1303,7 +1253,7 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
         const int seff = (num_k + per - 1) / per;
         if (seff != s) continue;
         // global partials must fit the buffer (a cluster split needs none)
-        const bool fits = s == 1 || (size_t)M * N * s * 4 <= kSplitKPartBytes;
+        const bool fits = s == 1 || (size_t)M * N * s * 4 <= kSplitKWsBytes;
         if (!fits && !(allow_cs && !pr && s <= kMaxClusterSplit)) break;
         // a folded LayerNorm keeps one tile per CTA (its statistics readers would hold the ring otherwise)
         if (single && (long long)mtiles * (geglu ? N / bc : (N + bc - 1) / bc) > slots) continue;
@@ -1338,14 +1288,10 @@ void choose_tiling(Ctx* c, int M, int N, int num_k, int geglu, int* bn, int* spl
   }
 }
 
-// Kernels one GEMM launches inside a plan (whose split-K buffers allow the in-kernel reduction).
 int gemm_kernel_count(Ctx* c, int M, int N, int K, int geglu) {
   int bn, s, pr, cs;
   choose_tiling(c, M, N, K / 64, geglu, &bn, &s, &pr, &cs);
-  const long long nctr = (long long)((M + BM - 1) / BM + 1) * (geglu ? N / bn : (N + bn - 1) / bn) * 4 * (bn / 32);
-  const bool fused = fused_reduce_on() && !geglu && !c->gn_stats && !g_gemm_generic &&
-                     nctr * (long long)sizeof(int) <= (long long)kSplitKCntBytes;
-  return (s > 1 && !cs && !fused) ? 2 : 1;
+  return (s > 1 && !cs) ? 2 : 1;
 }
 
 template <int XF>
@@ -1415,19 +1361,10 @@ int launch_gemm(Ctx* c, GemmParams& p, bool bf16, int bn, int splits, int pair, 
   }
   if (p.splits > 1) {
     const size_t need = sizeof(float) * (size_t)p.splits * p.M * p.N;
-    if (need > kSplitKPartBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
+    if (need > kSplitKWsBytes) return set_error(c, DI_EINVAL, "gemm: split-K partials exceed the workspace");
     p.partial = static_cast<float*>(splitk_ws ? splitk_ws : workspace(c, need, 4));
     if (!p.partial) return set_error(c, DI_ENOMEM, "gemm: split-K workspace");
     p.staged = (p.N % 4 == 0 && reinterpret_cast<uintptr_t>(p.partial) % 16 == 0) ? 1 : 0;
-    // in-kernel reduction: plan buffers only (their counter tail is zeroed), not GEGLU or statistics
-    p.fused = 0;
-    const long long nctr = (long long)((p.M + BM - 1) / BM + 1) * p.n_tiles * 4 * (bn / 32);
-    if (splitk_ws && fused_reduce_on() && !p.geglu && !p.gstats && !p.dbg && !g_gemm_generic &&
-        nctr * (long long)sizeof(int) <= (long long)kSplitKCntBytes) {
-      p.fused = 1;
-      p.cnt = reinterpret_cast<int*>(static_cast<char*>(splitk_ws) + kSplitKPartBytes);
-      return dispatch_variant(c, p, bn, bf16, pair);
-    }
     int r = dispatch_variant(c, p, bn, bf16, pair);
     if (r) return r;
     if (p.gstats) {

@@ -484,7 +484,6 @@ struct Plan {
         return -1;
       }
       splitk_side = dalloc(kSplitKBytes);
-      if (splitk_side) cudaMemset(static_cast<char*>(splitk_side) + kSplitKPartBytes, 0, kSplitKCntBytes);
     }
     const int j = (int)fork_ev.size() / 2;
     fork_ev.resize(fork_ev.size() + 2);
@@ -695,7 +694,6 @@ struct Plan {
     cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
     cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
     splitk = dalloc(kSplitKBytes);
-    if (splitk) cudaMemset(static_cast<char*>(splitk) + kSplitKPartBytes, 0, kSplitKCntBytes);
     tmp_cap = tmp_bytes;
     tmp_base = static_cast<char*>(dalloc(tmp_bytes));
     act_bytes += tmp_bytes;
