@@ -866,6 +866,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
             const int nv = n0 + g * 128 + h * 32;  // packed value column
             nb = (n0 + g * 128) / 2 + h * 32;
             if (nb < n_out) {
+              // bias of value column nv + lane and gate column nv + 64 + lane, broadcast by full-warp shuffles
+              // (nb is warp-uniform and no lane skips this block)
+              const float bvl = p.bias ? __ldg(p.bias + nv + lane) : 0.f;
+              const float bgl = p.bias ? __ldg(p.bias + nv + 64 + lane) : 0.f;
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 float a = __uint_as_float(r[j]), gt = __uint_as_float(rg[j]);
@@ -873,7 +877,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(const __grid_c
                   a = fmaf(ln_rs, a, -ln_rm * __ldg(p.ln_c1 + nv + j));
                   gt = fmaf(ln_rs, gt, -ln_rm * __ldg(p.ln_c1 + nv + 64 + j));
                 }
-                if (p.bias) { a += __ldg(p.bias + nv + j); gt += __ldg(p.bias + nv + 64 + j); }
+                a += __shfl_sync(0xffffffffu, bvl, j);
+                gt += __shfl_sync(0xffffffffu, bgl, j);
                 v[j] = a * gelu_erf(gt);
               }
             }
